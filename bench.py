@@ -1,0 +1,471 @@
+"""Benchmark of the B200 GDN kernels; prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline metric: GDN decode at B = 64 (H = 16, HV = 32,
+K = V = 128, state read and written in place), reported as state GB/s with
+us/step beside it; the prefill tokens/s at one 8192-token sequence (zero
+initial state) rides along in the same line under "prefill".
+
+* ``value``: whole-job state GB/s, device-timed with CUDA events around each
+  step's kernel, inputs resident in HBM, L2 flushed (a 256 MiB write) before
+  every timed step.  Multi-GPU: one process per GPU (torchrun), each rank runs
+  its own B = 64 shard of a 64*N batch (weak scaling, no data-path
+  collective); the time is the max over ranks.
+* ``e2e``: the same metric through the public ``gdn_decode.run`` with every
+  input copied from pinned host memory and both outputs copied back inside
+  the timed region.
+* ``roofline``: the decode kernel's algorithmic bytes per launch over its
+  event-timed duration, against the measured HBM copy bandwidth.
+* ``cpu_baseline``: the C oracle (oracle/gdn_oracle.c, all host cores) on the
+  same workload, rank 0 at N = 1 only.
+* ``--impl reference``: the reference's algorithm on the host cores (the C
+  oracle port; the reference's own solutions are Triton/AITER code for
+  MI300X and cannot run here), same metric and config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+D = 128
+H, HV = 16, 32
+DECODE_B = 64
+PREFILL_T = 8192
+FLUSH_BYTES = 256 << 20
+
+METRIC = "gdn_decode state GB/s at B=64 (H=16, HV=32, d=128)"
+UNIT = "GB/s"
+
+
+def decode_state_bytes(B):
+    return 2 * B * HV * D * D * 4
+
+
+def decode_alg_bytes(B):
+    """Algorithmic HBM bytes of one decode launch: state in + out (fp32),
+    q and k (bf16), v in and o out (bf16), a and b (bf16), A_log and dt_bias."""
+    return (decode_state_bytes(B) + 2 * B * H * D * 2 + 2 * B * HV * D * 2 + 2 * B * HV * 2
+            + 2 * HV * 4)
+
+
+def prefill_alg_flops(T):
+    """Chunk-form algorithmic FLOPs (C = 64, d = 128): per chunk-head
+    5 * 2C^2d + 3 * 2Cd^2 = 11,534,336, i.e. 180,224 per token-head."""
+    return T * HV * 180224
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch from a committed ncu summary (a line
+    'traffic_bytes_per_launch: N'), or None when no capture exists yet."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip()))
+    return None
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (barrier and max-over-ranks of timings only)
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local) if backend == "nccl" else None)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# clocks: nvidia-smi sampler around the measured window
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        try:  # address the GPU by UUID: indices differ under CUDA_VISIBLE_DEVICES
+            self.gpu = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            self.gpu = str(device.index or 0)
+        self.proc = None
+        self.path = os.path.join("/tmp", f"gdn_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "window": "warm-up soak + timed steps"}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+
+def timed_steps(fn, steps, flush, stream):
+    """Run `steps` steps; before each, flush L2 (outside the events).  Returns
+    per-step device milliseconds from CUDA events recorded on `stream`."""
+    evs = []
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            flush.add_(1)  # 256 MiB read-modify-write evicts L2 (126 MB)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            fn()
+            e.record(stream)
+            evs.append((s, e))
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in evs]
+
+
+def bench_ours(args, rank, world, local):
+    from rocm_flashinfer_contest_b200 import gdn_decode, gdn_prefill, inputs, partition
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peaks = load_peaks()
+    flush = torch.zeros(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+
+    # ---- decode: this rank's shard of a 64*N batch (weak scaling) ----
+    Bglob = DECODE_B * world
+    shard = partition.plan_decode(Bglob, H, HV, world)[rank]
+    Bloc = len(shard.seqs)
+    dargs = inputs.decode_inputs(Bloc, H, HV, seed=1000 + rank, device=dev)
+    out = torch.empty((Bloc, 1, HV, D), dtype=torch.bfloat16, device=dev)
+    state = dargs[3]
+
+    def dec_step():
+        gdn_decode.run_into(*dargs[:3], state, *dargs[4:], output=out, new_state=state)
+
+    for _ in range(max(3, args.warmup)):
+        dec_step()
+    torch.cuda.synchronize()
+
+    with ClockSampler(dev) as clk:
+        # soak so the clock sampler sees the GPU under this load
+        t_end = time.time() + 1.5
+        while time.time() < t_end:
+            for _ in range(50):
+                dec_step()
+            torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        dec_ms = timed_steps(dec_step, args.steps, flush, stream)
+        torch.cuda.synchronize()
+        barrier(world)
+
+        # ---- prefill: one 8192-token sequence per rank, zero initial state ----
+        pargs = inputs.prefill_inputs([PREFILL_T], H, HV, seed=2000 + rank, device=dev,
+                                      with_state=False)
+        pout = torch.empty((PREFILL_T, HV, D), dtype=torch.bfloat16, device=dev)
+        pstate = torch.empty((1, HV, D, D), dtype=torch.float32, device=dev)
+
+        def pre_step():
+            gdn_prefill.run_into(*pargs, output=pout, new_state=pstate)
+
+        for _ in range(max(3, args.warmup)):
+            pre_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        pre_ms = timed_steps(pre_step, args.steps, flush, stream)
+        barrier(world)
+    clocks = clk.summary()
+
+    dec_step_ms = max_over_ranks(statistics.mean(dec_ms), world, dev)
+    pre_step_ms = max_over_ranks(statistics.mean(pre_ms), world, dev)
+
+    # ---- e2e through the public run() with host buffers ----
+    host_in = [x.cpu().pin_memory() if isinstance(x, torch.Tensor) else x for x in dargs]
+    h2d = sum(x.numel() * x.element_size() for x in host_in if isinstance(x, torch.Tensor))
+    host_o = torch.empty((Bloc, 1, HV, D), dtype=torch.bfloat16).pin_memory()
+    host_s = torch.empty((Bloc, HV, D, D), dtype=torch.float32).pin_memory()
+    d2h = host_o.numel() * 2 + host_s.numel() * 4
+
+    def e2e_step():
+        dv = [x.to(dev, non_blocking=True) if isinstance(x, torch.Tensor) else x for x in host_in]
+        o, s = gdn_decode.run(*dv)
+        host_o.copy_(o, non_blocking=True)
+        host_s.copy_(s, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_steps = max(3, min(args.steps, 20))
+    pe2e_steps = max(3, min(args.steps, 10))
+    e2e_ms = timed_steps(e2e_step, e2e_steps, flush, stream)
+    e2e_step_ms = max_over_ranks(statistics.mean(e2e_ms), world, dev)
+
+    # prefill e2e
+    phost = [x.cpu().pin_memory() if isinstance(x, torch.Tensor) else x for x in pargs[:3]] + \
+        [None] + [x.cpu().pin_memory() for x in pargs[4:9]] + [pargs[9]]
+    p_h2d = sum(x.numel() * x.element_size() for x in phost if isinstance(x, torch.Tensor))
+    p_ho = torch.empty((PREFILL_T, HV, D), dtype=torch.bfloat16).pin_memory()
+    p_hs = torch.empty((1, HV, D, D), dtype=torch.float32).pin_memory()
+    p_d2h = p_ho.numel() * 2 + p_hs.numel() * 4
+
+    def pre_e2e_step():
+        dv = [x.to(dev, non_blocking=True) if isinstance(x, torch.Tensor) else x for x in phost]
+        o, s = gdn_prefill.run(*dv)
+        p_ho.copy_(o, non_blocking=True)
+        p_hs.copy_(s, non_blocking=True)
+
+    for _ in range(2):
+        pre_e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    pe2e_ms = timed_steps(pre_e2e_step, pe2e_steps, flush, stream)
+    pe2e_step_ms = max_over_ranks(statistics.mean(pe2e_ms), world, dev)
+
+    if rank != 0:
+        return None
+
+    state_bytes = decode_state_bytes(DECODE_B) * world
+    value = state_bytes / (dec_step_ms * 1e-3) / 1e9
+    alg = decode_alg_bytes(DECODE_B)
+    achieved = alg / (statistics.mean(dec_ms) * 1e-3) / 1e9
+    pre_flops = prefill_alg_flops(PREFILL_T)
+    pre_achieved = pre_flops / (statistics.mean(pre_ms) * 1e-3) / 1e12
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dec_step_ms, 5),
+        "us_per_step": round(dec_step_ms * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32 state / bf16 io",
+        "data": "synthetic (seeded; contest dataset not available offline)",
+        "config": {"workload": "gdn_decode B=64 per GPU, in-place state (BASELINE configs[1])",
+                   "B_per_gpu": DECODE_B, "B_total": DECODE_B * world, "H": H, "HV": HV,
+                   "head_size": D, "l2": "flushed (256 MiB write) before every timed step",
+                   "parallelism": f"sequence shards x{world}, no collective"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     "traffic": profile_traffic("gdn_decode_B64_ncu.txt"),
+                     "alg_bytes_per_launch": alg, "peak_src": peaks["src"]},
+        "e2e": {"value": round(state_bytes / (e2e_step_ms * 1e-3) / 1e9, 3), "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "gdn_decode.run, pinned host inputs -> device -> pinned host outputs"},
+        # one kernel per decode / prefill call; counted over every timed region
+        "gpu_launches": 2 * args.steps + e2e_steps + pe2e_steps,
+        "gpu_launches_by_region": {"decode": args.steps, "prefill": args.steps,
+                                   "decode_e2e": e2e_steps, "prefill_e2e": pe2e_steps},
+        "clocks": clocks,
+        "prefill": {
+            "metric": "gdn_prefill tokens/s at T=8192 (1 sequence, zero state)",
+            "value": round(PREFILL_T * world / (pre_step_ms * 1e-3), 1), "unit": "tokens/s",
+            "ms_per_step": round(pre_step_ms, 4),
+            "roofline": {"bound": "tensor", "achieved": round(pre_achieved, 3),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(pre_achieved / peaks["bf16_tflops"], 5),
+                         "traffic": profile_traffic("gdn_prefill_T8192_ncu.txt"),
+                         "alg_flops_per_launch": pre_flops, "peak_src": peaks["src"]},
+            "e2e": {"value": round(PREFILL_T * world / (pe2e_step_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h},
+        },
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+        line["prefill"]["cpu_baseline"] = cpu_prefill_baseline()
+    return line
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference algorithm on the host cores (C oracle port)
+
+def _cpu_decode_rate(seconds, steps=None, warmup=0):
+    from oracle import oracle
+    from rocm_flashinfer_contest_b200 import inputs
+    args = inputs.decode_inputs(DECODE_B, H, HV, seed=1000)
+    cores = os.cpu_count() or 1
+    for _ in range(warmup):
+        oracle.decode(*args, threads=cores)
+    times = []
+    t_stop = time.perf_counter() + seconds
+    while True:
+        t0 = time.perf_counter()
+        oracle.decode(*args, threads=cores)
+        times.append(time.perf_counter() - t0)
+        if steps is not None and len(times) >= steps:
+            break
+        if steps is None and time.perf_counter() > t_stop and len(times) >= 3:
+            break
+    return times, cores
+
+
+def cpu_baseline(seconds=10.0):
+    times, cores = _cpu_decode_rate(seconds)
+    t = statistics.median(times)
+    return {"value": round(decode_state_bytes(DECODE_B) / t / 1e9, 3), "unit": UNIT, "cores": cores,
+            "kind": "port",
+            "sample": f"full gdn_decode B=64 steps on the CPU oracle (oracle/gdn_oracle.c, "
+                      f"{cores} OpenMP threads), median of {len(times)} runs, {t * 1e3:.1f} ms each"}
+
+
+def cpu_prefill_baseline(tokens=512):
+    """Prefill tokens/s of the C oracle on the first `tokens` tokens of the
+    8192-token workload (all 32 v-heads; the cost is linear in tokens)."""
+    from oracle import oracle
+    from rocm_flashinfer_contest_b200 import inputs
+    args = inputs.prefill_inputs([tokens], H, HV, seed=2000, with_state=False)
+    cores = os.cpu_count() or 1
+    times = []
+    for _ in range(3):
+        t0 = time.perf_counter()
+        oracle.prefill(*args, threads=cores)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": round(tokens / t, 1), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"first {tokens} tokens of the T=8192 sequence, all {HV} v-heads, C oracle, "
+                      f"median of 3"}
+
+
+def bench_reference(args, rank, world):
+    if rank != 0:
+        return None
+    times, cores = _cpu_decode_rate(0.0, steps=args.steps, warmup=args.warmup)
+    t = statistics.mean(times)
+    value = decode_state_bytes(DECODE_B) / t / 1e9
+    return {
+        "impl": "reference",
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 state / bf16 io",
+        "data": "synthetic (seeded; contest dataset not available offline)",
+        "config": {"workload": "gdn_decode B=64, in-place state (BASELINE configs[1])",
+                   "B_per_gpu": DECODE_B, "H": H, "HV": HV, "head_size": D},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{len(times)} full gdn_decode B=64 steps, C oracle port of the "
+                                   f"contest reference, {cores} OpenMP threads"},
+        "note": "the reference's own GDN solutions are Triton/AITER kernels for MI300X (ROCm); "
+                "its algorithm is timed on the host cores through the C oracle port",
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        # the reference arm is host-only: rank 0 runs it, other ranks exit at once
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        line = bench_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    rank, world, local = dist_setup()
+    if world != args.gpus and world > 1:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    try:
+        line = bench_ours(args, rank, world, local)
+        if rank == 0 and line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

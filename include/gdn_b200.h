@@ -1,0 +1,84 @@
+/*
+ * gdn_b200.h — C ABI of the B200 (sm_100a) gated-delta-rule (GDN) kernels.
+ *
+ * These entry points are the drop-in boundary under the contest solutions'
+ * Python `run(...)` functions.  They take plain device pointers, sizes and a
+ * CUDA stream (passed as void*), allocate nothing, never synchronise the
+ * host, and return a status code (GDN_OK == 0); argument errors are reported
+ * before anything is launched.
+ *
+ * Layouts (all contiguous, k-last state as in the contest definitions
+ * gdn_decode_*_k_last / gdn_prefill_*_k_last):
+ *   decode : q,k [B,1,H,K] bf16; v [B,1,HV,V] bf16; a,b [B,1,HV] bf16;
+ *            A_log,dt_bias [HV] fp32; state/new_state [B,HV,V,K] fp32;
+ *            out [B,1,HV,V] bf16
+ *   prefill: q,k [T,H,K] bf16; v [T,HV,V] bf16; a,b [T,HV] bf16;
+ *            cu_seqlens [N+1] int32 or int64; state/new_state [N,HV,V,K] fp32;
+ *            out [T,HV,V] bf16
+ * Supported sizes: K == V == 128, H >= 1, HV % H == 0 (v-head h reads q/k head
+ * h / (HV/H)).  `state` may be NULL (zero initial state).  `scale` == 0 means
+ * 1/sqrt(K).  Pointers to bf16 data must be 8-byte aligned, state pointers
+ * 16-byte aligned.
+ */
+#ifndef GDN_B200_H_
+#define GDN_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GDN_OK 0
+#define GDN_ERR_INVALID 1     /* null pointer, negative size, bad flag        */
+#define GDN_ERR_UNSUPPORTED 2 /* K != 128, V != 128, HV % H != 0              */
+#define GDN_ERR_ALIGN 3       /* a pointer violates the alignment above       */
+#define GDN_ERR_CUDA 4        /* the launch failed (cudaGetLastError)         */
+
+/* Version of this ABI (bumped on any signature change). */
+int gdn_abi_version(void);
+
+/* Human-readable text for a status code. */
+const char *gdn_strerror(int status);
+
+/*
+ * One decode step (one token per sequence) for B sequences.
+ *
+ * Replaces the reference solution's kernel launch `_run_klast`
+ * (solutions/gdn_decode/main.py:97-114) behind `run` (main.py:117-135); the
+ * maths is the contest definition gdn_decode_*_k_last
+ * (flashinfer/trace/templates/gdn.py:27-94).
+ *
+ * new_state may equal state (in-place update); any other overlap between
+ * inputs and outputs is not allowed.
+ */
+int gdn_decode_fwd(const void *q, const void *k, const void *v, const float *state,
+                   const float *A_log, const void *a, const float *dt_bias, const void *b,
+                   float scale, int B, int H, int HV, int K, int V, void *out,
+                   float *new_state, void *stream);
+
+/*
+ * Variable-length prefill over N sequences packed into T tokens.
+ *
+ * Replaces the body of the reference solution's `run`
+ * (solutions/gdn_prefill/main.py:31-84: host gates, state transposes and the
+ * AITER chunk / recurrent kernels); the maths is the contest definition
+ * gdn_prefill_*_k_last (flashinfer/trace/templates/gdn.py:189-273).
+ *
+ * cu_seqlens is read on the device only.  A zero-length sequence gets an
+ * all-zero new_state (gdn.py:234-235); tokens outside [cu_seqlens[0],
+ * cu_seqlens[N]) get a zero output.  Entries are clamped to [0, T] so a
+ * malformed cu_seqlens cannot make the kernel read or write out of bounds.
+ * new_state may equal state (in-place update).
+ */
+int gdn_prefill_fwd(const void *q, const void *k, const void *v, const float *state,
+                    const float *A_log, const void *a, const float *dt_bias, const void *b,
+                    const void *cu_seqlens, int cu_seqlens_is_int64, int N, int T,
+                    float scale, int H, int HV, int K, int V, void *out, float *new_state,
+                    void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H_ */

@@ -1,0 +1,169 @@
+/*
+ * CPU oracle for the gated-delta-rule (GDN) decode and prefill paths.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker the CUDA kernels are
+ * compared against, and the CPU baseline that bench.py times beside them.  No
+ * product code path may call it.
+ *
+ * It restates, in plain C with fp32 arithmetic, the contest's pure-torch
+ * reference that the reference repository is scored against
+ * (jhinpan/rocm-flashinfer-contest: tools/local_verify.py:94,108 builds and runs
+ * it; the definitions live in the third-party package flashinfer-python
+ * 0.6.11.post2, flashinfer/trace/templates/gdn.py).  Per step and per v-head:
+ *
+ *   x     = a + dt_bias                              gdn.py:51 / :214
+ *   g     = exp(-exp(A_log) * softplus(x))           gdn.py:52 / :215
+ *           softplus(x) = x if x > 20 else log1p(exp(x))   (torch default,
+ *           threshold 20; also solutions/gdn_decode/main.py:82-84)
+ *   beta  = sigmoid(b)                               gdn.py:53 / :216
+ *   GVA   : v-head h reads q/k head h / (HV / H)     gdn.py:66-67 / :218-219
+ *   with S the state as [K][V] (stored k-last, [V][K]):
+ *     old    = g * S                                 gdn.py:83 / :256
+ *     old_v  = k^T old          (per v)              gdn.py:84 / :258
+ *     new_v  = beta*v + (1-beta)*old_v               gdn.py:85 / :259
+ *     S      = old - k (x) old_v + k (x) new_v       gdn.py:86-88 / :260-266
+ *     o      = scale * q^T S    -> bf16               gdn.py:90,93 / :268-269
+ *   prefill: sequences delimited by cu_seqlens; a zero-length sequence keeps
+ *   an all-zero final state even when an initial state is given (gdn.py:234-235);
+ *   the output is rounded to bf16 per token (gdn.py:269).
+ *
+ * Parity of this restatement is pinned by tests/golden/ (fixtures generated
+ * from the flashinfer reference by tests/golden/make_golden.py).
+ *
+ * Layouts are the contest's, all contiguous:
+ *   decode : q,k [B,H,K]; v [B,HV,V]; state/new_state [B,HV,V,K]; a,b [B,HV];
+ *            out [B,HV,V]
+ *   prefill: q,k [T,H,K]; v [T,HV,V]; a,b [T,HV]; cu_seqlens [N+1] (int64);
+ *            state/new_state [N,HV,V,K]; out [T,HV,V]
+ * bf16 inputs are passed widened to fp32 (exact); the output is returned as
+ * bf16 bit patterns (round to nearest even, as torch's .to(bfloat16)).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+static uint16_t f32_to_bf16_rne(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu)) {
+        return (uint16_t)((u >> 16) | 0x0040u); /* quiet NaN */
+    }
+    uint32_t lsb = (u >> 16) & 1u;
+    u += 0x7fffu + lsb;
+    return (uint16_t)(u >> 16);
+}
+
+static float softplus_t20(float x) {
+    /* torch.nn.functional.softplus(x, beta=1, threshold=20) */
+    return x > 20.0f ? x : log1pf(expf(x));
+}
+
+static void gates(float A_log, float a, float dt_bias, float b, float *g, float *beta) {
+    float x = a + dt_bias;
+    *g = expf(-expf(A_log) * softplus_t20(x));
+    *beta = 1.0f / (1.0f + expf(-b));
+}
+
+/* One token of the recurrence for one v-head, updating the k-last [V][K] state
+ * S in place.  Writes scale * q^T S_new (fp32, V values) into o. */
+static void step_head(float *S, const float *q, const float *k, const float *v,
+                      float g, float beta, float scale, int K, int V, float *o) {
+    for (int vi = 0; vi < V; ++vi) {
+        float *row = S + (size_t)vi * K;
+        float old_v = 0.0f;
+        for (int ki = 0; ki < K; ++ki) {
+            row[ki] *= g; /* old = g * S */
+            old_v += k[ki] * row[ki];
+        }
+        float new_v = beta * v[vi] + (1.0f - beta) * old_v;
+        float acc = 0.0f;
+        for (int ki = 0; ki < K; ++ki) {
+            row[ki] = row[ki] - k[ki] * old_v + k[ki] * new_v;
+            acc += q[ki] * row[ki];
+        }
+        o[vi] = scale * acc;
+    }
+}
+
+static int resolve_threads(int nthreads) {
+#ifdef _OPENMP
+    if (nthreads <= 0) nthreads = omp_get_max_threads();
+    return nthreads;
+#else
+    (void)nthreads;
+    return 1;
+#endif
+}
+
+int gdn_oracle_decode(const float *q, const float *k, const float *v, const float *state,
+                      const float *A_log, const float *a, const float *dt_bias,
+                      const float *b, float scale, int B, int H, int HV, int K, int V,
+                      uint16_t *out_bf16, float *out_f32, float *new_state, int nthreads) {
+    if (B < 0 || H <= 0 || HV <= 0 || K <= 0 || V <= 0 || HV % H) return 1;
+    if (scale == 0.0f) scale = 1.0f / sqrtf((float)K);
+    const int rep = HV / H;
+    const long long heads = (long long)B * HV;
+    nthreads = resolve_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nthreads)
+    for (long long bh = 0; bh < heads; ++bh) {
+        int bi = (int)(bh / HV), h = (int)(bh % HV), hq = h / rep;
+        float *S = new_state + (size_t)bh * V * K;
+        if (state) memcpy(S, state + (size_t)bh * V * K, sizeof(float) * (size_t)V * K);
+        else memset(S, 0, sizeof(float) * (size_t)V * K);
+        float g, beta;
+        gates(A_log[h], a[bh], dt_bias[h], b[bh], &g, &beta);
+        float *o = (float *)malloc(sizeof(float) * V);
+        step_head(S, q + ((size_t)bi * H + hq) * K, k + ((size_t)bi * H + hq) * K,
+                  v + (size_t)bh * V, g, beta, scale, K, V, o);
+        for (int vi = 0; vi < V; ++vi) {
+            out_bf16[(size_t)bh * V + vi] = f32_to_bf16_rne(o[vi]);
+            if (out_f32) out_f32[(size_t)bh * V + vi] = o[vi];
+        }
+        free(o);
+    }
+    return 0;
+}
+
+int gdn_oracle_prefill(const float *q, const float *k, const float *v, const float *state,
+                       const float *A_log, const float *a, const float *dt_bias,
+                       const float *b, const int64_t *cu_seqlens, int N, int T, float scale,
+                       int H, int HV, int K, int V, uint16_t *out_bf16, float *new_state,
+                       int nthreads) {
+    if (N < 0 || T < 0 || H <= 0 || HV <= 0 || K <= 0 || V <= 0 || HV % H) return 1;
+    if (N > 0 && (cu_seqlens[0] < 0 || cu_seqlens[N] > T)) return 1;
+    for (int n = 0; n < N; ++n)
+        if (cu_seqlens[n + 1] < cu_seqlens[n]) return 1;
+    if (scale == 0.0f) scale = 1.0f / sqrtf((float)K);
+    const int rep = HV / H;
+    /* tokens outside every sequence keep a zero output, as the reference's
+     * torch.zeros output buffer does (gdn.py:221-223) */
+    memset(out_bf16, 0, sizeof(uint16_t) * (size_t)T * HV * V);
+    nthreads = resolve_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nthreads)
+    for (long long nh = 0; nh < (long long)N * HV; ++nh) {
+        int n = (int)(nh / HV), h = (int)(nh % HV), hq = h / rep;
+        float *S = new_state + (size_t)nh * V * K;
+        int64_t t0 = cu_seqlens[n], t1 = cu_seqlens[n + 1];
+        if (t1 - t0 <= 0) { /* gdn.py:234-235: state stays zero */
+            memset(S, 0, sizeof(float) * (size_t)V * K);
+            continue;
+        }
+        if (state) memcpy(S, state + (size_t)nh * V * K, sizeof(float) * (size_t)V * K);
+        else memset(S, 0, sizeof(float) * (size_t)V * K);
+        float *o = (float *)malloc(sizeof(float) * V);
+        for (int64_t t = t0; t < t1; ++t) {
+            float g, beta;
+            gates(A_log[h], a[(size_t)t * HV + h], dt_bias[h], b[(size_t)t * HV + h], &g, &beta);
+            step_head(S, q + ((size_t)t * H + hq) * K, k + ((size_t)t * H + hq) * K,
+                      v + ((size_t)t * HV + h) * V, g, beta, scale, K, V, o);
+            for (int vi = 0; vi < V; ++vi)
+                out_bf16[((size_t)t * HV + h) * V + vi] = f32_to_bf16_rne(o[vi]);
+        }
+        free(o);
+    }
+    return 0;
+}

@@ -1,0 +1,47 @@
+"""Argument handling shared by the decode and prefill ``run`` shims."""
+from __future__ import annotations
+
+import math
+
+import torch
+
+
+def normalize_scale(scale, K: int) -> float:
+    """The reference's scale rule (solutions/gdn_decode/main.py:118-123,
+    solutions/gdn_prefill/main.py:32-37): a tensor is read with ``.item()``,
+    ``None`` or 0 means 1/sqrt(K)."""
+    if isinstance(scale, torch.Tensor):
+        scale = float(scale.item())
+    elif scale is None:
+        scale = 0.0
+    else:
+        scale = float(scale)
+    if scale == 0.0:
+        scale = 1.0 / math.sqrt(K)
+    return scale
+
+
+def require(t: torch.Tensor, name: str, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor, got {type(t).__name__}")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    return t.contiguous()
+
+
+def cuda_device_of(q: torch.Tensor) -> torch.device:
+    if not isinstance(q, torch.Tensor) or q.device.type != "cuda":
+        raise RuntimeError(
+            "the GDN kernels run on CUDA devices only (sm_100a); got "
+            f"{getattr(q, 'device', type(q).__name__)} — there is no CPU path")
+    return q.device
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t) -> int:
+    return 0 if t is None else t.data_ptr()

@@ -1,0 +1,15 @@
+// gdn_abi.cu — version and status-text entry points of the C ABI.
+#include "../../include/gdn_b200.h"
+
+extern "C" int gdn_abi_version(void) { return 1; }
+
+extern "C" const char* gdn_strerror(int status) {
+    switch (status) {
+        case GDN_OK: return "ok";
+        case GDN_ERR_INVALID: return "invalid argument (null pointer, negative size or bad flag)";
+        case GDN_ERR_UNSUPPORTED: return "unsupported shape (needs K == V == 128 and HV % H == 0)";
+        case GDN_ERR_ALIGN: return "misaligned pointer (bf16 data 8-byte, state 16-byte aligned)";
+        case GDN_ERR_CUDA: return "CUDA launch failed";
+        default: return "unknown status";
+    }
+}

@@ -1,0 +1,57 @@
+// Shared device helpers and host-side argument checks for the GDN kernels.
+//
+// The gate arithmetic follows the contest definition of gdn_decode/gdn_prefill
+// (flashinfer-python 0.6.11.post2, flashinfer/trace/templates/gdn.py:51-53 and
+// :214-216; the reference solution's kernel uses the same softplus threshold
+// of 20, solutions/gdn_decode/main.py:81-86):
+//   g    = exp(-exp(A_log) * softplus(a + dt_bias))
+//   beta = sigmoid(b)
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/gdn_b200.h"
+
+namespace gdn {
+
+constexpr int kDim = 128;  // head_size: K == V == 128 in every contest definition
+
+// log(g) = -exp(A_log) * softplus(a + dt_bias), softplus with threshold 20.
+__device__ __forceinline__ float log_gate(float A_log, float a, float dt_bias) {
+    float x = a + dt_bias;
+    float sp = x > 20.0f ? x : log1pf(expf(x));
+    return -expf(A_log) * sp;
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__device__ __forceinline__ float bf16_to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+// Four consecutive bf16 (8 bytes) widened to fp32.
+__device__ __forceinline__ float4 load_bf16x4(const __nv_bfloat16* p) {
+    uint2 raw = *reinterpret_cast<const uint2*>(p);
+    __nv_bfloat162 lo = *reinterpret_cast<__nv_bfloat162*>(&raw.x);
+    __nv_bfloat162 hi = *reinterpret_cast<__nv_bfloat162*>(&raw.y);
+    float2 a = __bfloat1622float2(lo), b = __bfloat1622float2(hi);
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+
+__device__ __forceinline__ float warp_xor_sum(float x, int width_mask_bits) {
+    // butterfly over the low `width_mask_bits` lane bits
+    for (int m = 1; m < (1 << width_mask_bits); m <<= 1) x += __shfl_xor_sync(0xffffffffu, x, m);
+    return x;
+}
+
+}  // namespace gdn
+
+// Host-side helpers shared by the C-ABI entry points.
+static inline bool gdn_aligned(const void* p, uintptr_t a) {
+    return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+static inline int gdn_launch_status() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+}

@@ -1,0 +1,58 @@
+// gdn_prefill.cu — C-ABI entry point of the varlen GDN prefill.
+//
+// Replaces the body of the reference solution's `run`
+// (solutions/gdn_prefill/main.py:31-84).  The reference computes the gates
+// with separate torch kernels, transposes the state to [N,HV,K,V] and back,
+// expands q/k to HV heads and then runs AITER's chunk or recurrent kernel;
+// here the gates are computed inside the kernel, the state is read and
+// written in the contest's k-last layout directly and q/k are indexed per
+// v-head (h / (HV/H)) without expansion.
+#include "gdn_prefill_common.cuh"
+
+extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state,
+                               const float* A_log, const void* a, const float* dt_bias,
+                               const void* b, const void* cu_seqlens, int cu_seqlens_is_int64,
+                               int N, int T, float scale, int H, int HV, int K, int V, void* out,
+                               float* new_state, void* stream) {
+    if (N < 0 || T < 0 || H <= 0 || HV <= 0) return GDN_ERR_INVALID;
+    if (cu_seqlens_is_int64 != 0 && cu_seqlens_is_int64 != 1) return GDN_ERR_INVALID;
+    if (K != gdn::kDim || V != gdn::kDim || HV % H != 0) return GDN_ERR_UNSUPPORTED;
+    if (N == 0 && T == 0) return GDN_OK;
+    if (!cu_seqlens || !A_log || !dt_bias || !out) return GDN_ERR_INVALID;
+    if (N > 0 && !new_state) return GDN_ERR_INVALID;
+    if (T > 0 && (!q || !k || !v || !a || !b)) return GDN_ERR_INVALID;
+    if (!gdn_aligned(q, 8) || !gdn_aligned(k, 8) || (new_state && !gdn_aligned(new_state, 16)) ||
+        (state && !gdn_aligned(state, 16)) || !gdn_aligned(v, 2) || !gdn_aligned(out, 2) ||
+        !gdn_aligned(a, 2) || !gdn_aligned(b, 2) || !gdn_aligned(A_log, 4) ||
+        !gdn_aligned(dt_bias, 4) || !gdn_aligned(cu_seqlens, cu_seqlens_is_int64 ? 8 : 4))
+        return GDN_ERR_ALIGN;
+    if (scale == 0.0f) scale = 1.0f / sqrtf((float)K);
+
+    gdn::PrefillParams p;
+    p.q = static_cast<const __nv_bfloat16*>(q);
+    p.k = static_cast<const __nv_bfloat16*>(k);
+    p.v = static_cast<const __nv_bfloat16*>(v);
+    p.state = state;
+    p.A_log = A_log;
+    p.a = static_cast<const __nv_bfloat16*>(a);
+    p.dt_bias = dt_bias;
+    p.b = static_cast<const __nv_bfloat16*>(b);
+    p.cu_seqlens = cu_seqlens;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.new_state = new_state;
+    p.scale = scale;
+    p.cu_is_int64 = cu_seqlens_is_int64;
+    p.N = N;
+    p.T = T;
+    p.H = H;
+    p.HV = HV;
+    p.rep = HV / H;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (N == 0) {
+        // no sequence: every token is uncovered, its output is zero
+        cudaError_t e = cudaMemsetAsync(out, 0, (size_t)T * HV * V * 2, st);
+        return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
+    }
+    gdn::launch_prefill_recurrent(p, st);
+    return gdn_launch_status();
+}

@@ -1,0 +1,55 @@
+// Parameters and sequence bookkeeping shared by the prefill kernels.
+#pragma once
+
+#include "gdn_common.cuh"
+
+namespace gdn {
+
+struct PrefillParams {
+    const __nv_bfloat16* q;  // [T, H, K]
+    const __nv_bfloat16* k;  // [T, H, K]
+    const __nv_bfloat16* v;  // [T, HV, V]
+    const float* state;      // [N, HV, V, K] or null
+    const float* A_log;      // [HV]
+    const __nv_bfloat16* a;  // [T, HV]
+    const float* dt_bias;    // [HV]
+    const __nv_bfloat16* b;  // [T, HV]
+    const void* cu_seqlens;  // [N + 1], int32 or int64
+    __nv_bfloat16* out;      // [T, HV, V]
+    float* new_state;        // [N, HV, V, K]
+    float scale;
+    int cu_is_int64;
+    int N, T, H, HV, rep;    // rep = HV / H
+};
+
+__device__ __forceinline__ long long load_cu(const PrefillParams& p, int i) {
+    return p.cu_is_int64 ? static_cast<const long long*>(p.cu_seqlens)[i]
+                         : (long long)static_cast<const int*>(p.cu_seqlens)[i];
+}
+
+// Token range [t0, t1) of sequence n, clamped into [0, T] and made monotone so
+// a malformed cu_seqlens cannot send any access out of bounds.
+__device__ __forceinline__ void seq_bounds(const PrefillParams& p, int n, long long& t0, long long& t1) {
+    long long a = load_cu(p, n), b = load_cu(p, n + 1);
+    a = a < 0 ? 0 : (a > p.T ? p.T : a);
+    b = b < a ? a : (b > p.T ? p.T : b);
+    t0 = a;
+    t1 = b;
+}
+
+// Tokens before cu_seqlens[0] or from cu_seqlens[N] on belong to no sequence;
+// the reference leaves their output at zero (gdn.py:221-223).  The CTAs of the
+// first / last sequence write those zeros for their own (head, row).
+__device__ __forceinline__ void zero_uncovered_outputs(const PrefillParams& p, int n, long long t0,
+                                                       long long t1, int hv, int row, bool writer) {
+    if (!writer) return;
+    const __nv_bfloat16 z = __float2bfloat16_rn(0.0f);
+    if (n == 0)
+        for (long long t = 0; t < t0; ++t) p.out[((size_t)t * p.HV + hv) * kDim + row] = z;
+    if (n == p.N - 1)
+        for (long long t = t1; t < p.T; ++t) p.out[((size_t)t * p.HV + hv) * kDim + row] = z;
+}
+
+void launch_prefill_recurrent(const PrefillParams& p, cudaStream_t st);
+
+}  // namespace gdn

@@ -1,0 +1,82 @@
+"""``run`` for the contest definition ``gdn_decode_*_k_last`` on B200.
+
+Same signature, argument order, dtypes and return tuple as the reference
+solution (solutions/gdn_decode/main.py:117-135) and the contest definition
+(flashinfer/trace/templates/gdn.py:97-184):
+
+    run(q, k, v, state, A_log, a, dt_bias, b, scale) -> (output, new_state)
+
+    q, k     [B, 1, H, 128]   bf16        v        [B, 1, HV, 128] bf16
+    state    [B, HV, 128, 128] fp32 (k-last [B, HV, V, K]) or None
+    A_log    [HV] fp32        a, b [B, 1, HV] bf16      dt_bias [HV] fp32
+    scale    float or 0-d tensor; 0 / None -> 1/sqrt(128)
+    output   [B, 1, HV, 128]  bf16        new_state [B, HV, 128, 128] fp32
+
+Inputs are never modified: ``new_state`` is a fresh tensor, as in the
+reference (main.py:104).  ``run_into`` is the destination-passing form; it
+accepts ``new_state is state`` for an in-place update with identical traffic.
+One kernel launch on the current stream of the inputs' device; no host sync
+unless ``scale`` is a device tensor (the reference reads it with ``.item()``).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _common as C
+from ._lib import check, lib
+
+
+def _validate(q, k, v, state, A_log, a, dt_bias, b):
+    dev = C.cuda_device_of(q)
+    bf, f32 = torch.bfloat16, torch.float32
+    q = C.require(q, "q", bf, dev)
+    k = C.require(k, "k", bf, dev)
+    v = C.require(v, "v", bf, dev)
+    a = C.require(a, "a", bf, dev)
+    b = C.require(b, "b", bf, dev)
+    A_log = C.require(A_log, "A_log", f32, dev)
+    dt_bias = C.require(dt_bias, "dt_bias", f32, dev)
+    if q.dim() != 4 or q.shape[1] != 1:
+        raise ValueError(f"q must be [B, 1, H, K], got {tuple(q.shape)}")
+    B, _, H, K = q.shape
+    if tuple(k.shape) != (B, 1, H, K):
+        raise ValueError(f"k must be {(B, 1, H, K)}, got {tuple(k.shape)}")
+    if v.dim() != 4 or v.shape[0] != B or v.shape[1] != 1:
+        raise ValueError(f"v must be [B, 1, HV, V], got {tuple(v.shape)}")
+    HV, V = v.shape[2], v.shape[3]
+    for name, t, shp in (("a", a, (B, 1, HV)), ("b", b, (B, 1, HV)),
+                         ("A_log", A_log, (HV,)), ("dt_bias", dt_bias, (HV,))):
+        if tuple(t.shape) != shp:
+            raise ValueError(f"{name} must be {shp}, got {tuple(t.shape)}")
+    if state is not None:
+        state = C.require(state, "state", f32, dev)
+        if tuple(state.shape) != (B, HV, V, K):
+            raise ValueError(f"state must be {(B, HV, V, K)}, got {tuple(state.shape)}")
+    return dev, (q, k, v, state, A_log, a, dt_bias, b), (B, H, HV, K, V)
+
+
+def run_into(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
+    """Destination-passing decode: writes ``output`` [B,1,HV,V] bf16 and
+    ``new_state`` [B,HV,V,K] fp32 (``new_state`` may be ``state``)."""
+    dev, (q, k, v, state, A_log, a, dt_bias, b), (B, H, HV, K, V) = _validate(
+        q, k, v, state, A_log, a, dt_bias, b)
+    if output.dtype != torch.bfloat16 or tuple(output.shape) != (B, 1, HV, V) \
+            or not output.is_contiguous() or output.device != dev:
+        raise ValueError("output must be a contiguous bf16 [B, 1, HV, V] tensor on the inputs' device")
+    if new_state.dtype != torch.float32 or tuple(new_state.shape) != (B, HV, V, K) \
+            or not new_state.is_contiguous() or new_state.device != dev:
+        raise ValueError("new_state must be a contiguous fp32 [B, HV, V, K] tensor on the inputs' device")
+    scale = C.normalize_scale(scale, K)
+    st = lib().gdn_decode_fwd(
+        C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(state), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias),
+        C.ptr(b), scale, B, H, HV, K, V, C.ptr(output), C.ptr(new_state), C.stream_handle(dev))
+    check("gdn_decode_fwd", st)
+    return output, new_state
+
+
+def run(q, k, v, state, A_log, a, dt_bias, b, scale):
+    """Contest entry point; see the module docstring."""
+    dev, _, (B, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b)
+    output = torch.empty((B, 1, HV, V), dtype=torch.bfloat16, device=dev)
+    new_state = torch.empty((B, HV, V, K), dtype=torch.float32, device=dev)
+    return run_into(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)

@@ -1,0 +1,90 @@
+"""``run`` for the contest definition ``gdn_prefill_*_k_last`` on B200.
+
+Same signature, argument order, dtypes and return tuple as the reference
+solution (solutions/gdn_prefill/main.py:31-84) and the contest definition
+(flashinfer/trace/templates/gdn.py:276-373):
+
+    run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)
+        -> (output, new_state)
+
+    q, k     [T, H, 128] bf16          v     [T, HV, 128] bf16
+    state    [N, HV, 128, 128] fp32 (k-last) or None
+    A_log    [HV] fp32    a, b [T, HV] bf16    dt_bias [HV] fp32
+    cu_seqlens [N + 1] int32 or int64 (read on the device only)
+    output   [T, HV, 128] bf16         new_state [N, HV, 128, 128] fp32
+
+A zero-length sequence gets an all-zero final state (gdn.py:234-235).
+Inputs are never modified; ``run_into`` is the destination-passing form and
+accepts ``new_state is state``.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _common as C
+from ._lib import check, lib
+
+
+def _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens):
+    dev = C.cuda_device_of(q)
+    bf, f32 = torch.bfloat16, torch.float32
+    q = C.require(q, "q", bf, dev)
+    k = C.require(k, "k", bf, dev)
+    v = C.require(v, "v", bf, dev)
+    a = C.require(a, "a", bf, dev)
+    b = C.require(b, "b", bf, dev)
+    A_log = C.require(A_log, "A_log", f32, dev)
+    dt_bias = C.require(dt_bias, "dt_bias", f32, dev)
+    if not isinstance(cu_seqlens, torch.Tensor) or cu_seqlens.dtype not in (torch.int32, torch.int64):
+        raise TypeError("cu_seqlens must be an int32 or int64 tensor")
+    if cu_seqlens.device != dev:
+        raise ValueError(f"cu_seqlens is on {cu_seqlens.device}, expected {dev}")
+    cu_seqlens = cu_seqlens.contiguous()
+    if q.dim() != 3:
+        raise ValueError(f"q must be [T, H, K], got {tuple(q.shape)}")
+    T, H, K = q.shape
+    if tuple(k.shape) != (T, H, K):
+        raise ValueError(f"k must be {(T, H, K)}, got {tuple(k.shape)}")
+    if v.dim() != 3 or v.shape[0] != T:
+        raise ValueError(f"v must be [T, HV, V], got {tuple(v.shape)}")
+    HV, V = v.shape[1], v.shape[2]
+    if cu_seqlens.dim() != 1 or cu_seqlens.numel() < 1:
+        raise ValueError("cu_seqlens must be a 1-d tensor of N + 1 offsets")
+    N = cu_seqlens.numel() - 1
+    for name, t, shp in (("a", a, (T, HV)), ("b", b, (T, HV)),
+                         ("A_log", A_log, (HV,)), ("dt_bias", dt_bias, (HV,))):
+        if tuple(t.shape) != shp:
+            raise ValueError(f"{name} must be {shp}, got {tuple(t.shape)}")
+    if state is not None:
+        state = C.require(state, "state", f32, dev)
+        if tuple(state.shape) != (N, HV, V, K):
+            raise ValueError(f"state must be {(N, HV, V, K)}, got {tuple(state.shape)}")
+    return dev, (q, k, v, state, A_log, a, dt_bias, b, cu_seqlens), (T, N, H, HV, K, V)
+
+
+def run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state):
+    """Destination-passing prefill into ``output`` [T,HV,V] bf16 and
+    ``new_state`` [N,HV,V,K] fp32 (``new_state`` may be ``state``)."""
+    dev, args, (T, N, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
+    q, k, v, state, A_log, a, dt_bias, b, cu = args
+    if output.dtype != torch.bfloat16 or tuple(output.shape) != (T, HV, V) \
+            or not output.is_contiguous() or output.device != dev:
+        raise ValueError("output must be a contiguous bf16 [T, HV, V] tensor on the inputs' device")
+    if new_state.dtype != torch.float32 or tuple(new_state.shape) != (N, HV, V, K) \
+            or not new_state.is_contiguous() or new_state.device != dev:
+        raise ValueError("new_state must be a contiguous fp32 [N, HV, V, K] tensor on the inputs' device")
+    scale = C.normalize_scale(scale, K)
+    st = lib().gdn_prefill_fwd(
+        C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(state), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias),
+        C.ptr(b), C.ptr(cu), 1 if cu.dtype == torch.int64 else 0, N, T, scale, H, HV, K, V,
+        C.ptr(output), C.ptr(new_state), C.stream_handle(dev))
+    check("gdn_prefill_fwd", st)
+    return output, new_state
+
+
+def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
+    """Contest entry point; see the module docstring."""
+    dev, _, (T, N, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
+    output = torch.empty((T, HV, V), dtype=torch.bfloat16, device=dev)
+    new_state = torch.empty((N, HV, V, K), dtype=torch.float32, device=dev)
+    return run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)

@@ -1,0 +1,110 @@
+"""Generates the golden fixtures that pin the CPU oracle (oracle/gdn_oracle.c).
+
+The fixtures are inputs and outputs of the contest's own pure-torch reference
+for the GDN definitions, ``_gdn_decode_reference`` and
+``_gdn_prefill_reference`` (third-party package flashinfer-python
+0.6.11.post2, flashinfer/trace/templates/gdn.py:27-94 and :189-273), run on
+the CPU on small seeded inputs.  That reference is the oracle the reference
+repository is scored against (its tools/local_verify.py:94,108 builds and runs
+it through flashinfer-bench).  The reference repository's own solutions
+import AITER at module level (solutions/gdn_decode/main.py:32-35,
+solutions/gdn_prefill/main.py:21-24), which is not installed here, so they
+cannot be run.
+
+Run once where flashinfer is importable:
+    python tests/golden/make_golden.py
+It writes tests/golden/gdn_golden.npz (bf16 tensors stored as uint16 bits).
+The tests only read the .npz; they never import flashinfer.
+"""
+from __future__ import annotations
+
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+
+from rocm_flashinfer_contest_b200.inputs import decode_inputs, prefill_inputs  # noqa: E402
+
+# (name, B, H, HV, K, with_state, scale, seed, gate_override)
+DECODE_CASES = [
+    ("dec_small", 3, 2, 4, 16, True, 0.0, 1, None),
+    ("dec_nostate", 2, 1, 2, 32, False, 0.5, 2, None),
+    ("dec_k128", 1, 1, 2, 128, True, 1.0 / math.sqrt(128), 3, None),
+    ("dec_gva4_extreme", 2, 1, 4, 16, True, 0.25, 4, "extreme"),
+    ("dec_contest_b2", 2, 4, 8, 32, True, 0.0, 5, None),
+]
+# (name, seqlens, H, HV, K, with_state, scale, seed, cu dtype)
+PREFILL_CASES = [
+    ("pre_varlen_empty", [5, 0, 17, 1], 2, 4, 16, True, 0.0, 11, torch.int64),
+    ("pre_nostate", [70], 1, 2, 32, False, 0.3, 12, torch.int32),
+    ("pre_k128", [40, 90], 1, 2, 128, True, 0.0, 13, torch.int32),
+    ("pre_gva4_extreme", [9, 3], 1, 4, 16, True, 1.0, 14, torch.int64),
+]
+
+
+def _extreme_gates(args, a_idx, b_idx):
+    """Push a and b into the saturating ranges: softplus threshold (x > 20),
+    sigmoid near 0 and 1, and a decay g near 1 (very negative a)."""
+    a = args[a_idx].float()
+    b = args[b_idx].float()
+    flat_a = a.view(-1)
+    flat_b = b.view(-1)
+    pattern_a = torch.tensor([25.0, -30.0, 19.5, 0.0, -5.0, 40.0])
+    pattern_b = torch.tensor([30.0, -30.0, 8.0, -8.0, 0.0, 1.0])
+    for i in range(flat_a.numel()):
+        flat_a[i] = pattern_a[i % len(pattern_a)]
+        flat_b[i] = pattern_b[i % len(pattern_b)]
+    args[a_idx] = a.to(torch.bfloat16)
+    args[b_idx] = b.to(torch.bfloat16)
+
+
+def _np(t):
+    if t is None:
+        return None
+    if t.dtype == torch.bfloat16:
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    return t.contiguous().numpy()
+
+
+def main():
+    from flashinfer.trace.templates.gdn import _gdn_decode_reference, _gdn_prefill_reference
+
+    out = {}
+    for name, B, H, HV, K, with_state, scale, seed, gate in DECODE_CASES:
+        args = decode_inputs(B, H, HV, K, K, seed=seed, with_state=with_state)
+        args[8] = scale
+        if gate == "extreme":
+            _extreme_gates(args, 5, 7)
+        o, s = _gdn_decode_reference(*args)
+        keys = ["q", "k", "v", "state", "A_log", "a", "dt_bias", "b"]
+        for kname, t in zip(keys, args[:8]):
+            if t is not None:
+                out[f"{name}/{kname}"] = _np(t)
+        out[f"{name}/scale"] = np.float32(scale)
+        out[f"{name}/out"] = _np(o)
+        out[f"{name}/new_state"] = _np(s)
+    for name, lens, H, HV, K, with_state, scale, seed, cu_dtype in PREFILL_CASES:
+        args = prefill_inputs(lens, H, HV, K, K, seed=seed, with_state=with_state, cu_dtype=cu_dtype)
+        args[9] = scale
+        if name.endswith("extreme"):
+            _extreme_gates(args, 5, 7)
+        o, s = _gdn_prefill_reference(*args)
+        keys = ["q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens"]
+        for kname, t in zip(keys, args[:9]):
+            if t is not None:
+                out[f"{name}/{kname}"] = _np(t)
+        out[f"{name}/scale"] = np.float32(scale)
+        out[f"{name}/out"] = _np(o)
+        out[f"{name}/new_state"] = _np(s)
+    path = os.path.join(HERE, "gdn_golden.npz")
+    np.savez_compressed(path, **out)
+    print(f"wrote {path}: {len(out)} arrays, {os.path.getsize(path)} bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,102 @@
+"""The C ABI library loads without a GPU, exports every function that
+include/gdn_b200.h declares, and rejects bad arguments with status codes
+before anything is launched (no CUDA call is made on these paths)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from rocm_flashinfer_contest_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER_DIR = os.path.join(ROOT, "include")
+
+
+def _declared():
+    names = set()
+    for fn in os.listdir(HEADER_DIR):
+        if fn.endswith(".h"):
+            src = open(os.path.join(HEADER_DIR, fn)).read()
+            src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+            names |= set(re.findall(r"\b(gdn_\w+)\s*\(", src))
+    return names
+
+
+def test_header_declares_the_abi():
+    assert {"gdn_decode_fwd", "gdn_prefill_fwd", "gdn_abi_version", "gdn_strerror"} <= _declared()
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    for name in _declared():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (gdn_\w+)", out))
+    assert _declared() <= exported
+
+
+def test_python_signatures_cover_the_header():
+    assert _declared() == set(_lib.SIGNATURES)
+
+
+def test_version_and_strerror():
+    lib = _lib.lib()
+    assert lib.gdn_abi_version() >= 1
+    for code in (0, 1, 2, 3, 4):
+        assert lib.gdn_strerror(code)
+    assert b"unknown" in lib.gdn_strerror(99)
+
+
+def _decode(**over):
+    d = dict(q=16, k=16, v=16, state=16, A_log=16, a=16, dt_bias=16, b=16, scale=0.0,
+             B=1, H=1, HV=2, K=128, V=128, out=16, new_state=16, stream=None)
+    d.update(over)
+    return _lib.lib().gdn_decode_fwd(*d.values())
+
+
+def _prefill(**over):
+    d = dict(q=16, k=16, v=16, state=16, A_log=16, a=16, dt_bias=16, b=16, cu=16, cu64=1,
+             N=1, T=4, scale=0.0, H=1, HV=2, K=128, V=128, out=16, new_state=16, stream=None)
+    d.update(over)
+    return _lib.lib().gdn_prefill_fwd(*d.values())
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(K=64), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(V=96), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(H=3, HV=4), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(H=0), _lib.GDN_ERR_INVALID),
+    (dict(B=-1), _lib.GDN_ERR_INVALID),
+    (dict(q=None), _lib.GDN_ERR_INVALID),
+    (dict(new_state=None), _lib.GDN_ERR_INVALID),
+    (dict(state=24), _lib.GDN_ERR_ALIGN),
+    (dict(q=18), _lib.GDN_ERR_ALIGN),
+    (dict(B=0), _lib.GDN_OK),  # nothing to do: returns before any launch
+])
+def test_decode_rejects_bad_arguments(over, code):
+    assert _decode(**over) == code
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(K=64), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(H=5, HV=8), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(N=-1), _lib.GDN_ERR_INVALID),
+    (dict(T=-2), _lib.GDN_ERR_INVALID),
+    (dict(cu64=2), _lib.GDN_ERR_INVALID),
+    (dict(cu=None), _lib.GDN_ERR_INVALID),
+    (dict(new_state=None), _lib.GDN_ERR_INVALID),
+    (dict(cu=20, cu64=1), _lib.GDN_ERR_ALIGN),
+    (dict(new_state=40), _lib.GDN_ERR_ALIGN),
+    (dict(N=0, T=0), _lib.GDN_OK),
+])
+def test_prefill_rejects_bad_arguments(over, code):
+    assert _prefill(**over) == code
+
+
+def test_error_is_raised_as_exception():
+    with pytest.raises(_lib.GDNError) as ei:
+        _lib.check("gdn_decode_fwd", _decode(K=64))
+    assert ei.value.status == _lib.GDN_ERR_UNSUPPORTED

@@ -1,0 +1,105 @@
+"""Pins the CPU oracle (oracle/gdn_oracle.c) to the contest reference.
+
+The fixtures in tests/golden/gdn_golden.npz are inputs and outputs of the
+contest's pure-torch reference (flashinfer-python 0.6.11.post2,
+flashinfer/trace/templates/gdn.py), written by tests/golden/make_golden.py.
+The oracle computes in fp32 like the reference, in a different summation
+order, so the state agrees to ~1e-6 and the bf16 output to within one bf16
+rounding step.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from parity import bf16_from_u16
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "gdn_golden.npz")
+
+
+def _load():
+    z = np.load(GOLD)
+    cases = {}
+    for key in z.files:
+        name, field = key.split("/")
+        cases.setdefault(name, {})[field] = z[key]
+    return cases
+
+
+CASES = _load()
+BF16_FIELDS = {"q", "k", "v", "a", "b", "out"}
+
+
+def _t(case, field):
+    if field not in case:
+        return None
+    arr = case[field]
+    if field in BF16_FIELDS:
+        return bf16_from_u16(arr)
+    return torch.from_numpy(np.array(arr))
+
+
+def _check(o, s, case):
+    ref_o = _t(case, "out").float()
+    ref_s = _t(case, "new_state")
+    o = o.float()
+    # state: fp32 vs fp32 in another summation order
+    err = (s - ref_s).abs()
+    assert float(err.max()) <= 1e-5 * float(ref_s.abs().max()) + 1e-6, float(err.max())
+    # output: bf16 -- identical except where the fp32 value sits on a rounding boundary
+    d = (o - ref_o).abs()
+    assert float((d <= 1e-6 + 2 ** -7 * ref_o.abs()).float().mean()) == 1.0
+    assert float((d == 0).float().mean()) >= 0.98
+
+
+def test_golden_file_present():
+    assert len([c for c in CASES if c.startswith("dec_")]) >= 4
+    assert len([c for c in CASES if c.startswith("pre_")]) >= 4
+
+
+@pytest.mark.parametrize("name", sorted(c for c in CASES if c.startswith("dec_")))
+def test_oracle_decode_matches_reference(name):
+    c = CASES[name]
+    args = [_t(c, f) for f in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b")]
+    o, s = oracle.decode(*args, float(c["scale"]))
+    _check(o, s, c)
+
+
+@pytest.mark.parametrize("name", sorted(c for c in CASES if c.startswith("pre_")))
+def test_oracle_prefill_matches_reference(name):
+    c = CASES[name]
+    args = [_t(c, f) for f in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens")]
+    o, s = oracle.prefill(*args, float(c["scale"]))
+    _check(o, s, c)
+
+
+def test_golden_covers_edge_cases():
+    # a zero-length sequence keeps a zero state even with an initial state given
+    c = CASES["pre_varlen_empty"]
+    cu = c["cu_seqlens"]
+    empty = [i for i in range(len(cu) - 1) if cu[i + 1] == cu[i]]
+    assert empty and "state" in c
+    for i in empty:
+        assert not c["new_state"][i].any()
+    # the softplus threshold and saturated sigmoid are exercised
+    a = bf16_from_u16(CASES["dec_gva4_extreme"]["a"]).float()
+    assert float(a.max()) > 20 and float(a.min()) < -20
+
+
+def test_oracle_plants_are_caught():
+    """A wrong gate or a wrong GVA mapping in the oracle must fail the golden check."""
+    c = CASES["dec_small"]
+    args = [_t(c, f) for f in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b")]
+    bad = list(args)
+    bad[4] = args[4] + 0.5  # A_log off by 0.5
+    o, s = oracle.decode(*bad, float(c["scale"]))
+    with pytest.raises(AssertionError):
+        _check(o, s, c)
+    bad = list(args)
+    bad[0] = args[0].flip(2)  # q heads swapped
+    bad[1] = args[1].flip(2)
+    o, s = oracle.decode(*bad, float(c["scale"]))
+    with pytest.raises(AssertionError):
+        _check(o, s, c)

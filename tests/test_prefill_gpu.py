@@ -1,0 +1,108 @@
+"""Parity of the sm_100a varlen prefill (through the C ABI) with the CPU oracle.
+
+Cases: the benchmark configurations (one 8192-token sequence with a zero
+state; 16 sequences of seeded lengths in [1, 1024] with non-zero states), the
+contest shape, zero-length sequences, lengths around the 64-token chunk
+(1, 63, 64, 65, 127, 129), int32 / int64 cu_seqlens, H == HV, many short
+sequences, tokens outside every sequence, in-place update and non-mutation.
+"""
+import pytest
+import torch
+
+from oracle import oracle
+from parity import assert_output_close, assert_state_close
+from rocm_flashinfer_contest_b200 import gdn_prefill, inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(args, dev, head_subset=None):
+    dargs = inputs.to_device(args, dev)
+    o, s = gdn_prefill.run(*dargs)
+    torch.cuda.synchronize()
+    o, s = o.cpu(), s.cpu()
+    cpu = inputs.to_cpu(args)
+    if head_subset is not None:
+        # v-heads are independent: check the v-heads of q/k head `j` only
+        j = head_subset
+        q, k, v, st, A_log, a, dt_bias, b, cu, scale = cpu
+        H, HV = q.shape[1], v.shape[1]
+        rep = HV // H
+        hs = slice(j * rep, (j + 1) * rep)
+        cpu = [q[:, j:j + 1], k[:, j:j + 1], v[:, hs], None if st is None else st[:, hs],
+               A_log[hs], a[:, hs], dt_bias[hs], b[:, hs], cu, scale]
+        o, s = o[:, hs], s[:, hs]
+    ro, rs = oracle.prefill(*cpu)
+    assert_output_close(o, ro)
+    rep = assert_state_close(s, rs)
+    return rep
+
+
+@pytest.mark.parametrize("lens,H,HV,with_state,cu_dtype", [
+    ([64], 4, 8, True, torch.int32),
+    ([1], 16, 32, True, torch.int64),
+    ([63, 65, 64, 1, 127, 129], 4, 8, True, torch.int32),
+    ([5, 0, 17, 0, 1], 4, 8, True, torch.int64),   # zero-length sequences
+    ([0], 2, 4, True, torch.int32),                 # only an empty sequence
+    ([300, 20], 16, 32, False, torch.int32),        # zero initial state
+    ([100, 37], 8, 8, True, torch.int64),           # H == HV
+    ([1] * 48, 4, 8, True, torch.int32),            # many one-token sequences
+    ([6], 4, 8, True, torch.int32),
+    ([139 // 3, 139 // 3, 139 - 2 * (139 // 3)], 4, 8, True, torch.int32),
+])
+def test_prefill_matches_oracle(cuda_device, lens, H, HV, with_state, cu_dtype):
+    args = inputs.prefill_inputs(lens, H, HV, seed=sum(lens) + len(lens), with_state=with_state,
+                                 cu_dtype=cu_dtype)
+    _check(args, cuda_device)
+
+
+def test_prefill_config3_varlen_16(cuda_device):
+    """Benchmark config 3: 16 sequences, lengths U[1, 1024], total <= 8192,
+    non-zero initial states."""
+    lens = inputs.seqlens_uniform(16, 1, 1024, seed=0, max_total=8192)
+    args = inputs.prefill_inputs(lens, seed=3)
+    _check(args, cuda_device)
+
+
+@pytest.mark.parametrize("j", [0, 11])
+def test_prefill_config2_8k(cuda_device, j):
+    """Benchmark config 2: one 8192-token sequence, zero initial state (the
+    oracle checks two v-heads of q/k head j; all heads run on the GPU)."""
+    args = inputs.prefill_inputs([8192], seed=2, with_state=False)
+    _check(args, cuda_device, head_subset=j)
+
+
+def test_prefill_uncovered_tokens_are_zero(cuda_device):
+    args = inputs.prefill_inputs([10, 20], 4, 8, seed=21, device=cuda_device)
+    cu = args[8]
+    # sequences cover tokens [3, 25) of 30; the rest belong to no sequence
+    args[8] = torch.tensor([3, 13, 25], dtype=cu.dtype, device=cuda_device)
+    o = torch.full((30, 8, 128), 5.0, device=cuda_device).to(torch.bfloat16)
+    s = torch.empty((2, 8, 128, 128), device=cuda_device)
+    gdn_prefill.run_into(*args, output=o, new_state=s)
+    torch.cuda.synchronize()
+    assert bool((o[:3] == 0).all()) and bool((o[25:] == 0).all())
+    ro, rs = oracle.prefill(*inputs.to_cpu(args))
+    assert_output_close(o.cpu(), ro)
+    assert_state_close(s.cpu(), rs)
+
+
+def test_prefill_in_place_and_no_mutation(cuda_device):
+    args = inputs.prefill_inputs([70, 5, 130], 4, 8, seed=22, device=cuda_device)
+    snap = [x.clone() if isinstance(x, torch.Tensor) else x for x in args]
+    o1, s1 = gdn_prefill.run(*args)
+    torch.cuda.synchronize()
+    for x, y in zip(args, snap):
+        if isinstance(x, torch.Tensor):
+            assert torch.equal(x, y)
+    st = args[3].clone()
+    o2 = torch.empty_like(o1)
+    gdn_prefill.run_into(*args[:3], st, *args[4:], output=o2, new_state=st)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2) and torch.equal(s1, st)
+
+
+def test_prefill_no_sequences(cuda_device):
+    args = inputs.prefill_inputs([], 4, 8, device=cuda_device)
+    o, s = gdn_prefill.run(*args)
+    assert o.shape == (0, 8, 128) and s.shape == (0, 8, 128, 128)
