@@ -34,6 +34,7 @@ extern "C" {
 #define GDN_ERR_UNSUPPORTED 2 /* K != 128, V != 128, HV % H != 0              */
 #define GDN_ERR_ALIGN 3       /* a pointer violates the alignment above       */
 #define GDN_ERR_CUDA 4        /* the launch failed (cudaGetLastError)         */
+#define GDN_ERR_DEVICE 5      /* a kernel reported an error (bounded wait timed out) */
 
 /* Version of this ABI (bumped on any signature change). */
 int gdn_abi_version(void);

@@ -16,10 +16,11 @@ GDN_ERR_INVALID = 1
 GDN_ERR_UNSUPPORTED = 2
 GDN_ERR_ALIGN = 3
 GDN_ERR_CUDA = 4
+GDN_ERR_DEVICE = 5
 
 _vp, _f, _i = ctypes.c_void_p, ctypes.c_float, ctypes.c_int
 
-# (name, restype, argtypes) for every function declared in include/gdn_b200.h
+# (name, restype, argtypes) for every function declared in include/*.h
 SIGNATURES = {
     "gdn_abi_version": (_i, []),
     "gdn_strerror": (ctypes.c_char_p, [_i]),
@@ -27,6 +28,7 @@ SIGNATURES = {
                             _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "gdn_prefill_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                              _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "gdn_umma_selftest": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
 }
 
 _lib = None

@@ -18,9 +18,9 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
     if (cu_seqlens_is_int64 != 0 && cu_seqlens_is_int64 != 1) return GDN_ERR_INVALID;
     if (K != gdn::kDim || V != gdn::kDim || HV % H != 0) return GDN_ERR_UNSUPPORTED;
     if (N == 0 && T == 0) return GDN_OK;
-    if (!cu_seqlens || !A_log || !dt_bias || !out) return GDN_ERR_INVALID;
+    if (!cu_seqlens || !A_log || !dt_bias) return GDN_ERR_INVALID;
     if (N > 0 && !new_state) return GDN_ERR_INVALID;
-    if (T > 0 && (!q || !k || !v || !a || !b)) return GDN_ERR_INVALID;
+    if (T > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_INVALID;
     if (!gdn_aligned(q, 8) || !gdn_aligned(k, 8) || (new_state && !gdn_aligned(new_state, 16)) ||
         (state && !gdn_aligned(state, 16)) || !gdn_aligned(v, 2) || !gdn_aligned(out, 2) ||
         !gdn_aligned(a, 2) || !gdn_aligned(b, 2) || !gdn_aligned(A_log, 4) ||

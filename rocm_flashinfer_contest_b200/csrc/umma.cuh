@@ -1,0 +1,177 @@
+// umma.cuh — thin inline-PTX layer over the sm_100a tensor-core instructions
+// (tcgen05.*) used by the chunked prefill kernel, written against the PTX ISA
+// (tcgen05 family, sm_100a) with the descriptor bit layouts cross-checked
+// against CUTLASS's cute/arch/mma_sm100_desc.hpp.
+//
+// Conventions
+//  * One MMA computes D[M x N] (+)= A[M x K] * B[N x K]^T, fp32 accumulators
+//    in tensor memory (TMEM), A and B in shared memory, K = 16 per
+//    instruction for 16-bit operands.  Only M = 128 (cta_group::1) is used,
+//    so row m of D is TMEM lane m and column n is TMEM column base + n.
+//  * Shared-memory operands use the 128-byte swizzle, in one of two forms:
+//      K-major  ("row" = M or N index, 64 K-elements = 128 B per line; K
+//               beyond 64 in further slabs of rows x 128 B; 8-line groups
+//               1024 B apart (SBO));
+//      MN-major ("line" = one K index, 64 M/N-elements = 128 B per line; 8
+//               lines (K) per 1024-B group (SBO); further 64-element M/N
+//               blocks `kext * 128` bytes apart (LBO)).
+//    In both, 16-byte chunk c of the line at address bits [7,10) = r sits
+//    at chunk position c ^ r, so every tile base must be 1024-byte aligned.
+//  * Every wait on an mbarrier is bounded by a clock budget; on expiry the
+//    kernel sets kDevStatTimeout in the device status word of its translation
+//    unit and carries on (results are then garbage but the context stays
+//    usable and the TMEM it holds is still freed).
+#pragma once
+
+#include <stdint.h>
+
+namespace gdn {
+
+// Device status word of this translation unit: error bits set by its kernels,
+// read back by the unit's host code (gdn_device_status() for the prefill).
+static __device__ unsigned int g_device_status;
+constexpr unsigned int kDevStatTimeout = 1u;
+
+namespace umma {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- shared-memory layouts (byte offsets inside a 1024-B aligned tile) ----
+
+// K-major, 16-bit elements: element (row, k) of a tile with `rows` rows.
+__host__ __device__ constexpr uint32_t kmaj_off(uint32_t row, uint32_t k, uint32_t rows) {
+    return (k >> 6) * rows * 128u + row * 128u + ((((k & 63u) >> 3) ^ (row & 7u)) << 4) + ((k & 7u) << 1);
+}
+
+// MN-major, 16-bit elements: element (mn, k) of a tile whose K extent is `kext`.
+__host__ __device__ constexpr uint32_t mnmaj_off(uint32_t mn, uint32_t k, uint32_t kext) {
+    return (mn >> 6) * kext * 128u + (k >> 3) * 1024u + (k & 7u) * 128u +
+           ((((mn & 63u) >> 3) ^ (k & 7u)) << 4) + ((mn & 7u) << 1);
+}
+
+// Shared-memory matrix descriptor (SWIZZLE_128B, version 1, base offset 0).
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;  // descriptor version (sm_100)
+    d |= (uint64_t)2u << 61;  // layout: 128-byte swizzle
+    return d;
+}
+
+// K-major operand, K step starting at element k0 (multiple of 16).
+__device__ __forceinline__ uint64_t desc_kmaj(uint32_t tile_saddr, uint32_t rows, uint32_t k0) {
+    return desc_sw128(tile_saddr + (k0 >> 6) * rows * 128u + (k0 & 63u) * 2u, 16u, 1024u);
+}
+
+// MN-major operand, K step starting at element k0 (multiple of 8).
+__device__ __forceinline__ uint64_t desc_mnmaj(uint32_t tile_saddr, uint32_t kext, uint32_t k0) {
+    return desc_sw128(tile_saddr + (k0 >> 3) * 1024u, kext * 128u, 1024u);
+}
+
+// Instruction descriptor, kind::f16 with fp32 accumulation.
+// fmt: 0 = f16, 1 = bf16.  major: 0 = K-major, 1 = MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_fmt, int b_fmt, int a_major, int b_major) {
+    return (1u << 4)                                   // D format: f32
+         | ((uint32_t)a_fmt << 7) | ((uint32_t)b_fmt << 10)
+         | ((uint32_t)a_major << 15) | ((uint32_t)b_major << 16)
+         | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---- TMEM management (one full warp executes these) ----
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(taddr), "r"(ncols) : "memory");
+}
+
+// ---- MMA issue (a single thread) and completion ----
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        :: "r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate) : "memory");
+}
+
+// Arrive (once) on the mbarrier when every MMA issued so far by this thread completes.
+__device__ __forceinline__ void mma_commit(uint64_t* mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 :: "r"(smem_u32(mbar)) : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Generic-proxy shared-memory writes -> visible to the tensor core (async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- mbarriers ----
+
+__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(mbar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* mbar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(mbar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after ~`budget` SM clock cycles, flags the timeout
+// and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity,
+                                          long long budget = (1ll << 31)) {
+    if (mbar_try_wait(mbar, parity)) return true;
+    const long long t0 = clock64();
+    while (true) {
+        if (mbar_try_wait(mbar, parity)) return true;
+        if (clock64() - t0 > budget) {
+            atomicOr(&g_device_status, kDevStatTimeout);
+            return false;
+        }
+    }
+}
+
+// ---- TMEM -> registers (32 lanes x 32 bit, one lane per thread) ----
+
+// 16 consecutive fp32 columns starting at `taddr` for this warp's 32 lanes
+// (lane field of taddr = 32 * (warp % 4)).  The load and its wait sit in one
+// asm block, so the registers are never read before they are valid.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr) : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+}  // namespace umma
+}  // namespace gdn
