@@ -189,6 +189,7 @@ def timed_steps(fn, steps, flush, stream):
     """Run `steps` steps; before each, flush L2 (outside the events).  Returns
     per-step device milliseconds from CUDA events recorded on `stream`."""
     evs = []
+    torch.cuda.nvtx.range_push("timed")  # ncu --nvtx-include timed/ selects these launches
     with torch.cuda.stream(stream):
         for _ in range(steps):
             flush.add_(1)  # 256 MiB read-modify-write evicts L2 (126 MB)
@@ -197,6 +198,7 @@ def timed_steps(fn, steps, flush, stream):
             fn()
             e.record(stream)
             evs.append((s, e))
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     return [s.elapsed_time(e) for s, e in evs]
 

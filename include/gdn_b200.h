@@ -17,8 +17,8 @@
  *            out [T,HV,V] bf16
  * Supported sizes: K == V == 128, H >= 1, HV % H == 0 (v-head h reads q/k head
  * h / (HV/H)).  `state` may be NULL (zero initial state).  `scale` == 0 means
- * 1/sqrt(K).  Pointers to bf16 data must be 8-byte aligned, state pointers
- * 16-byte aligned.
+ * 1/sqrt(K).  Decode: pointers to q and k must be 8-byte aligned; prefill:
+ * q, k, v and out 16-byte aligned; state pointers 16-byte aligned always.
  */
 #ifndef GDN_B200_H_
 #define GDN_B200_H_
@@ -41,6 +41,11 @@ int gdn_abi_version(void);
 
 /* Human-readable text for a status code. */
 const char *gdn_strerror(int status);
+
+/* Error bits recorded by the prefill kernels since the last clear (1 = a
+ * bounded wait on the tensor cores timed out); synchronises the device.
+ * clear != 0 resets the word.  Returns -1 if it cannot be read. */
+int gdn_device_status(int clear);
 
 /*
  * One decode step (one token per sequence) for B sequences.
@@ -71,6 +76,9 @@ int gdn_decode_fwd(const void *q, const void *k, const void *v, const float *sta
  * cu_seqlens[N]) get a zero output.  Entries are clamped to [0, T] so a
  * malformed cu_seqlens cannot make the kernel read or write out of bounds.
  * new_state may equal state (in-place update).
+ *
+ * T >= GDN_PREFILL_CHUNK_MIN (environment, default 128) runs the chunked
+ * tensor-core kernel, shorter batches the token-serial kernel.
  */
 int gdn_prefill_fwd(const void *q, const void *k, const void *v, const float *state,
                     const float *A_log, const void *a, const float *dt_bias, const void *b,

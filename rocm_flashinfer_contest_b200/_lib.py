@@ -24,6 +24,7 @@ _vp, _f, _i = ctypes.c_void_p, ctypes.c_float, ctypes.c_int
 SIGNATURES = {
     "gdn_abi_version": (_i, []),
     "gdn_strerror": (ctypes.c_char_p, [_i]),
+    "gdn_device_status": (_i, [_i]),
     "gdn_decode_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f,
                             _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "gdn_prefill_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,

@@ -8,7 +8,7 @@ extern "C" const char* gdn_strerror(int status) {
         case GDN_OK: return "ok";
         case GDN_ERR_INVALID: return "invalid argument (null pointer, negative size or bad flag)";
         case GDN_ERR_UNSUPPORTED: return "unsupported shape (needs K == V == 128 and HV % H == 0)";
-        case GDN_ERR_ALIGN: return "misaligned pointer (bf16 data 8-byte, state 16-byte aligned)";
+        case GDN_ERR_ALIGN: return "misaligned pointer (see the alignment rules in gdn_b200.h)";
         case GDN_ERR_CUDA: return "CUDA launch failed";
         case GDN_ERR_DEVICE: return "a kernel reported a device-side error (bounded wait timed out)";
         default: return "unknown status";

@@ -7,7 +7,20 @@
 // here the gates are computed inside the kernel, the state is read and
 // written in the contest's k-last layout directly and q/k are indexed per
 // v-head (h / (HV/H)) without expansion.
+#include <stdlib.h>
+
 #include "gdn_prefill_common.cuh"
+
+// Total-length threshold between the token-serial kernel and the chunked
+// tensor-core kernel, as the reference's CHUNK_MIN_SEQ_LEN
+// (solutions/gdn_prefill/main.py:26-28, env GDN_PREFILL_CHUNK_MIN): the
+// chunked kernel runs when T >= threshold.  Both kernels compute the same
+// recurrence; the threshold only trades launch latency against throughput.
+static long long chunk_threshold() {
+    const char* e = getenv("GDN_PREFILL_CHUNK_MIN");
+    if (e && *e) return atoll(e);
+    return 128;
+}
 
 extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state,
                                const float* A_log, const void* a, const float* dt_bias,
@@ -21,7 +34,7 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
     if (!cu_seqlens || !A_log || !dt_bias) return GDN_ERR_INVALID;
     if (N > 0 && !new_state) return GDN_ERR_INVALID;
     if (T > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_INVALID;
-    if (!gdn_aligned(q, 8) || !gdn_aligned(k, 8) || (new_state && !gdn_aligned(new_state, 16)) ||
+    if (!gdn_aligned(q, 16) || !gdn_aligned(k, 16) || !gdn_aligned(v, 16) || !gdn_aligned(out, 16) || (new_state && !gdn_aligned(new_state, 16)) ||
         (state && !gdn_aligned(state, 16)) || !gdn_aligned(v, 2) || !gdn_aligned(out, 2) ||
         !gdn_aligned(a, 2) || !gdn_aligned(b, 2) || !gdn_aligned(A_log, 4) ||
         !gdn_aligned(dt_bias, 4) || !gdn_aligned(cu_seqlens, cu_seqlens_is_int64 ? 8 : 4))
@@ -53,6 +66,9 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
         cudaError_t e = cudaMemsetAsync(out, 0, (size_t)T * HV * V * 2, st);
         return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
     }
-    gdn::launch_prefill_recurrent(p, st);
+    if ((long long)T >= chunk_threshold())
+        gdn::launch_prefill_chunk(p, st);
+    else
+        gdn::launch_prefill_recurrent(p, st);
     return gdn_launch_status();
 }

@@ -51,5 +51,6 @@ __device__ __forceinline__ void zero_uncovered_outputs(const PrefillParams& p, i
 }
 
 void launch_prefill_recurrent(const PrefillParams& p, cudaStream_t st);
+void launch_prefill_chunk(const PrefillParams& p, cudaStream_t st);
 
 }  // namespace gdn

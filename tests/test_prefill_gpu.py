@@ -16,6 +16,14 @@ from rocm_flashinfer_contest_b200 import gdn_prefill, inputs
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=["chunk", "recurrent"])
+def path(request, monkeypatch):
+    """Runs a test through the chunked tensor-core kernel (threshold 0) or the
+    token-serial kernel (threshold above any T used here)."""
+    monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "0" if request.param == "chunk" else "1000000000")
+    return request.param
+
+
 def _check(args, dev, head_subset=None):
     dargs = inputs.to_device(args, dev)
     o, s = gdn_prefill.run(*dargs)
@@ -33,8 +41,9 @@ def _check(args, dev, head_subset=None):
                A_log[hs], a[:, hs], dt_bias[hs], b[:, hs], cu, scale]
         o, s = o[:, hs], s[:, hs]
     ro, rs = oracle.prefill(*cpu)
-    assert_output_close(o, ro)
+    rep_o = assert_output_close(o, ro)
     rep = assert_state_close(s, rs)
+    print("parity", rep_o, rep)
     return rep
 
 
@@ -50,13 +59,13 @@ def _check(args, dev, head_subset=None):
     ([6], 4, 8, True, torch.int32),
     ([139 // 3, 139 // 3, 139 - 2 * (139 // 3)], 4, 8, True, torch.int32),
 ])
-def test_prefill_matches_oracle(cuda_device, lens, H, HV, with_state, cu_dtype):
+def test_prefill_matches_oracle(cuda_device, path, lens, H, HV, with_state, cu_dtype):
     args = inputs.prefill_inputs(lens, H, HV, seed=sum(lens) + len(lens), with_state=with_state,
                                  cu_dtype=cu_dtype)
     _check(args, cuda_device)
 
 
-def test_prefill_config3_varlen_16(cuda_device):
+def test_prefill_config3_varlen_16(cuda_device, path):
     """Benchmark config 3: 16 sequences, lengths U[1, 1024], total <= 8192,
     non-zero initial states."""
     lens = inputs.seqlens_uniform(16, 1, 1024, seed=0, max_total=8192)
@@ -65,14 +74,14 @@ def test_prefill_config3_varlen_16(cuda_device):
 
 
 @pytest.mark.parametrize("j", [0, 11])
-def test_prefill_config2_8k(cuda_device, j):
+def test_prefill_config2_8k(cuda_device, path, j):
     """Benchmark config 2: one 8192-token sequence, zero initial state (the
     oracle checks two v-heads of q/k head j; all heads run on the GPU)."""
     args = inputs.prefill_inputs([8192], seed=2, with_state=False)
     _check(args, cuda_device, head_subset=j)
 
 
-def test_prefill_uncovered_tokens_are_zero(cuda_device):
+def test_prefill_uncovered_tokens_are_zero(cuda_device, path):
     args = inputs.prefill_inputs([10, 20], 4, 8, seed=21, device=cuda_device)
     cu = args[8]
     # sequences cover tokens [3, 25) of 30; the rest belong to no sequence
@@ -87,7 +96,7 @@ def test_prefill_uncovered_tokens_are_zero(cuda_device):
     assert_state_close(s.cpu(), rs)
 
 
-def test_prefill_in_place_and_no_mutation(cuda_device):
+def test_prefill_in_place_and_no_mutation(cuda_device, path):
     args = inputs.prefill_inputs([70, 5, 130], 4, 8, seed=22, device=cuda_device)
     snap = [x.clone() if isinstance(x, torch.Tensor) else x for x in args]
     o1, s1 = gdn_prefill.run(*args)
@@ -102,7 +111,27 @@ def test_prefill_in_place_and_no_mutation(cuda_device):
     assert torch.equal(o1, o2) and torch.equal(s1, st)
 
 
-def test_prefill_no_sequences(cuda_device):
+def test_prefill_no_sequences(cuda_device, path):
     args = inputs.prefill_inputs([], 4, 8, device=cuda_device)
     o, s = gdn_prefill.run(*args)
     assert o.shape == (0, 8, 128) and s.shape == (0, 8, 128, 128)
+
+
+def test_prefill_device_status_clean(cuda_device):
+    """No bounded wait in the tensor-core kernel ran out during the suite."""
+    from rocm_flashinfer_contest_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.lib().gdn_device_status(1) == 0
+
+
+def test_prefill_strong_decay_and_saturated_gates(cuda_device, path):
+    """Very strong decay (A_log = ln 16 with large a) and saturated beta: every
+    in-chunk factor e^{gamma_i - gamma_j} underflows towards 0 without overflow."""
+    args = inputs.prefill_inputs([200, 70], 4, 8, seed=31)
+    T = 270
+    pat_a = torch.tensor([25.0, -30.0, 19.5, 0.0, -5.0, 40.0, 8.0, 3.0])
+    pat_b = torch.tensor([30.0, -30.0, 8.0, -8.0, 0.0, 1.0, -1.0, 15.0])
+    args[4] = torch.full((8,), 2.77)
+    args[5] = pat_a.repeat(T).view(T, 8).to(torch.bfloat16)
+    args[7] = pat_b.repeat(T).view(T, 8).to(torch.bfloat16)
+    _check(args, cuda_device)
