@@ -3,9 +3,10 @@
  *
  * These entry points are the drop-in boundary under the contest solutions'
  * Python `run(...)` functions.  They take plain device pointers, sizes and a
- * CUDA stream (passed as void*), allocate nothing, never synchronise the
- * host, and return a status code (GDN_OK == 0); argument errors are reported
- * before anything is launched.
+ * CUDA stream (passed as void*), allocate nothing (the prefill's scratch is a
+ * caller-provided workspace), never synchronise the host, and return a
+ * status code (GDN_OK == 0); argument errors are reported before anything is
+ * launched.
  *
  * Layouts (all contiguous, k-last state as in the contest definitions
  * gdn_decode_*_k_last / gdn_prefill_*_k_last):
@@ -23,6 +24,7 @@
 #ifndef GDN_B200_H_
 #define GDN_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -78,13 +80,25 @@ int gdn_decode_fwd(const void *q, const void *k, const void *v, const float *sta
  * new_state may equal state (in-place update).
  *
  * T >= GDN_PREFILL_CHUNK_MIN (environment, default 128) runs the chunked
- * tensor-core kernel, shorter batches the token-serial kernel.
+ * tensor-core kernels, which need a device workspace of at least
+ * gdn_prefill_workspace_bytes(N, T, HV) bytes (16-byte aligned; its contents
+ * on entry do not matter); shorter batches run the token-serial kernel and
+ * need none (workspace may then be NULL).
  */
 int gdn_prefill_fwd(const void *q, const void *k, const void *v, const float *state,
                     const float *A_log, const void *a, const float *dt_bias, const void *b,
                     const void *cu_seqlens, int cu_seqlens_is_int64, int N, int T,
                     float scale, int H, int HV, int K, int V, void *out, float *new_state,
-                    void *stream);
+                    void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * Workspace bytes gdn_prefill_fwd needs for (N, T, HV): 0 when the call will
+ * take the token-serial kernel.  The chunked kernels keep one slot per
+ * (64-token chunk, v-head) — the chunk's [T ; P'] operand tile plus its gates,
+ * 16,896 bytes — for floor(T/64) + N chunks.  No counterpart in the
+ * reference, whose AITER kernels allocate their intermediates with torch.
+ */
+size_t gdn_prefill_workspace_bytes(int N, int T, int HV);
 
 #ifdef __cplusplus
 }

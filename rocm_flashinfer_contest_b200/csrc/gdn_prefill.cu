@@ -22,11 +22,19 @@ static long long chunk_threshold() {
     return 128;
 }
 
+static bool use_chunk_path(int T) { return (long long)T >= chunk_threshold(); }
+
+extern "C" size_t gdn_prefill_workspace_bytes(int N, int T, int HV) {
+    if (N <= 0 || T <= 0 || HV <= 0 || !use_chunk_path(T)) return 0;
+    return gdn::prefill_workspace_bytes(N, T, HV);
+}
+
 extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state,
                                const float* A_log, const void* a, const float* dt_bias,
                                const void* b, const void* cu_seqlens, int cu_seqlens_is_int64,
                                int N, int T, float scale, int H, int HV, int K, int V, void* out,
-                               float* new_state, void* stream) {
+                               float* new_state, void* workspace, size_t workspace_bytes,
+                               void* stream) {
     if (N < 0 || T < 0 || H <= 0 || HV <= 0) return GDN_ERR_INVALID;
     if (cu_seqlens_is_int64 != 0 && cu_seqlens_is_int64 != 1) return GDN_ERR_INVALID;
     if (K != gdn::kDim || V != gdn::kDim || HV % H != 0) return GDN_ERR_UNSUPPORTED;
@@ -66,9 +74,13 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
         cudaError_t e = cudaMemsetAsync(out, 0, (size_t)T * HV * V * 2, st);
         return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
     }
-    if ((long long)T >= chunk_threshold())
-        gdn::launch_prefill_chunk(p, st);
-    else
+    if (T > 0 && use_chunk_path(T)) {
+        const size_t need = gdn::prefill_workspace_bytes(N, T, HV);
+        if (!workspace || workspace_bytes < need) return GDN_ERR_INVALID;
+        if (!gdn_aligned(workspace, 16)) return GDN_ERR_ALIGN;
+        gdn::launch_prefill_chunk(p, workspace, st);
+    } else {
         gdn::launch_prefill_recurrent(p, st);
+    }
     return gdn_launch_status();
 }

@@ -24,63 +24,39 @@
 // the decay.  Tokens past the end of the sequence get k = q = v = beta = 0 and
 // log g = 0, which leaves every formula exact for a partial last chunk.
 //
-// One CTA (128 threads, thread t <-> TMEM lane t) owns one (sequence, v-head,
-// 64-wide V tile) and walks its chunks in order.  Per chunk:
-//   MMA_A : [K ; Q] (128 x 128) x K^T           -> TMEM cols [0, 64)
-//   masks : rows 0-63 -> A (fp32, smem), rows 64-127 -> P (f16, A operand)
-//   MMA_1 : [K ; diag(scale e^gamma) Q] x S      -> TMEM cols [64, 128)  (overlaps the solve)
-//   solve : T = (I + A)^-1 on the CUDA cores in fp32, blocked by 16:
-//           the four diagonal blocks by right-looking substitution (one warp
-//           each), then the off-diagonal blocks level by level,
-//           T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj
-//   MMA_P : [T ; P] (128 x 64) x T               -> rows 64-127 = P' = P T
-//   Y     : rows 0-63 (f16, smem);  rows 64-127 keep Q~S for the output
-//   MMA_2 : [T ; P'] (128 x 64) x Y              -> TMEM cols [128, 192)
-//   out   : rows 64-127: O = Q~S + P'Y -> bf16 -> HBM;  rows 0-63: Delta (f16, smem)
-//   MMA_3 : K~^T (128 x 64, MN-major) x Delta    -> TMEM cols [192, 256)
-//   state : S = e^{gamma_C} S + K~^T Delta (fp32, smem), f16 copy for MMA_1
-// Operands are f16 (inputs are bf16 with |q|,|k| <= 1 after L2-normalisation;
-// f16 keeps 3 more mantissa bits), accumulation is fp32 in TMEM and the state
-// carried between chunks is fp32.
+// Two kernels:
+//  * prep  (one CTA per (chunk, v-head), all chunks of all sequences at once):
+//      the state-independent part — gates, gamma, MMA [K ; Q] K^T (bf16 as
+//      given), the decay masks, T = (I + A)^-1 by a blocked solve on the CUDA
+//      cores in fp32, and P' = P T on the tensor cores — and writes the f16
+//      operand tile [T ; P'] (already in its shared-memory swizzled layout),
+//      gamma and beta into a workspace slot.
+//  * chain (one CTA per (sequence, v-head, 64-wide V tile), 8 warps): walks
+//      the chunks in order with the state resident in TMEM (fp32):
+//        MMA_1 : [K ; diag(scale e^gamma) Q] x S -> Y (rows 0-63), Q~S (rows 64-127)
+//        MMA_2 : [T ; P'] x Y                     -> Delta (rows 0-63), P'Y (rows 64-127)
+//        MMA_3 : K~^T x Delta,  S = e^{gamma_C} S + K~^T Delta
+//      while the next chunk's q / k / v rows and workspace slot stream into
+//      shared memory with cp.async.
+// Operands are f16 except in the prep MMA (bf16 inputs as given); every
+// accumulation is fp32 and the state carried between chunks is fp32.
+//
+// Workspace slot of chunk j of sequence n: floor(cu[n] / 64) + n + j, which is
+// below floor(T / 64) + N for every chunk, so the workspace holds
+// (floor(T / 64) + N) * HV slots of kSlotBytes.
 #include "gdn_prefill_common.cuh"
 #include "umma.cuh"
 
 namespace gdn {
 namespace chunk {
 
-constexpr int C = 64;    // tokens per chunk
-constexpr int VT = 64;   // state columns (v) per CTA
-constexpr int NT = 128;  // threads per CTA
+constexpr int C = 64;                    // tokens per chunk
+constexpr int LDA = 68;                  // fp32 row stride of the solve matrices
+constexpr uint32_t kTileTP = 16384;      // [T ; P'] f16, K-major 128 x 64
+constexpr uint32_t kSlotBytes = kTileTP + 2 * 256;  // + gamma[64], beta[64] (fp32)
 
-// Shared-memory map (bytes from a 1024-byte aligned base).
-constexpr int LDA = 68;                         // fp32 row stride of the solve matrices
-constexpr uint32_t OFF_KQ = 0;                  // [K ; Q] K-major 128 x 128 f16      32 KiB
-constexpr uint32_t OFF_TP = OFF_KQ + 32768;     // [T ; P'] K-major 128 x 64 f16      16 KiB
-constexpr uint32_t OFF_TB = OFF_TP + 16384;     // T as MN-major B (m x j) f16         8 KiB
-constexpr uint32_t OFF_SH = OFF_TB + 8192;      // S^T K-major VT x 128 f16 (B op)    16 KiB
-constexpr uint32_t OFF_Y = OFF_SH + 16384;      // Y MN-major (v x 64 tokens) f16      8 KiB
-constexpr uint32_t OFF_DL = OFF_Y + 8192;       // Delta MN-major (v x 64 tokens) f16  8 KiB
-constexpr uint32_t OFF_KT = OFF_DL + 8192;      // K~ MN-major (k x 64 tokens) f16    16 KiB
-constexpr uint32_t OFF_SF = OFF_KT + 16384;     // S fp32 [v][k] (VT x 128)           32 KiB
-constexpr uint32_t OFF_A = OFF_SF + 32768;      // A fp32 [64][LDA]                   17 KiB
-constexpr uint32_t OFF_T = OFF_A + 64 * LDA * 4;  // T fp32 [64][LDA]                 17 KiB
-// solve scratch: rows 16-63 of a [64][LDA] fp32 matrix (12.75 KiB), aliased onto
-// the Y / Delta tiles, which are idle while T is being solved
-constexpr uint32_t OFF_X = OFF_Y;
-constexpr uint32_t OFF_RK = OFF_T + 64 * LDA * 4;  // raw next-chunk k rows bf16 [64][128]  16 KiB
-constexpr uint32_t OFF_RQ = OFF_RK + 16384;        // raw next-chunk q rows bf16 [64][128]  16 KiB
-constexpr uint32_t OFF_RV = OFF_RQ + 16384;        // raw v rows bf16 [2][64][VT] (swizzled) 16 KiB
-constexpr uint32_t OFF_G = OFF_RV + 2 * C * VT * 2;  // gamma[64] fp32
-constexpr uint32_t OFF_BETA = OFF_G + 256;      // beta[64] fp32
-constexpr uint32_t SMEM_USED = OFF_BETA + 256;
-constexpr uint32_t SMEM_BYTES = SMEM_USED + 1024;  // + alignment slack
-static_assert(48 * LDA * 4 <= 16384, "solve scratch fits the Y / Delta tiles");
-static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
-
-constexpr uint32_t TM_A = 0, TM_1 = 64, TM_2 = 128, TM_3 = 192, TM_COLS = 256;
-
-// Clock budget of one wait for MMA completion (~70 ms at 1.9 GHz; a chunk's
-// MMAs take microseconds).  On expiry the CTA stops, frees its TMEM and
+// Clock budget of one wait for MMA completion (~70 ms at 1.9 GHz; the MMAs of
+// a chunk take microseconds).  On expiry the CTA stops, frees its TMEM and
 // leaves kDevStatTimeout in the status word.
 constexpr long long kWaitBudget = 1ll << 27;
 
@@ -91,8 +67,7 @@ __device__ __forceinline__ void st_f16x8(unsigned char* base, uint32_t off, cons
     *reinterpret_cast<uint4*>(base + off) = *reinterpret_cast<uint4*>(h);
 }
 
-__device__ __forceinline__ void ld_bf16x8(const __nv_bfloat16* p, float* x) {
-    uint4 raw = *reinterpret_cast<const uint4*>(p);
+__device__ __forceinline__ void unpack_bf16x8(const uint4& raw, float* x) {
     const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -110,48 +85,39 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// Raw-row buffers of one chunk: q and k rows [64][128] bf16, linear; v rows
-// [64][VT] bf16 with 16-byte chunk c of row r stored at c ^ (r & 7).
-__device__ __forceinline__ uint32_t rawv_off(int r, int c) { return r * (VT * 2) + ((c ^ (r & 7)) << 4); }
-
-// Issues the asynchronous copies of chunk [tc, tc + len) into the raw buffers
-// (rows past len are zero-filled).  Piece idx of q / k is copied by thread
-// idx % NT, the same thread that later converts it.
-__device__ __forceinline__ void prefetch_chunk(const PrefillParams& p, uint32_t rk, uint32_t rq, uint32_t rv,
-                                               long long tc, int len, int hq, int hv, int v0, int tid) {
-#pragma unroll
-    for (int it = 0; it < C * 16 / NT; ++it) {
-        const int idx = tid + it * NT, r = idx >> 4, c = idx & 15;
-        const bool ok = r < len;
-        const size_t row = ok ? ((size_t)(tc + r) * p.H + hq) * kDim + c * 8 : 0;
-        cp_async16(rk + idx * 16, p.k + row, ok);
-        cp_async16(rq + idx * 16, p.q + row, ok);
-    }
-#pragma unroll
-    for (int it = 0; it < C * (VT / 8) / NT; ++it) {
-        const int idx = tid + it * NT, r = idx / (VT / 8), c = idx % (VT / 8);
-        const bool ok = r < len;
-        const size_t off = ok ? ((size_t)(tc + r) * p.HV + hv) * kDim + v0 + c * 8 : 0;
-        cp_async16(rv + rawv_off(r, c), p.v + off, ok);
-    }
-    cp_async_commit();
+__device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t parity) {
+    // every thread waits; the CTA agrees on the outcome
+    const bool ok = umma::mbar_wait(bar, parity, kWaitBudget);
+    return !__syncthreads_or(!ok);
 }
 
-// Converts raw bf16 q / k rows into the f16 K-major [K ; Q] operand tile.
-__device__ __forceinline__ void convert_qk(unsigned char* sm, int tid) {
-#pragma unroll
-    for (int it = 0; it < C * 16 / NT; ++it) {
-        const int idx = tid + it * NT, r = idx >> 4, c = idx & 15;
-        float x[8];
-        ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(sm + OFF_RK + idx * 16), x);
-        st_f16x8(sm + OFF_KQ, umma::kmaj_off(r, c * 8, 128), x);
-        ld_bf16x8(reinterpret_cast<const __nv_bfloat16*>(sm + OFF_RQ + idx * 16), x);
-        st_f16x8(sm + OFF_KQ, umma::kmaj_off(64 + r, c * 8, 128), x);
-    }
+__device__ __forceinline__ void sync_for_mma() {
+    umma::fence_proxy_async_smem();
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
 }
 
-// Blocked T = (I + A)^-1 for the 64 x 64 strictly lower A in sA (fp32,
-// row stride LDA); writes T into sT (upper blocks must already be zero).
+// ============================================================================
+// prep kernel
+// ============================================================================
+namespace prep {
+
+constexpr int NT = 128;
+constexpr uint32_t OFF_KQ = 0;                     // [K ; Q] bf16 K-major 128 x 128   32 KiB
+constexpr uint32_t OFF_TP = 32768;                 // [T ; P] f16 K-major 128 x 64     16 KiB
+constexpr uint32_t OFF_TB = OFF_TP + kTileTP;      // T as MN-major B (m x j) f16        8 KiB
+constexpr uint32_t OFF_A = OFF_TB + 8192;          // A fp32 [64][LDA]                 17 KiB
+constexpr uint32_t OFF_T = OFF_A + 64 * LDA * 4;   // T fp32 [64][LDA]                 17 KiB
+constexpr uint32_t OFF_X = OFF_T + 64 * LDA * 4;   // solve scratch, rows 16-63        12.75 KiB
+constexpr uint32_t OFF_G = OFF_X + 48 * LDA * 4;   // gamma[64]
+constexpr uint32_t OFF_BETA = OFF_G + 256;         // beta[64]
+constexpr uint32_t SMEM_BYTES = OFF_BETA + 256 + 1024;  // + alignment slack (two CTAs per SM)
+constexpr uint32_t TM_COLS = 64;
+
+// Blocked T = (I + A)^-1 for the 64 x 64 strictly lower A in sA (fp32, row
+// stride LDA); writes T into sT, whose upper blocks must already be zero.
+// sX holds rows 16-63 of the level scratch X.
 __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
     // diagonal blocks: warp b inverts I + A_bb by right-looking substitution,
@@ -171,8 +137,8 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
         for (int r = 0; r < 16; ++r) sT[(b0 + r) * LDA + b0 + lane] = x[r];
     }
     __syncthreads();
-    // off-diagonal blocks, level d = i - j: X_ij = sum_k A_ik T_kj, then T_ij = -T_ii X_ij.
-    // Thread -> (rows r0, r0+1; column c) of a 16 x 16 block.
+    // off-diagonal blocks, level d = i - j: X_ij = sum_k A_ik T_kj, then
+    // T_ij = -T_ii X_ij.  Thread -> (rows r0, r0 + 1; column c) of a block.
     const int c = tid & 15, r0 = (tid >> 4) * 2;
 #pragma unroll
     for (int d = 1; d < 4; ++d) {
@@ -194,7 +160,7 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
                     acc1 += x1.x * t0 + x1.y * t1 + x1.z * t2 + x1.w * t3;
                 }
             }
-            sX[(16 * i + r0 - 16) * LDA + 16 * j + c] = acc0;  // sX holds rows 16-63
+            sX[(16 * i + r0 - 16) * LDA + 16 * j + c] = acc0;
             sX[(16 * i + r0 - 15) * LDA + 16 * j + c] = acc1;
         }
         __syncthreads();
@@ -220,50 +186,276 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
     }
 }
 
-__global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(NT, 2) gdn_prefill_chunk_prep_kernel(const PrefillParams p, unsigned char* ws) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t mbar[5];
+    __shared__ uint64_t mbar[2];
     __shared__ uint32_t tmem_base_sh;
 
     const int tid = threadIdx.x, warp = tid >> 5;
+    const long long s = blockIdx.x / p.HV;
+    const int hv = blockIdx.x % p.HV, hq = hv / p.rep;
+
+    // locate the chunk: the largest n with floor(cu[n] / 64) + n <= s, then j
+    int lo = 0, hi = p.N - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        long long a, b;
+        seq_bounds(p, mid, a, b);
+        if (a / C + mid <= s) lo = mid; else hi = mid - 1;
+    }
+    const int n = lo;
+    long long t0, t1;
+    seq_bounds(p, n, t0, t1);
+    const long long j = s - (t0 / C + n);
+    if (j < 0 || t0 + C * j >= t1) return;  // slot of no chunk
+    const long long tc = t0 + C * j;
+    const int len = (int)((t1 - tc) < C ? (t1 - tc) : C);
+
+    float* sA = reinterpret_cast<float*>(sm + OFF_A);
+    float* sT = reinterpret_cast<float*>(sm + OFF_T);
+    float* sX = reinterpret_cast<float*>(sm + OFF_X);
+    float* sG = reinterpret_cast<float*>(sm + OFF_G);
+    float* sBeta = reinterpret_cast<float*>(sm + OFF_BETA);
+
+    // raw k rows -> [K ; Q] rows 0-63, q rows -> rows 64-127 (bf16, swizzled K-major)
+    const uint32_t sKQ = umma::smem_u32(sm + OFF_KQ);
+#pragma unroll
+    for (int it = 0; it < C * 16 / NT; ++it) {
+        const int idx = tid + it * NT, r = idx >> 4, c = idx & 15;
+        const bool ok = r < len;
+        const size_t row = ok ? ((size_t)(tc + r) * p.H + hq) * kDim + c * 8 : 0;
+        cp_async16(sKQ + umma::kmaj_off(r, c * 8, 128), p.k + row, ok);
+        cp_async16(sKQ + umma::kmaj_off(64 + r, c * 8, 128), p.q + row, ok);
+    }
+    cp_async_commit();
+    for (int idx = tid; idx < 64 * 64; idx += NT) {  // T's upper blocks are zero
+        const int i = idx >> 6, jj = idx & 63;
+        if ((jj >> 4) > (i >> 4)) sT[i * LDA + jj] = 0.f;
+    }
+    // gates and the inclusive scan of log g (warps 0 and 1)
+    float lg = 0.f, beta = 0.f;
+    if (tid < len) {
+        const size_t gi = (size_t)(tc + tid) * p.HV + hv;
+        lg = log_gate(p.A_log[hv], bf16_to_f32(p.a[gi]), p.dt_bias[hv]);
+        beta = sigmoidf_(bf16_to_f32(p.b[gi]));
+    }
+    if (warp < 2) {
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, lg, o);
+            if ((tid & 31) >= o) lg += y;
+        }
+        if (warp == 0) sG[tid] = lg;
+        sBeta[tid] = beta;
+    }
+    if (warp == 0) {
+        umma::tmem_alloc(&tmem_base_sh, TM_COLS);
+        umma::tmem_relinquish();
+    }
+    if (tid == 0) {
+        umma::mbar_init(&mbar[0], 1);
+        umma::mbar_init(&mbar[1], 1);
+        umma::fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == 1) sG[tid] = lg + sG[31];
+    cp_async_wait_all();
+    sync_for_mma();
+    const uint32_t tmem = tmem_base_sh;
+    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+
+    // MMA_A: [K ; Q] K^T in bf16
+    if (tid == 0) {
+        constexpr uint32_t ID = umma::idesc_f16(128, 64, 1, 1, 0, 0);
+#pragma unroll
+        for (int k0 = 0; k0 < kDim; k0 += 16)
+            umma::mma_f16(tmem, umma::desc_kmaj(sKQ, 128, k0), umma::desc_kmaj(sKQ, 128, k0), ID, k0 > 0);
+        umma::mma_commit(&mbar[0]);
+    }
+    if (!wait_mma(&mbar[0], 0)) goto done;
+    umma::fence_after_sync();
+
+    // masks: rows 0-63 -> A (fp32), rows 64-127 -> P (f16, rows 64-127 of [T ; P])
+    {
+        const int i = tid & 63;
+        const float gi = sG[i];
+        const float bi = sBeta[i];
+#pragma unroll
+        for (int c16 = 0; c16 < C; c16 += 16) {
+            float d[16];
+            umma::tmem_ld16(tmem + lane_base + c16, d);
+            float r[16];
+            if (tid < 64) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int jj = c16 + e;
+                    r[e] = (jj < i) ? bi * __expf(fminf(gi - sG[jj], 0.f)) * d[e] : 0.f;
+                }
+#pragma unroll
+                for (int e = 0; e < 16; e += 4)
+                    *reinterpret_cast<float4*>(sA + i * LDA + c16 + e) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int jj = c16 + e;
+                    r[e] = (jj <= i) ? p.scale * __expf(fminf(gi - sG[jj], 0.f)) * d[e] : 0.f;
+                }
+                st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), r);
+                st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), r + 8);
+            }
+        }
+    }
+    __syncthreads();
+
+    // T = (I + A)^-1; f16 copies: rows 0-63 of [T ; P] and T as MN-major B
+    solve_T(sA, sT, sX, tid);
+    {
+        const int i = tid >> 1, h = (tid & 1) * 32;  // row i, columns h..h+31
+        const float* tr = sT + i * LDA + h;
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+            const float4 a = *reinterpret_cast<const float4*>(tr + c);
+            const float4 b = *reinterpret_cast<const float4*>(tr + c + 4);
+            const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            st_f16x8(sm + OFF_TP, umma::kmaj_off(i, h + c, 128), x);  // A rows: T[i][j]
+            st_f16x8(sm + OFF_TB, umma::mnmaj_off(h + c, i, C), x);   // B: (n = m, k = j) = T[j][m]
+        }
+    }
+    sync_for_mma();
+
+    // MMA_P: [T ; P] T -> rows 64-127 = P' = P T
+    if (tid == 0) {
+        constexpr uint32_t ID = umma::idesc_f16(128, 64, 0, 0, 0, 1);
+        const uint32_t sTP = umma::smem_u32(sm + OFF_TP), sTB = umma::smem_u32(sm + OFF_TB);
+#pragma unroll
+        for (int k0 = 0; k0 < C; k0 += 16)
+            umma::mma_f16(tmem, umma::desc_kmaj(sTP, 128, k0), umma::desc_mnmaj(sTB, C, k0), ID, k0 > 0);
+        umma::mma_commit(&mbar[1]);
+    }
+    if (!wait_mma(&mbar[1], 0)) goto done;
+    umma::fence_after_sync();
+    if (tid >= 64) {
+        const int i = tid - 64;
+#pragma unroll
+        for (int c16 = 0; c16 < C; c16 += 16) {
+            float d[16];
+            umma::tmem_ld16(tmem + lane_base + c16, d);
+            st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), d);
+            st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), d + 8);
+        }
+    }
+    __syncthreads();
+
+    // slot <- [T ; P'] tile as laid out in shared memory, gamma, beta
+    {
+        unsigned char* slot = ws + ((size_t)s * p.HV + hv) * kSlotBytes;
+#pragma unroll
+        for (int it = 0; it < (int)(kTileTP / 16 / NT); ++it) {
+            const int idx = tid + it * NT;
+            reinterpret_cast<uint4*>(slot)[idx] = reinterpret_cast<const uint4*>(sm + OFF_TP)[idx];
+        }
+        if (tid < 64) {
+            reinterpret_cast<float*>(slot + kTileTP)[tid] = sG[tid];
+            reinterpret_cast<float*>(slot + kTileTP + 256)[tid] = sBeta[tid];
+        }
+    }
+
+done:
+    umma::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, TM_COLS);
+}
+
+}  // namespace prep
+
+// ============================================================================
+// chain kernel
+// ============================================================================
+namespace chain {
+
+constexpr int NT = 256;  // 8 warps: TMEM lane quarter = warp % 4, column half = warp / 4
+constexpr int VT = 64;   // state columns (v) per CTA
+constexpr int HALF = VT / 2;
+
+constexpr uint32_t OFF_KQ = 0;                     // [K ; Q~] f16 K-major 128 x 128     32 KiB
+constexpr uint32_t OFF_TP = 32768;                 // [T ; P'] f16, 2 buffers            32 KiB
+constexpr uint32_t OFF_SH = OFF_TP + 2 * kTileTP;  // S f16 MN-major (v x k, kext 128)   16 KiB
+constexpr uint32_t OFF_Y = OFF_SH + 16384;         // Y MN-major (v x 64 tokens)          8 KiB
+constexpr uint32_t OFF_DL = OFF_Y + 8192;          // Delta MN-major (v x 64 tokens)      8 KiB
+constexpr uint32_t OFF_KT = OFF_DL + 8192;         // K~ MN-major (k x 64 tokens)        16 KiB
+constexpr uint32_t OFF_RK = OFF_KT + 16384;        // raw k rows bf16 [64][128]          16 KiB
+constexpr uint32_t OFF_RQ = OFF_RK + 16384;        // raw q rows bf16 [64][128]          16 KiB
+constexpr uint32_t OFF_RV = OFF_RQ + 16384;        // raw v rows bf16 [2][64][VT] (swz)  16 KiB
+constexpr uint32_t OFF_GB = OFF_RV + 2 * C * VT * 2;  // gamma / beta fp32, 2 buffers    1 KiB
+constexpr uint32_t SMEM_BYTES = OFF_GB + 2 * 512 + 1024;
+static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
+
+constexpr uint32_t TM_1 = 0, TM_2 = 64, TM_3 = 128, TM_S = 192, TM_COLS = 256;
+
+// raw v row r, 16-byte piece c (8 values), XOR-swizzled for conflict-free row reads
+__device__ __forceinline__ uint32_t rawv_off(int r, int c) { return r * (VT * 2) + ((c ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ void prefetch(const PrefillParams& p, const unsigned char* ws, unsigned char* sm,
+                                         int buf, long long tc, int len, long long slot, int hq, int hv,
+                                         int v0, int tid) {
+    const uint32_t rk = umma::smem_u32(sm + OFF_RK), rq = umma::smem_u32(sm + OFF_RQ);
+    const uint32_t rv = umma::smem_u32(sm + OFF_RV) + buf * (C * VT * 2);
+#pragma unroll
+    for (int it = 0; it < C * 16 / NT; ++it) {
+        const int idx = tid + it * NT, r = idx >> 4, c = idx & 15;
+        const bool ok = r < len;
+        const size_t row = ok ? ((size_t)(tc + r) * p.H + hq) * kDim + c * 8 : 0;
+        cp_async16(rk + idx * 16, p.k + row, ok);
+        cp_async16(rq + idx * 16, p.q + row, ok);
+    }
+#pragma unroll
+    for (int it = 0; it < C * (VT / 8) / NT; ++it) {
+        const int idx = tid + it * NT, r = idx / (VT / 8), c = idx % (VT / 8);
+        const bool ok = r < len;
+        const size_t off = ok ? ((size_t)(tc + r) * p.HV + hv) * kDim + v0 + c * 8 : 0;
+        cp_async16(rv + rawv_off(r, c), p.v + off, ok);
+    }
+    const unsigned char* src = ws + ((size_t)slot * p.HV + hv) * kSlotBytes;
+    const uint32_t tp = umma::smem_u32(sm + OFF_TP) + buf * kTileTP;
+#pragma unroll
+    for (int it = 0; it < (int)(kTileTP / 16 / NT); ++it) {
+        const int idx = tid + it * NT;
+        cp_async16(tp + idx * 16, src + idx * 16, true);
+    }
+    if (tid < 32) cp_async16(umma::smem_u32(sm + OFF_GB) + buf * 512 + tid * 16, src + kTileTP + tid * 16, true);
+    cp_async_commit();
+}
+
+__global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const PrefillParams p,
+                                                                        const unsigned char* ws) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t mbar[3];
+    __shared__ uint32_t tmem_base_sh;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = 32 * quarter + lane;  // TMEM lane owned by this thread
     const int vt = blockIdx.x % (kDim / VT);
     const long long nh = blockIdx.x / (kDim / VT);
     const int hv = (int)(nh % p.HV), n = (int)(nh / p.HV);
     const int hq = hv / p.rep;
     const int v0 = vt * VT;
+    const int cb = HALF * half;  // this thread's first column within the tile
 
     long long t0, t1;
     seq_bounds(p, n, t0, t1);
     if (tid < VT) zero_uncovered_outputs(p, n, t0, t1, hv, v0 + tid, true);
-
-    float* sSf = reinterpret_cast<float*>(sm + OFF_SF);  // [v][k]
-    float* sA = reinterpret_cast<float*>(sm + OFF_A);    // [i][j], stride LDA
-    float* sT = reinterpret_cast<float*>(sm + OFF_T);    // [i][j], stride LDA
-    float* sX = reinterpret_cast<float*>(sm + OFF_X);
-    float* sG = reinterpret_cast<float*>(sm + OFF_G);
-    float* sBeta = reinterpret_cast<float*>(sm + OFF_BETA);
-    const size_t state_off = ((size_t)nh * kDim + v0) * kDim;  // new_state[n][hv][v0][0]
-
+    const size_t state_off = ((size_t)nh * kDim + v0) * kDim;  // [n][hv][v0][0]
     if (t1 == t0) {  // empty sequence: the final state stays zero
         for (int idx = tid; idx < VT * kDim / 4; idx += NT)
             reinterpret_cast<float4*>(p.new_state + state_off)[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
         return;
     }
-
-    // initial state: fp32 [v][k] in smem and its f16 K-major copy (B of MMA_1)
-    for (int idx = tid; idx < VT * kDim; idx += NT) {
-        const int v = idx >> 7, k = idx & 127;
-        const float s = p.state ? p.state[state_off + idx] : 0.f;
-        sSf[idx] = s;
-        *reinterpret_cast<__half*>(sm + OFF_SH + umma::kmaj_off(v, k, VT)) = __float2half_rn(s);
-    }
-    // T is lower triangular: its upper blocks stay zero for the whole kernel
-    for (int idx = tid; idx < 64 * 64; idx += NT) {
-        const int i = idx >> 6, j = idx & 63;
-        if ((j >> 4) > (i >> 4)) sT[i * LDA + j] = 0.f;
-    }
+    const long long slot0 = t0 / C + n;
 
     if (warp == 0) {
         umma::tmem_alloc(&tmem_base_sh, TM_COLS);
@@ -271,285 +463,144 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_kernel(const PrefillP
     }
     if (tid == 0) {
 #pragma unroll
-        for (int b = 0; b < 5; ++b) umma::mbar_init(&mbar[b], 1);
+        for (int b = 0; b < 3; ++b) umma::mbar_init(&mbar[b], 1);
         umma::fence_mbar_init();
     }
+    prefetch(p, ws, sm, 0, t0, (int)((t1 - t0) < C ? (t1 - t0) : C), slot0, hq, hv, v0, tid);
     umma::fence_before_sync();
     __syncthreads();
     umma::fence_after_sync();
     const uint32_t tmem = tmem_base_sh;
-    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);  // this warp's lane quarter
 
-    const uint32_t sKQ = umma::smem_u32(sm + OFF_KQ), sTP = umma::smem_u32(sm + OFF_TP);
-    const uint32_t sTB = umma::smem_u32(sm + OFF_TB);
-    const uint32_t sSH = umma::smem_u32(sm + OFF_SH), sY = umma::smem_u32(sm + OFF_Y);
-    const uint32_t sDL = umma::smem_u32(sm + OFF_DL), sKT = umma::smem_u32(sm + OFF_KT);
-    constexpr uint32_t ID_KK = umma::idesc_f16(128, 64, 0, 0, 0, 0);   // [K;Q] x K
-    constexpr uint32_t ID_S = umma::idesc_f16(128, VT, 0, 0, 0, 0);    // [K;Q~] x S
-    constexpr uint32_t ID_P = umma::idesc_f16(128, 64, 0, 0, 0, 1);    // [T;P] x T (MN-major B)
-    constexpr uint32_t ID_Y = umma::idesc_f16(128, VT, 0, 0, 0, 1);    // [T;P'] x Y (MN-major B)
-    constexpr uint32_t ID_D = umma::idesc_f16(128, VT, 0, 0, 1, 1);    // K~^T x Delta
-
-    const float A_log = p.A_log[hv], dt_bias = p.dt_bias[hv];
-    const float scale = p.scale;
-    uint32_t parity = 0;
-
-    // first chunk's rows and gates
-    const uint32_t rawK = umma::smem_u32(sm + OFF_RK), rawQ = umma::smem_u32(sm + OFF_RQ);
-    const uint32_t rawV = umma::smem_u32(sm + OFF_RV);
-    int buf = 0;
-    __nv_bfloat16 ga = __float2bfloat16_rn(0.f), gb = ga;
+    // initial state: S[k = row][v] for this thread's 32 columns -> TMEM (fp32) and f16 operand
     {
-        const int l0 = (int)((t1 - t0) < C ? (t1 - t0) : C);
-        prefetch_chunk(p, rawK, rawQ, rawV, t0, l0, hq, hv, v0, tid);
-        if (tid < l0) {
-            ga = p.a[(size_t)(t0 + tid) * p.HV + hv];
-            gb = p.b[(size_t)(t0 + tid) * p.HV + hv];
+#pragma unroll
+        for (int c16 = 0; c16 < HALF; c16 += 16) {
+            float s[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+                s[e] = p.state ? p.state[state_off + (size_t)(cb + c16 + e) * kDim + row] : 0.f;
+            umma::tmem_st16(tl + TM_S + cb + c16, s);
+            st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c16, row, kDim), s);
+            st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c16 + 8, row, kDim), s + 8);
         }
     }
 
+    const uint32_t sKQ = umma::smem_u32(sm + OFF_KQ), sTP0 = umma::smem_u32(sm + OFF_TP);
+    const uint32_t sSH = umma::smem_u32(sm + OFF_SH), sY = umma::smem_u32(sm + OFF_Y);
+    const uint32_t sDL = umma::smem_u32(sm + OFF_DL), sKT = umma::smem_u32(sm + OFF_KT);
+    constexpr uint32_t ID_S = umma::idesc_f16(128, VT, 0, 0, 0, 1);  // [K;Q~] x S (MN-major B)
+    constexpr uint32_t ID_Y = umma::idesc_f16(128, VT, 0, 0, 0, 1);  // [T;P'] x Y (MN-major B)
+    constexpr uint32_t ID_D = umma::idesc_f16(128, VT, 0, 0, 1, 1);  // K~^T x Delta
+    uint32_t parity = 0;
+    int buf = 0;
+
     for (long long tc = t0; tc < t1; tc += C, parity ^= 1, buf ^= 1) {
         const int len = (int)((t1 - tc) < C ? (t1 - tc) : C);
+        const float* sG = reinterpret_cast<const float*>(sm + OFF_GB + buf * 512);
+        const float* sBeta = sG + 64;
 
-        // ---- (a) this chunk's rows arrived: convert q / k; gates; prefetch the next chunk ----
+        // ---- (a) operands of this chunk from the raw rows; prefetch the next chunk ----
         cp_async_wait_all();
         __syncthreads();
-        convert_qk(sm, tid);
-        float lg = 0.f, beta = 0.f;
-        if (tid < len) {
-            lg = log_gate(A_log, bf16_to_f32(ga), dt_bias);
-            beta = sigmoidf_(bf16_to_f32(gb));
+        const float gC = sG[C - 1];
+#pragma unroll
+        for (int it = 0; it < C * 16 / NT; ++it) {
+            const int idx = tid + it * NT, r = idx >> 4, c = idx & 15;
+            const float gr = sG[r];
+            float x[8], y[8];
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + OFF_RK + idx * 16), x);
+            st_f16x8(sm + OFF_KQ, umma::kmaj_off(r, c * 8, 128), x);  // K
+            const float fk = __expf(fminf(gC - gr, 0.f));
+#pragma unroll
+            for (int e = 0; e < 8; ++e) y[e] = x[e] * fk;
+            st_f16x8(sm + OFF_KT, umma::mnmaj_off(c * 8, r, C), y);   // K~ (MN-major)
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + OFF_RQ + idx * 16), x);
+            const float fq = p.scale * __expf(fminf(gr, 0.f));
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[e] *= fq;
+            st_f16x8(sm + OFF_KQ, umma::kmaj_off(64 + r, c * 8, 128), x);  // Q~
         }
         {
             const long long tn = tc + C;
             if (tn < t1) {
                 const int ln = (int)((t1 - tn) < C ? (t1 - tn) : C);
-                prefetch_chunk(p, rawK, rawQ, rawV + (uint32_t)(buf ^ 1) * (C * VT * 2), tn, ln, hq, hv, v0, tid);
-                if (tid < ln) {
-                    ga = p.a[(size_t)(tn + tid) * p.HV + hv];
-                    gb = p.b[(size_t)(tn + tid) * p.HV + hv];
-                }
+                prefetch(p, ws, sm, buf ^ 1, tn, ln, slot0 + (tn - t0) / C, hq, hv, v0, tid);
             }
         }
-        // inclusive scan of log g over the 64 tokens (warps 0 and 1)
-        if (warp < 2) {
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                float y = __shfl_up_sync(0xffffffffu, lg, o);
-                if ((tid & 31) >= o) lg += y;
-            }
-            if (warp == 0) sG[tid] = lg;
-            sBeta[tid] = beta;
-        }
-        __syncthreads();
-        if (warp == 1) sG[tid] = lg + sG[31];
-        umma::fence_proxy_async_smem();
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
+        sync_for_mma();
 
-        // ---- (b) MMA_A: [K;Q] K^T ----
+        // ---- (b) MMA_1: [K ; Q~] S ----
         if (tid == 0) {
 #pragma unroll
             for (int k0 = 0; k0 < kDim; k0 += 16)
-                umma::mma_f16(tmem + TM_A, umma::desc_kmaj(sKQ, 128, k0), umma::desc_kmaj(sKQ, 128, k0), ID_KK,
+                umma::mma_f16(tmem + TM_1, umma::desc_kmaj(sKQ, 128, k0), umma::desc_mnmaj(sSH, kDim, k0), ID_S,
                               k0 > 0);
             umma::mma_commit(&mbar[0]);
         }
-        if (__syncthreads_or(!umma::mbar_wait(&mbar[0], parity, kWaitBudget))) goto done;
+        if (!wait_mma(&mbar[0], parity)) goto done;
         umma::fence_after_sync();
 
-        const float gC = sG[C - 1];
-        // ---- (c) masks -> A (fp32) and P (f16 operand); Q~ and K~ operands ----
-        {
-            const int i = tid & 63;
-            const float gi = sG[i];
+        // ---- (c) Y rows (0-63); Q~S rows (64-127) stay in registers ----
+        float qs[HALF];
+        if (row < 64) {
+            const int i = row;
+            const float eg = __expf(fminf(sG[i], 0.f)), b_i = sBeta[i];
 #pragma unroll
-            for (int c16 = 0; c16 < C; c16 += 16) {
-                float d[16];
-                umma::tmem_ld16(tmem + lane_base + TM_A + c16, d);
-                float r[16];
-                if (tid < 64) {
-                    const float bi = sBeta[i];
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int j = c16 + e;
-                        r[e] = (j < i) ? bi * __expf(fminf(gi - sG[j], 0.f)) * d[e] : 0.f;
-                    }
-#pragma unroll
-                    for (int e = 0; e < 16; e += 4)
-                        *reinterpret_cast<float4*>(sA + i * LDA + c16 + e) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int j = c16 + e;
-                        r[e] = (j <= i) ? scale * __expf(fminf(gi - sG[j], 0.f)) * d[e] : 0.f;
-                    }
-                    st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), r);
-                    st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), r + 8);
-                }
-            }
-            if (tid >= 64) {
-                // Q~ row i = scale e^{gamma_i} q_i, in place over Q (rows 64-127)
-                const float f = scale * expf(gi);
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const uint32_t off = umma::kmaj_off(64 + i, c * 8, 128);
-                    uint4 raw = *reinterpret_cast<uint4*>(sm + OFF_KQ + off);
-                    __half2* h = reinterpret_cast<__half2*>(&raw);
-                    float x[8];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        float2 f2 = __half22float2(h[e]);
-                        x[2 * e] = f2.x * f;
-                        x[2 * e + 1] = f2.y * f;
-                    }
-                    st_f16x8(sm + OFF_KQ, off, x);
-                }
-            } else {
-                // K~ row i = e^{gamma_C - gamma_i} k_i, MN-major (m = k index, K-dim = token)
-                const float f = expf(fminf(gC - gi, 0.f));
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    uint4 raw = *reinterpret_cast<uint4*>(sm + OFF_KQ + umma::kmaj_off(i, c * 8, 128));
-                    __half2* h = reinterpret_cast<__half2*>(&raw);
-                    float x[8];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        float2 f2 = __half22float2(h[e]);
-                        x[2 * e] = f2.x * f;
-                        x[2 * e + 1] = f2.y * f;
-                    }
-                    st_f16x8(sm + OFF_KT, umma::mnmaj_off(c * 8, i, C), x);
-                }
-            }
-        }
-        umma::fence_proxy_async_smem();
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
-
-        // ---- (d) MMA_1: [K ; Q~] S (runs during the solve) ----
-        if (tid == 0) {
-#pragma unroll
-            for (int k0 = 0; k0 < kDim; k0 += 16)
-                umma::mma_f16(tmem + TM_1, umma::desc_kmaj(sKQ, 128, k0), umma::desc_kmaj(sSH, VT, k0), ID_S,
-                              k0 > 0);
-            umma::mma_commit(&mbar[1]);
-        }
-
-        // ---- (e) T = (I + A)^-1; f16 copies: rows 0-63 of [T;P] and T as MN-major B ----
-        solve_T(sA, sT, sX, tid);
-        {
-            const int i = tid >> 1, h = (tid & 1) * 32;  // row i, columns h..h+31
-            const float* tr = sT + i * LDA + h;
-#pragma unroll
-            for (int c = 0; c < 32; c += 8) {
-                float x[8];
-                const float4 a = *reinterpret_cast<const float4*>(tr + c);
-                const float4 b = *reinterpret_cast<const float4*>(tr + c + 4);
-                x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-                x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-                st_f16x8(sm + OFF_TP, umma::kmaj_off(i, h + c, 128), x);  // A rows: T[i][j]
-                st_f16x8(sm + OFF_TB, umma::mnmaj_off(h + c, i, C), x);   // B: (n = m, k = j) = T[j][m]
-            }
-        }
-        umma::fence_proxy_async_smem();
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
-
-        // ---- (f) MMA_P: [T ; P] T -> rows 64-127 = P' ----
-        if (tid == 0) {
-#pragma unroll
-            for (int k0 = 0; k0 < C; k0 += 16)
-                umma::mma_f16(tmem + TM_A, umma::desc_kmaj(sTP, 128, k0), umma::desc_mnmaj(sTB, C, k0), ID_P,
-                              k0 > 0);
-            umma::mma_commit(&mbar[2]);
-        }
-
-        // ---- (g) Y rows (0-63) from MMA_1; keep Q~S rows (64-127) ----
-        if (__syncthreads_or(!umma::mbar_wait(&mbar[1], parity, kWaitBudget))) goto done;
-        umma::fence_after_sync();
-        float qs[VT];
-        if (tid < 64) {
-            const int i = tid;
-            const float eg = expf(sG[i]), b_i = sBeta[i];
-#pragma unroll
-            for (int c16 = 0; c16 < VT; c16 += 16) {
-                float d[16];
-                umma::tmem_ld16(tmem + lane_base + TM_1 + c16, d);
-                float y[16];
+            for (int c16 = 0; c16 < HALF; c16 += 16) {
+                float d[16], y[16];
+                umma::tmem_ld16(tl + TM_1 + cb + c16, d);
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const uint4 raw = *reinterpret_cast<const uint4*>(
-                        sm + OFF_RV + buf * (C * VT * 2) + rawv_off(i, c16 / 8 + h));
-                    const __nv_bfloat162* vb = reinterpret_cast<const __nv_bfloat162*>(&raw);
+                        sm + OFF_RV + buf * (C * VT * 2) + rawv_off(i, (cb + c16) / 8 + h));
+                    float vv[8];
+                    unpack_bf16x8(raw, vv);
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 vv = __bfloat1622float2(vb[e]);
-                        y[8 * h + 2 * e] = b_i * (vv.x - eg * d[8 * h + 2 * e]);
-                        y[8 * h + 2 * e + 1] = b_i * (vv.y - eg * d[8 * h + 2 * e + 1]);
-                    }
+                    for (int e = 0; e < 8; ++e) y[8 * h + e] = b_i * (vv[e] - eg * d[8 * h + e]);
                 }
-                st_f16x8(sm + OFF_Y, umma::mnmaj_off(c16, i, C), y);
-                st_f16x8(sm + OFF_Y, umma::mnmaj_off(c16 + 8, i, C), y + 8);
+                st_f16x8(sm + OFF_Y, umma::mnmaj_off(cb + c16, i, C), y);
+                st_f16x8(sm + OFF_Y, umma::mnmaj_off(cb + c16 + 8, i, C), y + 8);
             }
         } else {
 #pragma unroll
-            for (int c16 = 0; c16 < VT; c16 += 16) {
+            for (int c16 = 0; c16 < HALF; c16 += 16) {
                 float d[16];
-                umma::tmem_ld16(tmem + lane_base + TM_1 + c16, d);
+                umma::tmem_ld16(tl + TM_1 + cb + c16, d);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) qs[c16 + e] = d[e];
             }
         }
-        // P' rows (64-127) over P in [T ; P]
-        if (__syncthreads_or(!umma::mbar_wait(&mbar[2], parity, kWaitBudget))) goto done;
-        umma::fence_after_sync();
-        if (tid >= 64) {
-            const int i = tid - 64;
-#pragma unroll
-            for (int c16 = 0; c16 < C; c16 += 16) {
-                float d[16];
-                umma::tmem_ld16(tmem + lane_base + TM_A + c16, d);
-                st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), d);
-                st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), d + 8);
-            }
-        }
-        umma::fence_proxy_async_smem();
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
+        sync_for_mma();
 
-        // ---- (h) MMA_2: [T ; P'] Y ----
+        // ---- (d) MMA_2: [T ; P'] Y ----
         if (tid == 0) {
+            const uint32_t sTP = sTP0 + buf * kTileTP;
 #pragma unroll
             for (int k0 = 0; k0 < C; k0 += 16)
-                umma::mma_f16(tmem + TM_2, umma::desc_kmaj(sTP, 128, k0), umma::desc_mnmaj(sY, C, k0), ID_Y,
-                              k0 > 0);
-            umma::mma_commit(&mbar[3]);
+                umma::mma_f16(tmem + TM_2, umma::desc_kmaj(sTP, 128, k0), umma::desc_mnmaj(sY, C, k0), ID_Y, k0 > 0);
+            umma::mma_commit(&mbar[1]);
         }
-        if (__syncthreads_or(!umma::mbar_wait(&mbar[3], parity, kWaitBudget))) goto done;
+        if (!wait_mma(&mbar[1], parity)) goto done;
         umma::fence_after_sync();
 
-        // ---- (i) Delta rows (0-63) -> smem; output rows (64-127) -> HBM ----
-        if (tid < 64) {
-            const int i = tid;
+        // ---- (e) Delta rows (0-63) -> smem; output rows (64-127) -> HBM ----
+        if (row < 64) {
 #pragma unroll
-            for (int c16 = 0; c16 < VT; c16 += 16) {
+            for (int c16 = 0; c16 < HALF; c16 += 16) {
                 float d[16];
-                umma::tmem_ld16(tmem + lane_base + TM_2 + c16, d);
-                st_f16x8(sm + OFF_DL, umma::mnmaj_off(c16, i, C), d);
-                st_f16x8(sm + OFF_DL, umma::mnmaj_off(c16 + 8, i, C), d + 8);
+                umma::tmem_ld16(tl + TM_2 + cb + c16, d);
+                st_f16x8(sm + OFF_DL, umma::mnmaj_off(cb + c16, row, C), d);
+                st_f16x8(sm + OFF_DL, umma::mnmaj_off(cb + c16 + 8, row, C), d + 8);
             }
         } else {
-            const int i = tid - 64;
-            __nv_bfloat16* op = p.out + ((size_t)(tc + i) * p.HV + hv) * kDim + v0;
+            const int i = row - 64;
+            __nv_bfloat16* op = p.out + ((size_t)(tc + i) * p.HV + hv) * kDim + v0 + cb;
 #pragma unroll
-            for (int c16 = 0; c16 < VT; c16 += 16) {
+            for (int c16 = 0; c16 < HALF; c16 += 16) {
                 float d[16];
-                umma::tmem_ld16(tmem + lane_base + TM_2 + c16, d);
+                umma::tmem_ld16(tl + TM_2 + cb + c16, d);
                 if (i < len) {
                     __nv_bfloat162 o[8];
 #pragma unroll
@@ -560,47 +611,44 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_kernel(const PrefillP
                 }
             }
         }
-        umma::fence_proxy_async_smem();
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
+        sync_for_mma();
 
-        // ---- (j) MMA_3: K~^T Delta ----
+        // ---- (f) MMA_3: K~^T Delta ----
         if (tid == 0) {
 #pragma unroll
             for (int k0 = 0; k0 < C; k0 += 16)
-                umma::mma_f16(tmem + TM_3, umma::desc_mnmaj(sKT, C, k0), umma::desc_mnmaj(sDL, C, k0), ID_D,
-                              k0 > 0);
-            umma::mma_commit(&mbar[4]);
+                umma::mma_f16(tmem + TM_3, umma::desc_mnmaj(sKT, C, k0), umma::desc_mnmaj(sDL, C, k0), ID_D, k0 > 0);
+            umma::mma_commit(&mbar[2]);
         }
-        if (__syncthreads_or(!umma::mbar_wait(&mbar[4], parity, kWaitBudget))) goto done;
+        if (!wait_mma(&mbar[2], parity)) goto done;
         umma::fence_after_sync();
 
-        // ---- (k) state update: thread k owns row k of S (all VT columns) ----
+        // ---- (g) S = e^{gamma_C} S + K~^T Delta (TMEM, fp32) and its f16 operand copy ----
         {
-            const int k = tid;
-            const float decay = expf(gC);
+            const float decay = __expf(fminf(gC, 0.f));
 #pragma unroll
-            for (int c16 = 0; c16 < VT; c16 += 16) {
-                float d[16];
-                umma::tmem_ld16(tmem + lane_base + TM_3 + c16, d);
+            for (int c16 = 0; c16 < HALF; c16 += 16) {
+                float s[16], d[16];
+                umma::tmem_ld16(tl + TM_S + cb + c16, s);
+                umma::tmem_ld16(tl + TM_3 + cb + c16, d);
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int v = c16 + e;
-                    const float s = fmaf(decay, sSf[v * kDim + k], d[e]);
-                    sSf[v * kDim + k] = s;
-                    *reinterpret_cast<__half*>(sm + OFF_SH + umma::kmaj_off(v, k, VT)) = __float2half_rn(s);
-                }
+                for (int e = 0; e < 16; ++e) s[e] = fmaf(decay, s[e], d[e]);
+                umma::tmem_st16(tl + TM_S + cb + c16, s);
+                st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c16, row, kDim), s);
+                st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c16 + 8, row, kDim), s + 8);
             }
         }
-        umma::fence_proxy_async_smem();
-        umma::fence_before_sync();
-        __syncthreads();
-        umma::fence_after_sync();
+        sync_for_mma();
     }
 
-    // final state (fp32, k-last): consecutive threads write consecutive k
-    for (int idx = tid; idx < VT * kDim; idx += NT) __stcs(p.new_state + state_off + idx, sSf[idx]);
+    // final state (fp32, k-last): for each v, consecutive threads write consecutive k
+#pragma unroll
+    for (int c16 = 0; c16 < HALF; c16 += 16) {
+        float s[16];
+        umma::tmem_ld16(tl + TM_S + cb + c16, s);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) __stcs(p.new_state + state_off + (size_t)(cb + c16 + e) * kDim + row, s[e]);
+    }
 
 done:
     cp_async_wait_all();  // no copy may still target shared memory when the CTA exits
@@ -609,17 +657,29 @@ done:
     if (warp == 0) umma::tmem_dealloc(tmem, TM_COLS);
 }
 
+}  // namespace chain
 }  // namespace chunk
 
-void launch_prefill_chunk(const PrefillParams& p, cudaStream_t st) {
+size_t prefill_workspace_bytes(int N, int T, int HV) {
+    return ((size_t)(T / chunk::C) + (size_t)N) * (size_t)HV * chunk::kSlotBytes;
+}
+
+void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st) {
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(chunk::gdn_prefill_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)chunk::SMEM_BYTES);
+        cudaFuncSetAttribute(chunk::prep::gdn_prefill_chunk_prep_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::prep::SMEM_BYTES);
+        cudaFuncSetAttribute(chunk::chain::gdn_prefill_chunk_chain_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain::SMEM_BYTES);
         attr_set = true;
     }
-    const long long blocks = (long long)p.N * p.HV * (kDim / chunk::VT);
-    chunk::gdn_prefill_chunk_kernel<<<(unsigned)blocks, chunk::NT, chunk::SMEM_BYTES, st>>>(p);
+    unsigned char* ws = static_cast<unsigned char*>(workspace);
+    const long long slots = (long long)(p.T / chunk::C) + p.N;
+    chunk::prep::gdn_prefill_chunk_prep_kernel<<<(unsigned)(slots * p.HV), chunk::prep::NT,
+                                                 chunk::prep::SMEM_BYTES, st>>>(p, ws);
+    const long long blocks = (long long)p.N * p.HV * (kDim / chunk::chain::VT);
+    chunk::chain::gdn_prefill_chunk_chain_kernel<<<(unsigned)blocks, chunk::chain::NT, chunk::chain::SMEM_BYTES,
+                                                   st>>>(p, ws);
 }
 
 }  // namespace gdn

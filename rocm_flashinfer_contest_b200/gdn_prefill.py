@@ -15,7 +15,9 @@ solution (solutions/gdn_prefill/main.py:31-84) and the contest definition
 
 A zero-length sequence gets an all-zero final state (gdn.py:234-235).
 Inputs are never modified; ``run_into`` is the destination-passing form and
-accepts ``new_state is state``.
+accepts ``new_state is state``.  The chunked kernels' workspace
+(gdn_prefill_workspace_bytes) comes from torch's caching allocator, so a
+call makes no cudaMalloc in steady state.
 """
 from __future__ import annotations
 
@@ -74,10 +76,12 @@ def run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, ne
             or not new_state.is_contiguous() or new_state.device != dev:
         raise ValueError("new_state must be a contiguous fp32 [N, HV, V, K] tensor on the inputs' device")
     scale = C.normalize_scale(scale, K)
+    ws_bytes = lib().gdn_prefill_workspace_bytes(N, T, HV)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
     st = lib().gdn_prefill_fwd(
         C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(state), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias),
         C.ptr(b), C.ptr(cu), 1 if cu.dtype == torch.int64 else 0, N, T, scale, H, HV, K, V,
-        C.ptr(output), C.ptr(new_state), C.stream_handle(dev))
+        C.ptr(output), C.ptr(new_state), C.ptr(ws), ws_bytes, C.stream_handle(dev))
     check("gdn_prefill_fwd", st)
     return output, new_state
 

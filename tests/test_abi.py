@@ -59,7 +59,8 @@ def _decode(**over):
 
 def _prefill(**over):
     d = dict(q=16, k=16, v=16, state=16, A_log=16, a=16, dt_bias=16, b=16, cu=16, cu64=1,
-             N=1, T=4, scale=0.0, H=1, HV=2, K=128, V=128, out=16, new_state=16, stream=None)
+             N=1, T=4, scale=0.0, H=1, HV=2, K=128, V=128, out=16, new_state=16, ws=None, ws_bytes=0,
+             stream=None)
     d.update(over)
     return _lib.lib().gdn_prefill_fwd(*d.values())
 
@@ -91,9 +92,23 @@ def test_decode_rejects_bad_arguments(over, code):
     (dict(cu=20, cu64=1), _lib.GDN_ERR_ALIGN),
     (dict(new_state=40), _lib.GDN_ERR_ALIGN),
     (dict(N=0, T=0), _lib.GDN_OK),
+    (dict(T=4096, N=2), _lib.GDN_ERR_INVALID),            # chunk path without a workspace
+    (dict(T=4096, N=2, ws=40, ws_bytes=1 << 30), _lib.GDN_ERR_ALIGN),
+    (dict(q=24), _lib.GDN_ERR_ALIGN),                     # prefill needs 16-byte aligned q/k/v/out
 ])
 def test_prefill_rejects_bad_arguments(over, code):
     assert _prefill(**over) == code
+
+
+def test_prefill_workspace_size(monkeypatch):
+    ws = _lib.lib().gdn_prefill_workspace_bytes
+    monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "128")
+    assert ws(1, 8192, 32) == (8192 // 64 + 1) * 32 * 16896
+    assert ws(16, 5000, 8) == (5000 // 64 + 16) * 8 * 16896
+    assert ws(3, 100, 8) == 0          # below the threshold: token-serial kernel, no workspace
+    assert ws(0, 0, 8) == 0
+    monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "0")
+    assert ws(3, 100, 8) == (100 // 64 + 3) * 8 * 16896
 
 
 def test_error_is_raised_as_exception():
