@@ -17,7 +17,8 @@ B200 build's partitioner for the 1/2/4/8-GPU decode configuration.
 
 ``apply_decode`` / ``apply_prefill`` cut a rank's inputs out of the full
 argument list; ``gather_*`` reassembles full outputs (used by tests only: in a
-real deployment the outputs stay where they were computed).
+real deployment the outputs stay where they were computed); an empty shard's
+result may be None.
 """
 from __future__ import annotations
 
@@ -133,9 +134,10 @@ def gather_decode(shards, outs, B: int, HV: int, V: int = 128, K: int = 128):
     """Reassemble (output [B,1,HV,V], new_state [B,HV,V,K]) from per-rank results."""
     o = torch.zeros((B, 1, HV, V), dtype=torch.bfloat16)
     s = torch.zeros((B, HV, V, K), dtype=torch.float32)
-    for sh, (so, ss) in zip(shards, outs):
+    for sh, res in zip(shards, outs):
         if sh.empty:
             continue
+        so, ss = res
         h0, h1 = sh.heads
         idx = torch.tensor(sh.seqs, dtype=torch.long)
         o[idx, :, h0:h1] = so.cpu()
@@ -148,9 +150,10 @@ def gather_prefill(shards, outs, cu, HV: int, V: int = 128, K: int = 128):
     N, T = len(cu_l) - 1, cu_l[-1]
     o = torch.zeros((T, HV, V), dtype=torch.bfloat16)
     s = torch.zeros((N, HV, V, K), dtype=torch.float32)
-    for sh, (so, ss) in zip(shards, outs):
+    for sh, res in zip(shards, outs):
         if sh.empty:
             continue
+        so, ss = res
         h0, h1 = sh.heads
         pos = 0
         for j, seq in enumerate(sh.seqs):
