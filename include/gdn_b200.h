@@ -37,6 +37,7 @@ extern "C" {
 #define GDN_ERR_ALIGN 3       /* a pointer violates the alignment above       */
 #define GDN_ERR_CUDA 4        /* the launch failed (cudaGetLastError)         */
 #define GDN_ERR_DEVICE 5      /* a kernel reported an error (bounded wait timed out) */
+#define GDN_ERR_TOO_LARGE 6   /* needs more than gdn_prefill_fwd_noalloc's fixed scratch */
 
 /* Version of this ABI (bumped on any signature change). */
 int gdn_abi_version(void);
@@ -99,6 +100,42 @@ int gdn_prefill_fwd(const void *q, const void *k, const void *v, const float *st
  * reference, whose AITER kernels allocate their intermediates with torch.
  */
 size_t gdn_prefill_workspace_bytes(int N, int T, int HV);
+
+/*
+ * gdn_prefill_fwd for callers that cannot allocate device memory.  No
+ * counterpart in the reference, whose Python solution allocates through
+ * torch.
+ *
+ * Callers that bind this library directly (cgo, JNI, a C serving loop) have
+ * no caching allocator to hand a workspace from; cudaMalloc there is slow and
+ * can synchronise the device in the middle of a latency-critical step, and
+ * some runtimes carve up device memory once at start-up and allow no
+ * allocation afterwards.  This entry point takes the same arguments as
+ * gdn_prefill_fwd minus the workspace, which it takes from a scratch array of
+ * 16 MiB defined inside the library: every device that loads the library
+ * holds those 16 MiB until the process exits.  It calls no cudaMalloc,
+ * cudaFree or other allocating routine.
+ *
+ * Limit: gdn_prefill_workspace_bytes(N, T, HV) must not exceed 16 MiB
+ * (16,777,216 bytes), i.e. (floor(T/64) + N) * HV <= 992 when the chunked
+ * kernels run (for example T < 1,984 at N = 1, HV = 32, or T < 7,744 at
+ * N = 4, HV = 8); larger problems return GDN_ERR_TOO_LARGE before anything
+ * is launched.  Problems below the chunk threshold need no scratch at all.
+ *
+ * The first call on a device looks up the scratch array's device address
+ * with that device current (the device of `stream` must be the current
+ * device, as for every entry point here); make that first call before any
+ * stream capture.  All calls share the one array and its contents carry over
+ * from the previous call; the kernels overwrite every byte they read, so
+ * nothing needs clearing, but calls whose work overlaps on the GPU (on
+ * different streams, or different host threads) race on it and must be
+ * serialised by the caller.
+ */
+int gdn_prefill_fwd_noalloc(const void *q, const void *k, const void *v, const float *state,
+                            const float *A_log, const void *a, const float *dt_bias, const void *b,
+                            const void *cu_seqlens, int cu_seqlens_is_int64, int N, int T,
+                            float scale, int H, int HV, int K, int V, void *out, float *new_state,
+                            void *stream);
 
 #ifdef __cplusplus
 }

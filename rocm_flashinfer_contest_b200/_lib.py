@@ -17,6 +17,7 @@ GDN_ERR_UNSUPPORTED = 2
 GDN_ERR_ALIGN = 3
 GDN_ERR_CUDA = 4
 GDN_ERR_DEVICE = 5
+GDN_ERR_TOO_LARGE = 6
 
 _vp, _f, _i = ctypes.c_void_p, ctypes.c_float, ctypes.c_int
 
@@ -30,6 +31,8 @@ SIGNATURES = {
     "gdn_prefill_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                              _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "gdn_prefill_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i]),
+    "gdn_prefill_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
+                                     _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp]),
     "gdn_umma_selftest": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
 }
 

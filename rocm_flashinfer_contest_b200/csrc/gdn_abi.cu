@@ -11,6 +11,7 @@ extern "C" const char* gdn_strerror(int status) {
         case GDN_ERR_ALIGN: return "misaligned pointer (see the alignment rules in gdn_b200.h)";
         case GDN_ERR_CUDA: return "CUDA launch failed";
         case GDN_ERR_DEVICE: return "a kernel reported a device-side error (bounded wait timed out)";
+        case GDN_ERR_TOO_LARGE: return "problem needs more than the 16 MiB scratch of gdn_prefill_fwd_noalloc";
         default: return "unknown status";
     }
 }
