@@ -82,7 +82,7 @@ int gdn_decode_fwd(const void *q, const void *k, const void *v, const float *sta
  *
  * T >= GDN_PREFILL_CHUNK_MIN (environment, default 128) runs the chunked
  * tensor-core kernels, which need a device workspace of at least
- * gdn_prefill_workspace_bytes(N, T, HV) bytes (16-byte aligned; its contents
+ * gdn_prefill_workspace_bytes(N, T, H, HV) bytes (16-byte aligned; its contents
  * on entry do not matter); shorter batches run the token-serial kernel and
  * need none (workspace may then be NULL).
  */
@@ -93,13 +93,14 @@ int gdn_prefill_fwd(const void *q, const void *k, const void *v, const float *st
                     void *workspace, size_t workspace_bytes, void *stream);
 
 /*
- * Workspace bytes gdn_prefill_fwd needs for (N, T, HV): 0 when the call will
- * take the token-serial kernel.  The chunked kernels keep one slot per
- * (64-token chunk, v-head) — the chunk's [T ; P'] operand tile plus its gates,
- * 16,896 bytes — for floor(T/64) + N chunks.  No counterpart in the
- * reference, whose AITER kernels allocate their intermediates with torch.
+ * Workspace bytes gdn_prefill_fwd needs for (N, T, H, HV): 0 when the call
+ * will take the token-serial kernel.  For each of floor(T/64) + N chunk slots
+ * the chunked kernels keep, per v-head, the chunk's [T ; P'] operand tile and
+ * gates (16,896 bytes) and, per q/k head, its f16 [K ; Q] operand tile
+ * (32,768 bytes).  No counterpart in the reference, whose AITER kernels
+ * allocate their intermediates with torch.
  */
-size_t gdn_prefill_workspace_bytes(int N, int T, int HV);
+size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV);
 
 /*
  * gdn_prefill_fwd for callers that cannot allocate device memory.  No
@@ -116,11 +117,12 @@ size_t gdn_prefill_workspace_bytes(int N, int T, int HV);
  * holds those 16 MiB until the process exits.  It calls no cudaMalloc,
  * cudaFree or other allocating routine.
  *
- * Limit: gdn_prefill_workspace_bytes(N, T, HV) must not exceed 16 MiB
- * (16,777,216 bytes), i.e. (floor(T/64) + N) * HV <= 992 when the chunked
- * kernels run (for example T < 1,984 at N = 1, HV = 32, or T < 7,744 at
- * N = 4, HV = 8); larger problems return GDN_ERR_TOO_LARGE before anything
- * is launched.  Problems below the chunk threshold need no scratch at all.
+ * Limit: gdn_prefill_workspace_bytes(N, T, H, HV) must not exceed 16 MiB
+ * (16,777,216 bytes), i.e. (floor(T/64) + N) * (16,896 * HV + 32,768 * H)
+ * <= 16 MiB when the chunked kernels run (for example T < 960 at N = 1,
+ * H = 16, HV = 32, or T < 3,840 at N = 4, H = 4, HV = 8); larger problems
+ * return GDN_ERR_TOO_LARGE before anything is launched.  Problems below the
+ * chunk threshold need no scratch at all.
  *
  * The first call on a device looks up the scratch array's device address
  * with that device current (the device of `stream` must be the current

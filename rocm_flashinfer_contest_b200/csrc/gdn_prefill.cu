@@ -24,9 +24,9 @@ static long long chunk_threshold() {
 
 static bool use_chunk_path(int T) { return (long long)T >= chunk_threshold(); }
 
-extern "C" size_t gdn_prefill_workspace_bytes(int N, int T, int HV) {
-    if (N <= 0 || T <= 0 || HV <= 0 || !use_chunk_path(T)) return 0;
-    return gdn::prefill_workspace_bytes(N, T, HV);
+extern "C" size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV) {
+    if (N <= 0 || T <= 0 || H <= 0 || HV <= 0 || !use_chunk_path(T)) return 0;
+    return gdn::prefill_workspace_bytes(N, T, H, HV);
 }
 
 extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state,
@@ -75,7 +75,7 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
         return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
     }
     if (T > 0 && use_chunk_path(T)) {
-        const size_t need = gdn::prefill_workspace_bytes(N, T, HV);
+        const size_t need = gdn::prefill_workspace_bytes(N, T, H, HV);
         if (!workspace || workspace_bytes < need) return GDN_ERR_INVALID;
         if (!gdn_aligned(workspace, 16)) return GDN_ERR_ALIGN;
         gdn::launch_prefill_chunk(p, workspace, st);

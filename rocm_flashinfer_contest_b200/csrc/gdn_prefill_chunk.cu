@@ -33,11 +33,18 @@
 //      gamma and beta into a workspace slot.
 //  * chain (one CTA per (sequence, v-head, 64-wide V tile), 8 warps): walks
 //      the chunks in order with the state resident in TMEM (fp32):
-//        MMA_1 : [K ; diag(scale e^gamma) Q] x S -> Y (rows 0-63), Q~S (rows 64-127)
-//        MMA_2 : [T ; P'] x Y                     -> Delta (rows 0-63), P'Y (rows 64-127)
-//        MMA_3 : K~^T x Delta,  S = e^{gamma_C} S + K~^T Delta
-//      while the next chunk's q / k / v rows and workspace slot stream into
-//      shared memory with cp.async.
+//        MMA_1 : [K ; Q] x S     -> KS (rows 0-63: Y = beta (V - e^gamma KS)), QS (rows 64-127)
+//        MMA_2 : [T ; P'] x Y    -> Delta (rows 0-63), P'Y (rows 64-127);
+//                                   O = scale e^gamma QS + P'Y
+//        MMA_3 : K^T x Delta~ with Delta~ = diag(e^{gamma_C - gamma}) Delta,
+//                S = e^{gamma_C} S + K^T Delta~  (= K~^T Delta)
+//      The diagonal scalings of Q and K are applied to rows of the products
+//      instead of to the operands, so [K ; Q] is a plain f16 copy of the
+//      input rows; and since the K rows of that K-major tile have exactly the
+//      bytes of an MN-major K^T tile whose two 64-wide blocks sit 16 KiB
+//      apart, MMA_3 reads K^T from the same tile.  The next chunk's rows and
+//      workspace slot stream in with cp.async and are converted while MMA_3
+//      of the current chunk runs.
 // Operands are f16 except in the prep MMA (bf16 inputs as given); every
 // accumulation is fp32 and the state carried between chunks is fp32.
 //
@@ -54,6 +61,14 @@ constexpr int C = 64;                    // tokens per chunk
 constexpr int LDA = 68;                  // fp32 row stride of the solve matrices
 constexpr uint32_t kTileTP = 16384;      // [T ; P'] f16, K-major 128 x 64
 constexpr uint32_t kSlotBytes = kTileTP + 2 * 256;  // + gamma[64], beta[64] (fp32)
+constexpr uint32_t kTileKQ = 32768;      // [K ; Q] f16, K-major 128 x 128
+
+// Workspace: (floor(T/64) + N) chunk slots; per slot HV (chunk, v-head)
+// records of kSlotBytes, then per slot H [K ; Q] tiles of kTileKQ.
+__host__ __device__ inline long long ws_slots(int N, int T) { return (long long)(T / 64) + N; }
+__device__ __forceinline__ unsigned char* ws_kq(const PrefillParams& p, const unsigned char* ws) {
+    return const_cast<unsigned char*>(ws) + (size_t)ws_slots(p.N, p.T) * p.HV * kSlotBytes;
+}
 
 // Clock budget of one wait for MMA completion (~70 ms at 1.9 GHz; the MMAs of
 // a chunk take microseconds).  On expiry the CTA stops, frees its TMEM and
@@ -84,6 +99,8 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_n() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t parity) {
     // every thread waits; the CTA agrees on the outcome
@@ -105,14 +122,17 @@ namespace prep {
 
 constexpr int NT = 128;
 constexpr uint32_t OFF_KQ = 0;                     // [K ; Q] bf16 K-major 128 x 128   32 KiB
+// A and the level scratch X only live after MMA_A has consumed [K ; Q], so
+// they share its 32 KiB; three CTAs fit on an SM.
+constexpr uint32_t OFF_A = 0;                      // A fp32 [64][LDA]                 17 KiB
+constexpr uint32_t OFF_X = OFF_A + 64 * LDA * 4;   // solve scratch, rows 16-63        12.75 KiB
 constexpr uint32_t OFF_TP = 32768;                 // [T ; P] f16 K-major 128 x 64     16 KiB
 constexpr uint32_t OFF_TB = OFF_TP + kTileTP;      // T as MN-major B (m x j) f16        8 KiB
-constexpr uint32_t OFF_A = OFF_TB + 8192;          // A fp32 [64][LDA]                 17 KiB
-constexpr uint32_t OFF_T = OFF_A + 64 * LDA * 4;   // T fp32 [64][LDA]                 17 KiB
-constexpr uint32_t OFF_X = OFF_T + 64 * LDA * 4;   // solve scratch, rows 16-63        12.75 KiB
-constexpr uint32_t OFF_G = OFF_X + 48 * LDA * 4;   // gamma[64]
+constexpr uint32_t OFF_T = OFF_TB + 8192;          // T fp32 [64][LDA]                 17 KiB
+constexpr uint32_t OFF_G = OFF_T + 64 * LDA * 4;   // gamma[64]
 constexpr uint32_t OFF_BETA = OFF_G + 256;         // beta[64]
-constexpr uint32_t SMEM_BYTES = OFF_BETA + 256 + 1024;  // + alignment slack (two CTAs per SM)
+constexpr uint32_t SMEM_BYTES = OFF_BETA + 256 + 1024;  // + alignment slack
+static_assert(OFF_X + 48 * LDA * 4 <= OFF_TP, "A and X fit in the [K ; Q] tile");
 constexpr uint32_t TM_COLS = 64;
 
 // Blocked T = (I + A)^-1 for the 64 x 64 strictly lower A in sA (fp32, row
@@ -186,7 +206,7 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
     }
 }
 
-__global__ void __launch_bounds__(NT, 2) gdn_prefill_chunk_prep_kernel(const PrefillParams p, unsigned char* ws) {
+__global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const PrefillParams p, unsigned char* ws) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -276,6 +296,22 @@ __global__ void __launch_bounds__(NT, 2) gdn_prefill_chunk_prep_kernel(const Pre
     }
     if (!wait_mma(&mbar[0], 0)) goto done;
     umma::fence_after_sync();
+
+    // the first v-head of each q/k head also publishes the chunk's [K ; Q]
+    // tile for the chain kernel: the same swizzled layout, converted to f16
+    if (hv % p.rep == 0) {
+        uint4* dst = reinterpret_cast<uint4*>(ws_kq(p, ws) + ((size_t)s * p.H + hq) * kTileKQ);
+#pragma unroll 4
+        for (int idx = tid; idx < (int)(kTileKQ / 16); idx += NT) {
+            float x[8];
+            unpack_bf16x8(reinterpret_cast<const uint4*>(sm + OFF_KQ)[idx], x);
+            __half2 h[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(x[2 * e], x[2 * e + 1]);
+            dst[idx] = *reinterpret_cast<uint4*>(h);
+        }
+    }
+    __syncthreads();  // [K ; Q] is overwritten by A and X from here on
 
     // masks: rows 0-63 -> A (fp32), rows 64-127 -> P (f16, rows 64-127 of [T ; P])
     {
@@ -378,53 +414,56 @@ namespace chain {
 constexpr int NT = 256;  // 8 warps: TMEM lane quarter = warp % 4, column half = warp / 4
 constexpr int VT = 64;   // state columns (v) per CTA
 constexpr int HALF = VT / 2;
+constexpr uint32_t VROW = VT * 2 + 16;  // raw v row stride: padded so rows start in different banks
 
-constexpr uint32_t OFF_KQ = 0;                     // [K ; Q~] f16 K-major 128 x 128     32 KiB
-constexpr uint32_t OFF_TP = 32768;                 // [T ; P'] f16, 2 buffers            32 KiB
-constexpr uint32_t OFF_SH = OFF_TP + 2 * kTileTP;  // S f16 MN-major (v x k, kext 128)   16 KiB
-constexpr uint32_t OFF_Y = OFF_SH + 16384;         // Y MN-major (v x 64 tokens)          8 KiB
-constexpr uint32_t OFF_DL = OFF_Y + 8192;          // Delta MN-major (v x 64 tokens)      8 KiB
-constexpr uint32_t OFF_KT = OFF_DL + 8192;         // K~ MN-major (k x 64 tokens)        16 KiB
-constexpr uint32_t OFF_RK = OFF_KT + 16384;        // raw k rows bf16 [64][128]          16 KiB
-constexpr uint32_t OFF_RQ = OFF_RK + 16384;        // raw q rows bf16 [64][128]          16 KiB
-constexpr uint32_t OFF_RV = OFF_RQ + 16384;        // raw v rows bf16 [2][64][VT] (swz)  16 KiB
-constexpr uint32_t OFF_GB = OFF_RV + 2 * C * VT * 2;  // gamma / beta fp32, 2 buffers    1 KiB
-constexpr uint32_t SMEM_BYTES = OFF_GB + 2 * 512 + 1024;
+// Data of chunk j lives in buffer j % 2: chunk j + 2's copies start once
+// chunk j has finished with the buffer, a whole chunk before they are needed.
+constexpr int NBUF = 2;
+constexpr uint32_t OFF_KQ = 0;                         // [K ; Q] f16 (workspace copy), 2 bufs   64 KiB
+constexpr uint32_t OFF_TP = OFF_KQ + NBUF * kTileKQ;   // [T ; P'] f16 (workspace copy), 2 bufs  32 KiB
+constexpr uint32_t OFF_SH = OFF_TP + NBUF * kTileTP;   // S f16 MN-major (v x k, kext 128)       16 KiB
+constexpr uint32_t OFF_Y = OFF_SH + 16384;             // Y MN-major (v x 64 tokens)              8 KiB
+constexpr uint32_t OFF_DL = OFF_Y + 8192;              // Delta~ MN-major (v x 64 tokens)         8 KiB
+constexpr uint32_t OFF_RV = OFF_DL + 8192;             // v rows bf16 [2][64][VROW]              18 KiB
+constexpr uint32_t OFF_GB = OFF_RV + NBUF * C * VROW;  // gamma / beta fp32, 2 bufs               1 KiB
+constexpr uint32_t SMEM_BYTES = OFF_GB + NBUF * 512 + 1024;
 static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
 
 constexpr uint32_t TM_1 = 0, TM_2 = 64, TM_3 = 128, TM_S = 192, TM_COLS = 256;
+constexpr int kLowerBarrier = 1;  // named barrier of the four warps on TMEM lanes 0-63
 
-// raw v row r, 16-byte piece c (8 values), XOR-swizzled for conflict-free row reads
-__device__ __forceinline__ uint32_t rawv_off(int r, int c) { return r * (VT * 2) + ((c ^ (r & 7)) << 4); }
+__device__ __forceinline__ void lower_sync() {
+    asm volatile("bar.sync %0, %1;" ::"r"(kLowerBarrier), "r"(128) : "memory");
+}
 
-__device__ __forceinline__ void prefetch(const PrefillParams& p, const unsigned char* ws, unsigned char* sm,
-                                         int buf, long long tc, int len, long long slot, int hq, int hv,
-                                         int v0, int tid) {
-    const uint32_t rk = umma::smem_u32(sm + OFF_RK), rq = umma::smem_u32(sm + OFF_RQ);
-    const uint32_t rv = umma::smem_u32(sm + OFF_RV) + buf * (C * VT * 2);
-#pragma unroll
-    for (int it = 0; it < C * 16 / NT; ++it) {
-        const int idx = tid + it * NT, r = idx >> 4, c = idx & 15;
-        const bool ok = r < len;
-        const size_t row = ok ? ((size_t)(tc + r) * p.H + hq) * kDim + c * 8 : 0;
-        cp_async16(rk + idx * 16, p.k + row, ok);
-        cp_async16(rq + idx * 16, p.q + row, ok);
+// Copies of chunk [tc, tc + len) (workspace slot `slot`) into buffer `buf`:
+// the loader warp starts three bulk copies of the [K ; Q] and [T ; P'] tiles
+// and the gates, completing on `bar`; every thread copies its share of the v
+// rows with cp.async (rows past len zero-filled) as one commit group.
+__device__ __forceinline__ void issue_loads(const PrefillParams& p, const unsigned char* ws, unsigned char* sm,
+                                            uint64_t* bar, int buf, long long tc, int len, long long slot,
+                                            int hq, int hv, int v0, int tid, bool loader) {
+    if (loader) {
+        const int lane = tid & 31;
+        if (lane == 0) umma::mbar_arrive_expect_tx(bar, kTileKQ + kTileTP + 512);
+        __syncwarp();
+        const unsigned char* rec = ws + ((size_t)slot * p.HV + hv) * kSlotBytes;
+        const unsigned char* kq = ws_kq(p, ws) + ((size_t)slot * p.H + hq) * kTileKQ;
+        if (lane == 0) umma::bulk_g2s(umma::smem_u32(sm + OFF_KQ + buf * kTileKQ), kq, kTileKQ / 2, bar);
+        if (lane == 1)
+            umma::bulk_g2s(umma::smem_u32(sm + OFF_KQ + buf * kTileKQ + kTileKQ / 2), kq + kTileKQ / 2,
+                           kTileKQ / 2, bar);
+        if (lane == 2) umma::bulk_g2s(umma::smem_u32(sm + OFF_TP + buf * kTileTP), rec, kTileTP, bar);
+        if (lane == 3) umma::bulk_g2s(umma::smem_u32(sm + OFF_GB + buf * 512), rec + kTileTP, 512, bar);
     }
+    const uint32_t rv = umma::smem_u32(sm + OFF_RV) + buf * (C * VROW);
 #pragma unroll
     for (int it = 0; it < C * (VT / 8) / NT; ++it) {
         const int idx = tid + it * NT, r = idx / (VT / 8), c = idx % (VT / 8);
         const bool ok = r < len;
         const size_t off = ok ? ((size_t)(tc + r) * p.HV + hv) * kDim + v0 + c * 8 : 0;
-        cp_async16(rv + rawv_off(r, c), p.v + off, ok);
+        cp_async16(rv + r * VROW + c * 16, p.v + off, ok);
     }
-    const unsigned char* src = ws + ((size_t)slot * p.HV + hv) * kSlotBytes;
-    const uint32_t tp = umma::smem_u32(sm + OFF_TP) + buf * kTileTP;
-#pragma unroll
-    for (int it = 0; it < (int)(kTileTP / 16 / NT); ++it) {
-        const int idx = tid + it * NT;
-        cp_async16(tp + idx * 16, src + idx * 16, true);
-    }
-    if (tid < 32) cp_async16(umma::smem_u32(sm + OFF_GB) + buf * 512 + tid * 16, src + kTileTP + tid * 16, true);
     cp_async_commit();
 }
 
@@ -433,11 +472,13 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t mbar[3];
+    __shared__ uint64_t mbar[3];   // MMA_1, MMA_2, MMA_3 completion
+    __shared__ uint64_t ldbar[NBUF];  // chunk data of buffer 0 / 1 landed
     __shared__ uint32_t tmem_base_sh;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quarter = warp & 3, half = warp >> 2;
+    const bool lower = quarter < 2;       // TMEM lanes 0-63: the K rows (Y, Delta~)
     const int row = 32 * quarter + lane;  // TMEM lane owned by this thread
     const int vt = blockIdx.x % (kDim / VT);
     const long long nh = blockIdx.x / (kDim / VT);
@@ -445,6 +486,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
     const int hq = hv / p.rep;
     const int v0 = vt * VT;
     const int cb = HALF * half;  // this thread's first column within the tile
+    constexpr int kLoader = 2;   // warp issuing the bulk copies
 
     long long t0, t1;
     seq_bounds(p, n, t0, t1);
@@ -456,6 +498,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
         return;
     }
     const long long slot0 = t0 / C + n;
+    const long long nchunks = (t1 - t0 + C - 1) / C;
+    auto chunk_len = [&](long long j) { const long long r = t1 - t0 - C * j; return (int)(r < C ? r : C); };
 
     if (warp == 0) {
         umma::tmem_alloc(&tmem_base_sh, TM_COLS);
@@ -464,190 +508,166 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
     if (tid == 0) {
 #pragma unroll
         for (int b = 0; b < 3; ++b) umma::mbar_init(&mbar[b], 1);
+#pragma unroll
+        for (int b = 0; b < NBUF; ++b) umma::mbar_init(&ldbar[b], 1);
         umma::fence_mbar_init();
     }
-    prefetch(p, ws, sm, 0, t0, (int)((t1 - t0) < C ? (t1 - t0) : C), slot0, hq, hv, v0, tid);
-    umma::fence_before_sync();
     __syncthreads();
+    issue_loads(p, ws, sm, &ldbar[0], 0, t0, chunk_len(0), slot0, hq, hv, v0, tid, warp == kLoader);
+    if (nchunks > 1)
+        issue_loads(p, ws, sm, &ldbar[1], 1, t0 + C, chunk_len(1), slot0 + 1, hq, hv, v0, tid, warp == kLoader);
     umma::fence_after_sync();
     const uint32_t tmem = tmem_base_sh;
     const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);  // this warp's lane quarter
 
     // initial state: S[k = row][v] for this thread's 32 columns -> TMEM (fp32) and f16 operand
     {
+        float sv[HALF];
 #pragma unroll
-        for (int c16 = 0; c16 < HALF; c16 += 16) {
-            float s[16];
+        for (int e = 0; e < HALF; ++e) sv[e] = p.state ? p.state[state_off + (size_t)(cb + e) * kDim + row] : 0.f;
+        umma::tmem_st32(tl + TM_S + cb, sv);
 #pragma unroll
-            for (int e = 0; e < 16; ++e)
-                s[e] = p.state ? p.state[state_off + (size_t)(cb + c16 + e) * kDim + row] : 0.f;
-            umma::tmem_st16(tl + TM_S + cb + c16, s);
-            st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c16, row, kDim), s);
-            st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c16 + 8, row, kDim), s + 8);
-        }
+        for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c8, row, kDim), sv + c8);
     }
+    sync_for_mma();
 
-    const uint32_t sKQ = umma::smem_u32(sm + OFF_KQ), sTP0 = umma::smem_u32(sm + OFF_TP);
+    const uint32_t sKQ0 = umma::smem_u32(sm + OFF_KQ), sTP0 = umma::smem_u32(sm + OFF_TP);
     const uint32_t sSH = umma::smem_u32(sm + OFF_SH), sY = umma::smem_u32(sm + OFF_Y);
-    const uint32_t sDL = umma::smem_u32(sm + OFF_DL), sKT = umma::smem_u32(sm + OFF_KT);
-    constexpr uint32_t ID_S = umma::idesc_f16(128, VT, 0, 0, 0, 1);  // [K;Q~] x S (MN-major B)
+    const uint32_t sDL = umma::smem_u32(sm + OFF_DL);
+    constexpr uint32_t ID_S = umma::idesc_f16(128, VT, 0, 0, 0, 1);  // [K;Q] x S (MN-major B)
     constexpr uint32_t ID_Y = umma::idesc_f16(128, VT, 0, 0, 0, 1);  // [T;P'] x Y (MN-major B)
-    constexpr uint32_t ID_D = umma::idesc_f16(128, VT, 0, 0, 1, 1);  // K~^T x Delta
-    uint32_t parity = 0;
-    int buf = 0;
+    constexpr uint32_t ID_D = umma::idesc_f16(128, VT, 0, 0, 1, 1);  // K^T x Delta~ (both MN-major)
 
-    for (long long tc = t0; tc < t1; tc += C, parity ^= 1, buf ^= 1) {
-        const int len = (int)((t1 - tc) < C ? (t1 - tc) : C);
-        const float* sG = reinterpret_cast<const float*>(sm + OFF_GB + buf * 512);
+    for (long long j = 0; j < nchunks; ++j) {
+        const int b = (int)(j & 1);
+        const uint32_t par = (uint32_t)(j & 1), lpar = (uint32_t)((j >> 1) & 1);
+        const long long tc = t0 + C * j;
+        const int len = chunk_len(j);
+        // this chunk's v rows (chunk j + 1's commit group may still be in flight)
+        if (j + 1 < nchunks) cp_async_wait_n<1>(); else cp_async_wait_n<0>();
+        if (!wait_mma(&ldbar[b], lpar)) goto done;
+        const float* sG = reinterpret_cast<const float*>(sm + OFF_GB + b * 512);
         const float* sBeta = sG + 64;
-
-        // ---- (a) operands of this chunk from the raw rows; prefetch the next chunk ----
-        cp_async_wait_all();
-        __syncthreads();
         const float gC = sG[C - 1];
-#pragma unroll
-        for (int it = 0; it < C * 16 / NT; ++it) {
-            const int idx = tid + it * NT, r = idx >> 4, c = idx & 15;
-            const float gr = sG[r];
-            float x[8], y[8];
-            unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + OFF_RK + idx * 16), x);
-            st_f16x8(sm + OFF_KQ, umma::kmaj_off(r, c * 8, 128), x);  // K
-            const float fk = __expf(fminf(gC - gr, 0.f));
-#pragma unroll
-            for (int e = 0; e < 8; ++e) y[e] = x[e] * fk;
-            st_f16x8(sm + OFF_KT, umma::mnmaj_off(c * 8, r, C), y);   // K~ (MN-major)
-            unpack_bf16x8(*reinterpret_cast<const uint4*>(sm + OFF_RQ + idx * 16), x);
-            const float fq = p.scale * __expf(fminf(gr, 0.f));
-#pragma unroll
-            for (int e = 0; e < 8; ++e) x[e] *= fq;
-            st_f16x8(sm + OFF_KQ, umma::kmaj_off(64 + r, c * 8, 128), x);  // Q~
-        }
-        {
-            const long long tn = tc + C;
-            if (tn < t1) {
-                const int ln = (int)((t1 - tn) < C ? (t1 - tn) : C);
-                prefetch(p, ws, sm, buf ^ 1, tn, ln, slot0 + (tn - t0) / C, hq, hv, v0, tid);
-            }
-        }
-        sync_for_mma();
+        const uint32_t sKQ = sKQ0 + b * kTileKQ;
 
-        // ---- (b) MMA_1: [K ; Q~] S ----
+        // ---- MMA_1: [K ; Q] S ----
         if (tid == 0) {
+            umma::fence_after_sync();
 #pragma unroll
             for (int k0 = 0; k0 < kDim; k0 += 16)
                 umma::mma_f16(tmem + TM_1, umma::desc_kmaj(sKQ, 128, k0), umma::desc_mnmaj(sSH, kDim, k0), ID_S,
                               k0 > 0);
             umma::mma_commit(&mbar[0]);
         }
-        if (!wait_mma(&mbar[0], parity)) goto done;
+        if (!wait_mma(&mbar[0], par)) goto done;
         umma::fence_after_sync();
 
-        // ---- (c) Y rows (0-63); Q~S rows (64-127) stay in registers ----
+        // ---- lower: Y = beta (V - e^gamma KS) -> MMA_2;  upper: keep QS ----
         float qs[HALF];
-        if (row < 64) {
-            const int i = row;
-            const float eg = __expf(fminf(sG[i], 0.f)), b_i = sBeta[i];
+        {
+            float d[HALF];
+            umma::tmem_ld32(tl + TM_1 + cb, d);
+            if (lower) {
+                const int i = row;
+                const bool live = i < len;
+                const float eg = __expf(fminf(sG[i], 0.f)), b_i = sBeta[i];
+                const unsigned char* vrow = sm + OFF_RV + b * (C * VROW) + i * VROW + cb * 2;
 #pragma unroll
-            for (int c16 = 0; c16 < HALF; c16 += 16) {
-                float d[16], y[16];
-                umma::tmem_ld16(tl + TM_1 + cb + c16, d);
+                for (int c8 = 0; c8 < HALF; c8 += 8) {
+                    float vv[8], y[8];
+                    unpack_bf16x8(*reinterpret_cast<const uint4*>(vrow + c8 * 2), vv);
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint4 raw = *reinterpret_cast<const uint4*>(
-                        sm + OFF_RV + buf * (C * VT * 2) + rawv_off(i, (cb + c16) / 8 + h));
-                    float vv[8];
-                    unpack_bf16x8(raw, vv);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) y[8 * h + e] = b_i * (vv[e] - eg * d[8 * h + e]);
+                    for (int e = 0; e < 8; ++e) y[e] = live ? b_i * (vv[e] - eg * d[c8 + e]) : 0.f;
+                    st_f16x8(sm + OFF_Y, umma::mnmaj_off(cb + c8, i, C), y);
                 }
-                st_f16x8(sm + OFF_Y, umma::mnmaj_off(cb + c16, i, C), y);
-                st_f16x8(sm + OFF_Y, umma::mnmaj_off(cb + c16 + 8, i, C), y + 8);
-            }
-        } else {
+                umma::fence_proxy_async_smem();
+                umma::fence_before_sync();
+                lower_sync();
+                if (tid == 0) {
+                    umma::fence_after_sync();
+                    const uint32_t sTP = sTP0 + b * kTileTP;
 #pragma unroll
-            for (int c16 = 0; c16 < HALF; c16 += 16) {
-                float d[16];
-                umma::tmem_ld16(tl + TM_1 + cb + c16, d);
+                    for (int k0 = 0; k0 < C; k0 += 16)
+                        umma::mma_f16(tmem + TM_2, umma::desc_kmaj(sTP, 128, k0), umma::desc_mnmaj(sY, C, k0), ID_Y,
+                                      k0 > 0);
+                    umma::mma_commit(&mbar[1]);
+                }
+            } else {
 #pragma unroll
-                for (int e = 0; e < 16; ++e) qs[c16 + e] = d[e];
+                for (int e = 0; e < HALF; ++e) qs[e] = d[e];
             }
         }
-        sync_for_mma();
-
-        // ---- (d) MMA_2: [T ; P'] Y ----
-        if (tid == 0) {
-            const uint32_t sTP = sTP0 + buf * kTileTP;
-#pragma unroll
-            for (int k0 = 0; k0 < C; k0 += 16)
-                umma::mma_f16(tmem + TM_2, umma::desc_kmaj(sTP, 128, k0), umma::desc_mnmaj(sY, C, k0), ID_Y, k0 > 0);
-            umma::mma_commit(&mbar[1]);
-        }
-        if (!wait_mma(&mbar[1], parity)) goto done;
+        if (!wait_mma(&mbar[1], par)) goto done;
         umma::fence_after_sync();
 
-        // ---- (e) Delta rows (0-63) -> smem; output rows (64-127) -> HBM ----
-        if (row < 64) {
+        // ---- lower: Delta~ = e^{gamma_C - gamma} Delta -> MMA_3;  upper: outputs ----
+        {
+            float d[HALF];
+            umma::tmem_ld32(tl + TM_2 + cb, d);
+            if (lower) {
+                const float fk = __expf(fminf(gC - sG[row], 0.f));
 #pragma unroll
-            for (int c16 = 0; c16 < HALF; c16 += 16) {
-                float d[16];
-                umma::tmem_ld16(tl + TM_2 + cb + c16, d);
-                st_f16x8(sm + OFF_DL, umma::mnmaj_off(cb + c16, row, C), d);
-                st_f16x8(sm + OFF_DL, umma::mnmaj_off(cb + c16 + 8, row, C), d + 8);
-            }
-        } else {
-            const int i = row - 64;
-            __nv_bfloat16* op = p.out + ((size_t)(tc + i) * p.HV + hv) * kDim + v0 + cb;
+                for (int e = 0; e < HALF; ++e) d[e] *= fk;
 #pragma unroll
-            for (int c16 = 0; c16 < HALF; c16 += 16) {
-                float d[16];
-                umma::tmem_ld16(tl + TM_2 + cb + c16, d);
+                for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_DL, umma::mnmaj_off(cb + c8, row, C), d + c8);
+                umma::fence_proxy_async_smem();
+                umma::fence_before_sync();
+                lower_sync();
+                if (tid == 0) {
+                    // K^T read as MN-major from the [K ; Q] tile: its two 64-wide k
+                    // blocks are the tile's 16 KiB slabs
+                    umma::fence_after_sync();
+#pragma unroll
+                    for (int k0 = 0; k0 < C; k0 += 16)
+                        umma::mma_f16(tmem + TM_3, umma::desc_sw128(sKQ + (k0 >> 3) * 1024u, 16384u, 1024u),
+                                      umma::desc_mnmaj(sDL, C, k0), ID_D, k0 > 0);
+                    umma::mma_commit(&mbar[2]);
+                }
+            } else {
+                const int i = row - 64;
                 if (i < len) {
-                    __nv_bfloat162 o[8];
+                    const float fq = p.scale * __expf(fminf(sG[i], 0.f));  // scale e^{gamma_i}
+                    __nv_bfloat16* op = p.out + ((size_t)(tc + i) * p.HV + hv) * kDim + v0 + cb;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        o[e] = __floats2bfloat162_rn(qs[c16 + 2 * e] + d[2 * e], qs[c16 + 2 * e + 1] + d[2 * e + 1]);
-                    reinterpret_cast<uint4*>(op + c16)[0] = reinterpret_cast<uint4*>(o)[0];
-                    reinterpret_cast<uint4*>(op + c16)[1] = reinterpret_cast<uint4*>(o)[1];
+                    for (int c8 = 0; c8 < HALF; c8 += 8) {
+                        __nv_bfloat162 o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            o[e] = __floats2bfloat162_rn(fmaf(fq, qs[c8 + 2 * e], d[c8 + 2 * e]),
+                                                         fmaf(fq, qs[c8 + 2 * e + 1], d[c8 + 2 * e + 1]));
+                        *reinterpret_cast<uint4*>(op + c8) = *reinterpret_cast<uint4*>(o);
+                    }
                 }
             }
         }
-        sync_for_mma();
-
-        // ---- (f) MMA_3: K~^T Delta ----
-        if (tid == 0) {
-#pragma unroll
-            for (int k0 = 0; k0 < C; k0 += 16)
-                umma::mma_f16(tmem + TM_3, umma::desc_mnmaj(sKT, C, k0), umma::desc_mnmaj(sDL, C, k0), ID_D, k0 > 0);
-            umma::mma_commit(&mbar[2]);
-        }
-        if (!wait_mma(&mbar[2], parity)) goto done;
+        if (!wait_mma(&mbar[2], par)) goto done;
         umma::fence_after_sync();
 
-        // ---- (g) S = e^{gamma_C} S + K~^T Delta (TMEM, fp32) and its f16 operand copy ----
+        // ---- S = e^{gamma_C} S + K^T Delta~ (TMEM, fp32) and its f16 operand copy ----
         {
             const float decay = __expf(fminf(gC, 0.f));
+            float sv[HALF], d[HALF];
+            umma::tmem_ld32x2(tl + TM_S + cb, tl + TM_3 + cb, sv, d);
 #pragma unroll
-            for (int c16 = 0; c16 < HALF; c16 += 16) {
-                float s[16], d[16];
-                umma::tmem_ld16(tl + TM_S + cb + c16, s);
-                umma::tmem_ld16(tl + TM_3 + cb + c16, d);
+            for (int e = 0; e < HALF; ++e) sv[e] = fmaf(decay, sv[e], d[e]);
+            umma::tmem_st32(tl + TM_S + cb, sv);
 #pragma unroll
-                for (int e = 0; e < 16; ++e) s[e] = fmaf(decay, s[e], d[e]);
-                umma::tmem_st16(tl + TM_S + cb + c16, s);
-                st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c16, row, kDim), s);
-                st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c16 + 8, row, kDim), s + 8);
-            }
+            for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c8, row, kDim), sv + c8);
         }
         sync_for_mma();
+        // buffer b is free again: stream in chunk j + 2
+        if (j + 2 < nchunks)
+            issue_loads(p, ws, sm, &ldbar[b], b, tc + 2 * C, chunk_len(j + 2), slot0 + j + 2, hq, hv, v0, tid,
+                        warp == kLoader);
     }
 
     // final state (fp32, k-last): for each v, consecutive threads write consecutive k
+    {
+        float sv[HALF];
+        umma::tmem_ld32(tl + TM_S + cb, sv);
 #pragma unroll
-    for (int c16 = 0; c16 < HALF; c16 += 16) {
-        float s[16];
-        umma::tmem_ld16(tl + TM_S + cb + c16, s);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) __stcs(p.new_state + state_off + (size_t)(cb + c16 + e) * kDim + row, s[e]);
+        for (int e = 0; e < HALF; ++e) __stcs(p.new_state + state_off + (size_t)(cb + e) * kDim + row, sv[e]);
     }
 
 done:
@@ -660,8 +680,8 @@ done:
 }  // namespace chain
 }  // namespace chunk
 
-size_t prefill_workspace_bytes(int N, int T, int HV) {
-    return ((size_t)(T / chunk::C) + (size_t)N) * (size_t)HV * chunk::kSlotBytes;
+size_t prefill_workspace_bytes(int N, int T, int H, int HV) {
+    return (size_t)chunk::ws_slots(N, T) * ((size_t)HV * chunk::kSlotBytes + (size_t)H * chunk::kTileKQ);
 }
 
 void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st) {
@@ -674,7 +694,7 @@ void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t 
         attr_set = true;
     }
     unsigned char* ws = static_cast<unsigned char*>(workspace);
-    const long long slots = (long long)(p.T / chunk::C) + p.N;
+    const long long slots = chunk::ws_slots(p.N, p.T);
     chunk::prep::gdn_prefill_chunk_prep_kernel<<<(unsigned)(slots * p.HV), chunk::prep::NT,
                                                  chunk::prep::SMEM_BYTES, st>>>(p, ws);
     const long long blocks = (long long)p.N * p.HV * (kDim / chunk::chain::VT);

@@ -52,6 +52,6 @@ __device__ __forceinline__ void zero_uncovered_outputs(const PrefillParams& p, i
 
 void launch_prefill_recurrent(const PrefillParams& p, cudaStream_t st);
 void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st);
-size_t prefill_workspace_bytes(int N, int T, int HV);
+size_t prefill_workspace_bytes(int N, int T, int H, int HV);
 
 }  // namespace gdn

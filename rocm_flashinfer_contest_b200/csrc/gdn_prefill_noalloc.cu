@@ -51,7 +51,7 @@ extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void*
                                        int N, int T, float scale, int H, int HV, int K, int V, void* out,
                                        float* new_state, void* stream) {
     // the size check comes first and makes no CUDA call
-    if (N >= 0 && T >= 0 && HV > 0 && gdn_prefill_workspace_bytes(N, T, HV) > kScratchBytes)
+    if (N >= 0 && T >= 0 && H > 0 && HV > 0 && gdn_prefill_workspace_bytes(N, T, H, HV) > kScratchBytes)
         return GDN_ERR_TOO_LARGE;
     void* scratch = nullptr;
     const int st = scratch_on_current_device(&scratch);

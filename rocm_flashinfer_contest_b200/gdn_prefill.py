@@ -76,7 +76,7 @@ def run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, ne
             or not new_state.is_contiguous() or new_state.device != dev:
         raise ValueError("new_state must be a contiguous fp32 [N, HV, V, K] tensor on the inputs' device")
     scale = C.normalize_scale(scale, K)
-    ws_bytes = lib().gdn_prefill_workspace_bytes(N, T, HV)
+    ws_bytes = lib().gdn_prefill_workspace_bytes(N, T, H, HV)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
     st = lib().gdn_prefill_fwd(
         C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(state), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias),

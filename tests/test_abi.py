@@ -102,13 +102,14 @@ def test_prefill_rejects_bad_arguments(over, code):
 
 def test_prefill_workspace_size(monkeypatch):
     ws = _lib.lib().gdn_prefill_workspace_bytes
+    per_slot = lambda H, HV: HV * 16896 + H * 32768  # noqa: E731
     monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "128")
-    assert ws(1, 8192, 32) == (8192 // 64 + 1) * 32 * 16896
-    assert ws(16, 5000, 8) == (5000 // 64 + 16) * 8 * 16896
-    assert ws(3, 100, 8) == 0          # below the threshold: token-serial kernel, no workspace
-    assert ws(0, 0, 8) == 0
+    assert ws(1, 8192, 16, 32) == (8192 // 64 + 1) * per_slot(16, 32)
+    assert ws(16, 5000, 4, 8) == (5000 // 64 + 16) * per_slot(4, 8)
+    assert ws(3, 100, 4, 8) == 0          # below the threshold: token-serial kernel, no workspace
+    assert ws(0, 0, 4, 8) == 0
     monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "0")
-    assert ws(3, 100, 8) == (100 // 64 + 3) * 8 * 16896
+    assert ws(3, 100, 4, 8) == (100 // 64 + 3) * per_slot(4, 8)
 
 
 def test_error_is_raised_as_exception():
