@@ -365,10 +365,10 @@ def bench_ours(args, rank, world, local):
 # ---------------------------------------------------------------------------
 # CPU: the reference algorithm on the host cores (C oracle port)
 
-def _cpu_decode_rate(seconds, steps=None, warmup=0):
+def _cpu_decode_rate(seconds, steps=None, warmup=0, B=DECODE_B):
     from oracle import oracle
     from rocm_flashinfer_contest_b200 import inputs
-    args = inputs.decode_inputs(DECODE_B, H, HV, seed=1000)
+    args = inputs.decode_inputs(B, H, HV, seed=1000)
     cores = os.cpu_count() or 1
     for _ in range(warmup):
         oracle.decode(*args, threads=cores)
@@ -415,9 +415,10 @@ def cpu_prefill_baseline(tokens=512):
 def bench_reference(args, rank, world):
     if rank != 0:
         return None
-    times, cores = _cpu_decode_rate(0.0, steps=args.steps, warmup=args.warmup)
+    B = DECODE_B * world  # the same whole-job batch as our arm at this world size
+    times, cores = _cpu_decode_rate(0.0, steps=args.steps, warmup=args.warmup, B=B)
     t = statistics.mean(times)
-    value = decode_state_bytes(DECODE_B) / t / 1e9
+    value = decode_state_bytes(B) / t / 1e9
     return {
         "impl": "reference",
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
@@ -425,19 +426,31 @@ def bench_reference(args, rank, world):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f32 state / bf16 io",
         "data": "synthetic (seeded; contest dataset not available offline)",
-        "config": {"workload": "gdn_decode B=64, in-place state (BASELINE configs[1])",
-                   "B_per_gpu": DECODE_B, "H": H, "HV": HV, "head_size": D},
+        "config": {"workload": "gdn_decode B=64 per GPU, in-place state (BASELINE configs[1])",
+                   "B_per_gpu": DECODE_B, "B_total": B, "H": H, "HV": HV, "head_size": D},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{len(times)} full gdn_decode B=64 steps, C oracle port of the "
+                         "sample": f"{len(times)} full gdn_decode B={B} steps, C oracle port of the "
                                    f"contest reference, {cores} OpenMP threads"},
         "note": "the reference's own GDN solutions are Triton/AITER kernels for MI300X (ROCm); "
                 "its algorithm is timed on the host cores through the C oracle port",
     }
 
 
+def _json_channel():
+    """The JSON line is the only thing this program writes to stdout: a
+    duplicate of the original stdout carries it, and file descriptor 1 is
+    pointed at stderr so that library banners (NCCL prints its version at
+    communicator creation) cannot reach stdout."""
+    sys.stdout.flush()
+    out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    return out
+
+
 def main():
+    json_out = _json_channel()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -454,7 +467,7 @@ def main():
         world = int(os.environ.get("WORLD_SIZE", "1"))
         line = bench_reference(args, rank, world)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line), file=json_out, flush=True)
         return
     rank, world, local = dist_setup()
     if world != args.gpus and world > 1:
@@ -462,7 +475,7 @@ def main():
     try:
         line = bench_ours(args, rank, world, local)
         if rank == 0 and line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line), file=json_out, flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist
