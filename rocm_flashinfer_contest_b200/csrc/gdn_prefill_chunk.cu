@@ -160,13 +160,15 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
     // off-diagonal blocks, level d = i - j: X_ij = sum_k A_ik T_kj, then
     // T_ij = -T_ii X_ij.  Thread -> (rows r0, r0 + 1; column c) of a block.
     const int c = tid & 15, r0 = (tid >> 4) * 2;
-#pragma unroll
+    // outer loops stay rolled: the kernel is large and instruction fetch,
+    // not arithmetic, limits it
+#pragma unroll 1
     for (int d = 1; d < 4; ++d) {
-#pragma unroll
+#pragma unroll 1
         for (int j = 0; j + d < 4; ++j) {
             const int i = j + d;
             float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll
+#pragma unroll 1
             for (int k = j; k < i; ++k) {
                 const float* a0 = sA + (16 * i + r0) * LDA + 16 * k;
                 const float* tk = sT + (16 * k) * LDA + 16 * j + c;
@@ -184,7 +186,7 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
             sX[(16 * i + r0 - 15) * LDA + 16 * j + c] = acc1;
         }
         __syncthreads();
-#pragma unroll
+#pragma unroll 1
         for (int j = 0; j + d < 4; ++j) {
             const int i = j + d;
             const float* t0r = sT + (16 * i + r0) * LDA + 16 * i;
@@ -318,7 +320,7 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
         const int i = tid & 63;
         const float gi = sG[i];
         const float bi = sBeta[i];
-#pragma unroll
+#pragma unroll 1
         for (int c16 = 0; c16 < C; c16 += 16) {
             float d[16];
             umma::tmem_ld16(tmem + lane_base + c16, d);
@@ -416,16 +418,16 @@ constexpr int VT = 64;   // state columns (v) per CTA
 constexpr int HALF = VT / 2;
 constexpr uint32_t VROW = VT * 2 + 16;  // raw v row stride: padded so rows start in different banks
 
-// Data of chunk j lives in buffer j % 2: chunk j + 2's copies start once
-// chunk j has finished with the buffer, a whole chunk before they are needed.
-constexpr int NBUF = 2;
-constexpr uint32_t OFF_KQ = 0;                         // [K ; Q] f16 (workspace copy), 2 bufs   64 KiB
-constexpr uint32_t OFF_TP = OFF_KQ + NBUF * kTileKQ;   // [T ; P'] f16 (workspace copy), 2 bufs  32 KiB
+// Data of chunk j lives in buffer j % 3.  Chunk j + 2's copies are issued
+// while chunk j waits for its first MMA, into the buffer chunk j - 1 used.
+constexpr int NBUF = 3;
+constexpr uint32_t OFF_KQ = 0;                         // [K ; Q] f16 (workspace copy), 3 bufs   96 KiB
+constexpr uint32_t OFF_TP = OFF_KQ + NBUF * kTileKQ;   // [T ; P'] f16 (workspace copy), 3 bufs  48 KiB
 constexpr uint32_t OFF_SH = OFF_TP + NBUF * kTileTP;   // S f16 MN-major (v x k, kext 128)       16 KiB
 constexpr uint32_t OFF_Y = OFF_SH + 16384;             // Y MN-major (v x 64 tokens)              8 KiB
 constexpr uint32_t OFF_DL = OFF_Y + 8192;              // Delta~ MN-major (v x 64 tokens)         8 KiB
-constexpr uint32_t OFF_RV = OFF_DL + 8192;             // v rows bf16 [2][64][VROW]              18 KiB
-constexpr uint32_t OFF_GB = OFF_RV + NBUF * C * VROW;  // gamma / beta fp32, 2 bufs               1 KiB
+constexpr uint32_t OFF_RV = OFF_DL + 8192;             // v rows bf16 [3][64][VROW]              27 KiB
+constexpr uint32_t OFF_GB = OFF_RV + NBUF * C * VROW;  // gamma / beta fp32, 3 bufs             1.5 KiB
 constexpr uint32_t SMEM_BYTES = OFF_GB + NBUF * 512 + 1024;
 static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
 
@@ -473,7 +475,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint64_t mbar[3];   // MMA_1, MMA_2, MMA_3 completion
-    __shared__ uint64_t ldbar[NBUF];  // chunk data of buffer 0 / 1 landed
+    __shared__ uint64_t ldbar[NBUF];  // chunk data of buffer 0 / 1 / 2 landed
     __shared__ uint32_t tmem_base_sh;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -539,8 +541,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
     constexpr uint32_t ID_D = umma::idesc_f16(128, VT, 0, 0, 1, 1);  // K^T x Delta~ (both MN-major)
 
     for (long long j = 0; j < nchunks; ++j) {
-        const int b = (int)(j & 1);
-        const uint32_t par = (uint32_t)(j & 1), lpar = (uint32_t)((j >> 1) & 1);
+        const int b = (int)(j % NBUF);
+        const uint32_t par = (uint32_t)(j & 1), lpar = (uint32_t)((j / NBUF) & 1);
         const long long tc = t0 + C * j;
         const int len = chunk_len(j);
         // this chunk's v rows (chunk j + 1's commit group may still be in flight)
@@ -560,6 +562,10 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
                               k0 > 0);
             umma::mma_commit(&mbar[0]);
         }
+        // while MMA_1 runs: stream in chunk j + 2 (its buffer was chunk j - 1's)
+        if (j + 2 < nchunks)
+            issue_loads(p, ws, sm, &ldbar[(j + 2) % NBUF], (int)((j + 2) % NBUF), tc + 2 * C, chunk_len(j + 2),
+                        slot0 + j + 2, hq, hv, v0, tid, warp == kLoader);
         if (!wait_mma(&mbar[0], par)) goto done;
         umma::fence_after_sync();
 
@@ -656,10 +662,6 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
             for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c8, row, kDim), sv + c8);
         }
         sync_for_mma();
-        // buffer b is free again: stream in chunk j + 2
-        if (j + 2 < nchunks)
-            issue_loads(p, ws, sm, &ldbar[b], b, tc + 2 * C, chunk_len(j + 2), slot0 + j + 2, hq, hv, v0, tid,
-                        warp == kLoader);
     }
 
     // final state (fp32, k-last): for each v, consecutive threads write consecutive k
