@@ -29,8 +29,8 @@
 //      the state-independent part — gates, gamma, MMA [K ; Q] K^T (bf16 as
 //      given), the decay masks, T = (I + A)^-1 by a blocked solve on the CUDA
 //      cores in fp32, and P' = P T on the tensor cores — and writes the f16
-//      operand tile [T ; P'] (already in its shared-memory swizzled layout),
-//      gamma and beta into a workspace slot.
+//      operand tile [T ; P'] (already in its shared-memory swizzled layout)
+//      and the chunk's gate factors into a workspace slot.
 //  * chain (one CTA per (sequence, v-head, 64-wide V tile), 8 warps): walks
 //      the chunks in order with the state resident in TMEM (fp32):
 //        MMA_1 : [K ; Q] x S     -> KS (rows 0-63: Y = beta (V - e^gamma KS)), QS (rows 64-127)
@@ -60,7 +60,11 @@ namespace chunk {
 constexpr int C = 64;                    // tokens per chunk
 constexpr int LDA = 68;                  // fp32 row stride of the solve matrices
 constexpr uint32_t kTileTP = 16384;      // [T ; P'] f16, K-major 128 x 64
-constexpr uint32_t kSlotBytes = kTileTP + 2 * 256;  // + gamma[64], beta[64] (fp32)
+// Gate record of a chunk (fp32): beta e^gamma, beta, e^{gamma_C - gamma},
+// scale e^gamma (64 each), then e^{gamma_C}.
+constexpr uint32_t kGateBytes = 4 * 256 + 16;
+constexpr int GR_BEG = 0, GR_BETA = 64, GR_FK = 128, GR_FQ = 192, GR_DECAY = 256;
+constexpr uint32_t kSlotBytes = kTileTP + kGateBytes;
 constexpr uint32_t kTileKQ = 32768;      // [K ; Q] f16, K-major 128 x 128
 
 // Workspace: (floor(T/64) + N) chunk slots; per slot HV (chunk, v-head)
@@ -106,6 +110,13 @@ __device__ __forceinline__ bool wait_mma(uint64_t* bar, uint32_t parity) {
     // every thread waits; the CTA agrees on the outcome
     const bool ok = umma::mbar_wait(bar, parity, kWaitBudget);
     return !__syncthreads_or(!ok);
+}
+
+// Every thread waits on its own (the mbarrier orders the MMA's results for
+// each waiter); a timeout is remembered in `failed` and acted on at the next
+// CTA-wide vote.
+__device__ __forceinline__ void wait_local(uint64_t* bar, uint32_t parity, bool& failed) {
+    if (!umma::mbar_wait(bar, parity, kWaitBudget)) failed = true;
 }
 
 __device__ __forceinline__ void sync_for_mma() {
@@ -394,10 +405,15 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
             const int idx = tid + it * NT;
             reinterpret_cast<uint4*>(slot)[idx] = reinterpret_cast<const uint4*>(sm + OFF_TP)[idx];
         }
-        if (tid < 64) {
-            reinterpret_cast<float*>(slot + kTileTP)[tid] = sG[tid];
-            reinterpret_cast<float*>(slot + kTileTP + 256)[tid] = sBeta[tid];
+        float* gr = reinterpret_cast<float*>(slot + kTileTP);
+        if (tid < 64) {  // gamma <= 0: every factor is in (0, 1] (times scale)
+            const float eg = expf(sG[tid]);
+            gr[GR_BEG + tid] = sBeta[tid] * eg;
+            gr[GR_BETA + tid] = sBeta[tid];
+            gr[GR_FK + tid] = expf(fminf(sG[C - 1] - sG[tid], 0.f));
+            gr[GR_FQ + tid] = p.scale * eg;
         }
+        if (tid < 4) gr[GR_DECAY + tid] = expf(sG[C - 1]);
     }
 
 done:
@@ -427,8 +443,8 @@ constexpr uint32_t OFF_SH = OFF_TP + NBUF * kTileTP;   // S f16 MN-major (v x k,
 constexpr uint32_t OFF_Y = OFF_SH + 16384;             // Y MN-major (v x 64 tokens)              8 KiB
 constexpr uint32_t OFF_DL = OFF_Y + 8192;              // Delta~ MN-major (v x 64 tokens)         8 KiB
 constexpr uint32_t OFF_RV = OFF_DL + 8192;             // v rows bf16 [3][64][VROW]              27 KiB
-constexpr uint32_t OFF_GB = OFF_RV + NBUF * C * VROW;  // gamma / beta fp32, 3 bufs             1.5 KiB
-constexpr uint32_t SMEM_BYTES = OFF_GB + NBUF * 512 + 1024;
+constexpr uint32_t OFF_GB = OFF_RV + NBUF * C * VROW;  // gate records, 3 bufs                  3 KiB
+constexpr uint32_t SMEM_BYTES = OFF_GB + NBUF * kGateBytes + 1024;
 static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
 
 constexpr uint32_t TM_1 = 0, TM_2 = 64, TM_3 = 128, TM_S = 192, TM_COLS = 256;
@@ -447,7 +463,7 @@ __device__ __forceinline__ void issue_loads(const PrefillParams& p, const unsign
                                             int hq, int hv, int v0, int tid, bool loader) {
     if (loader) {
         const int lane = tid & 31;
-        if (lane == 0) umma::mbar_arrive_expect_tx(bar, kTileKQ + kTileTP + 512);
+        if (lane == 0) umma::mbar_arrive_expect_tx(bar, kTileKQ + kTileTP + kGateBytes);
         __syncwarp();
         const unsigned char* rec = ws + ((size_t)slot * p.HV + hv) * kSlotBytes;
         const unsigned char* kq = ws_kq(p, ws) + ((size_t)slot * p.H + hq) * kTileKQ;
@@ -456,7 +472,7 @@ __device__ __forceinline__ void issue_loads(const PrefillParams& p, const unsign
             umma::bulk_g2s(umma::smem_u32(sm + OFF_KQ + buf * kTileKQ + kTileKQ / 2), kq + kTileKQ / 2,
                            kTileKQ / 2, bar);
         if (lane == 2) umma::bulk_g2s(umma::smem_u32(sm + OFF_TP + buf * kTileTP), rec, kTileTP, bar);
-        if (lane == 3) umma::bulk_g2s(umma::smem_u32(sm + OFF_GB + buf * 512), rec + kTileTP, 512, bar);
+        if (lane == 3) umma::bulk_g2s(umma::smem_u32(sm + OFF_GB + buf * kGateBytes), rec + kTileTP, kGateBytes, bar);
     }
     const uint32_t rv = umma::smem_u32(sm + OFF_RV) + buf * (C * VROW);
 #pragma unroll
@@ -531,7 +547,10 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
 #pragma unroll
         for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c8, row, kDim), sv + c8);
     }
+    // chunk 0's v rows (copied by all threads) become visible at the barrier
+    if (nchunks > 1) cp_async_wait_n<1>(); else cp_async_wait_n<0>();
     sync_for_mma();
+    bool failed = false;
 
     const uint32_t sKQ0 = umma::smem_u32(sm + OFF_KQ), sTP0 = umma::smem_u32(sm + OFF_TP);
     const uint32_t sSH = umma::smem_u32(sm + OFF_SH), sY = umma::smem_u32(sm + OFF_Y);
@@ -545,12 +564,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
         const uint32_t par = (uint32_t)(j & 1), lpar = (uint32_t)((j / NBUF) & 1);
         const long long tc = t0 + C * j;
         const int len = chunk_len(j);
-        // this chunk's v rows (chunk j + 1's commit group may still be in flight)
-        if (j + 1 < nchunks) cp_async_wait_n<1>(); else cp_async_wait_n<0>();
-        if (!wait_mma(&ldbar[b], lpar)) goto done;
-        const float* sG = reinterpret_cast<const float*>(sm + OFF_GB + b * 512);
-        const float* sBeta = sG + 64;
-        const float gC = sG[C - 1];
+        wait_local(&ldbar[b], lpar, failed);
+        const float* gr = reinterpret_cast<const float*>(sm + OFF_GB + b * kGateBytes);
         const uint32_t sKQ = sKQ0 + b * kTileKQ;
 
         // ---- MMA_1: [K ; Q] S ----
@@ -566,7 +581,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
         if (j + 2 < nchunks)
             issue_loads(p, ws, sm, &ldbar[(j + 2) % NBUF], (int)((j + 2) % NBUF), tc + 2 * C, chunk_len(j + 2),
                         slot0 + j + 2, hq, hv, v0, tid, warp == kLoader);
-        if (!wait_mma(&mbar[0], par)) goto done;
+        wait_local(&mbar[0], par, failed);
         umma::fence_after_sync();
 
         // ---- lower: Y = beta (V - e^gamma KS) -> MMA_2;  upper: keep QS ----
@@ -577,14 +592,14 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
             if (lower) {
                 const int i = row;
                 const bool live = i < len;
-                const float eg = __expf(fminf(sG[i], 0.f)), b_i = sBeta[i];
+                const float beg = gr[GR_BEG + i], b_i = gr[GR_BETA + i];
                 const unsigned char* vrow = sm + OFF_RV + b * (C * VROW) + i * VROW + cb * 2;
 #pragma unroll
                 for (int c8 = 0; c8 < HALF; c8 += 8) {
                     float vv[8], y[8];
                     unpack_bf16x8(*reinterpret_cast<const uint4*>(vrow + c8 * 2), vv);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) y[e] = live ? b_i * (vv[e] - eg * d[c8 + e]) : 0.f;
+                    for (int e = 0; e < 8; ++e) y[e] = live ? fmaf(-beg, d[c8 + e], b_i * vv[e]) : 0.f;
                     st_f16x8(sm + OFF_Y, umma::mnmaj_off(cb + c8, i, C), y);
                 }
                 umma::fence_proxy_async_smem();
@@ -604,7 +619,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
                 for (int e = 0; e < HALF; ++e) qs[e] = d[e];
             }
         }
-        if (!wait_mma(&mbar[1], par)) goto done;
+        wait_local(&mbar[1], par, failed);
         umma::fence_after_sync();
 
         // ---- lower: Delta~ = e^{gamma_C - gamma} Delta -> MMA_3;  upper: outputs ----
@@ -612,7 +627,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
             float d[HALF];
             umma::tmem_ld32(tl + TM_2 + cb, d);
             if (lower) {
-                const float fk = __expf(fminf(gC - sG[row], 0.f));
+                const float fk = gr[GR_FK + row];
 #pragma unroll
                 for (int e = 0; e < HALF; ++e) d[e] *= fk;
 #pragma unroll
@@ -633,7 +648,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
             } else {
                 const int i = row - 64;
                 if (i < len) {
-                    const float fq = p.scale * __expf(fminf(sG[i], 0.f));  // scale e^{gamma_i}
+                    const float fq = gr[GR_FQ + i];  // scale e^{gamma_i}
                     __nv_bfloat16* op = p.out + ((size_t)(tc + i) * p.HV + hv) * kDim + v0 + cb;
 #pragma unroll
                     for (int c8 = 0; c8 < HALF; c8 += 8) {
@@ -647,12 +662,12 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
                 }
             }
         }
-        if (!wait_mma(&mbar[2], par)) goto done;
+        wait_local(&mbar[2], par, failed);
         umma::fence_after_sync();
 
         // ---- S = e^{gamma_C} S + K^T Delta~ (TMEM, fp32) and its f16 operand copy ----
         {
-            const float decay = __expf(fminf(gC, 0.f));
+            const float decay = gr[GR_DECAY];
             float sv[HALF], d[HALF];
             umma::tmem_ld32x2(tl + TM_S + cb, tl + TM_3 + cb, sv, d);
 #pragma unroll
@@ -661,7 +676,13 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
 #pragma unroll
             for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c8, row, kDim), sv + c8);
         }
-        sync_for_mma();
+        // the next chunk's v rows (copied by all threads) become visible at this barrier;
+        // the CTA stops here if any wait of this chunk timed out
+        if (j + 2 < nchunks) cp_async_wait_n<1>(); else cp_async_wait_n<0>();
+        umma::fence_proxy_async_smem();
+        umma::fence_before_sync();
+        if (__syncthreads_or(failed)) goto done;
+        umma::fence_after_sync();
     }
 
     // final state (fp32, k-last): for each v, consecutive threads write consecutive k
