@@ -430,25 +430,52 @@ done:
 namespace chain {
 
 constexpr int NT = 256;  // 8 warps: TMEM lane quarter = warp % 4, column half = warp / 4
-constexpr int VT = 64;   // state columns (v) per CTA
-constexpr int HALF = VT / 2;
-constexpr uint32_t VROW = VT * 2 + 16;  // raw v row stride: padded so rows start in different banks
-
-// Data of chunk j lives in buffer j % 3.  Chunk j + 2's copies are issued
-// while chunk j waits for its first MMA, into the buffer chunk j - 1 used.
-constexpr int NBUF = 3;
-constexpr uint32_t OFF_KQ = 0;                         // [K ; Q] f16 (workspace copy), 3 bufs   96 KiB
-constexpr uint32_t OFF_TP = OFF_KQ + NBUF * kTileKQ;   // [T ; P'] f16 (workspace copy), 3 bufs  48 KiB
-constexpr uint32_t OFF_SH = OFF_TP + NBUF * kTileTP;   // S f16 MN-major (v x k, kext 128)       16 KiB
-constexpr uint32_t OFF_Y = OFF_SH + 16384;             // Y MN-major (v x 64 tokens)              8 KiB
-constexpr uint32_t OFF_DL = OFF_Y + 8192;              // Delta~ MN-major (v x 64 tokens)         8 KiB
-constexpr uint32_t OFF_RV = OFF_DL + 8192;             // v rows bf16 [3][64][VROW]              27 KiB
-constexpr uint32_t OFF_GB = OFF_RV + NBUF * C * VROW;  // gate records, 3 bufs                  3 KiB
-constexpr uint32_t SMEM_BYTES = OFF_GB + NBUF * kGateBytes + 1024;
-static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
-
+constexpr int NBUF = 3;  // data of chunk j lives in buffer j % 3
 constexpr uint32_t TM_1 = 0, TM_2 = 64, TM_3 = 128, TM_S = 192, TM_COLS = 256;
 constexpr int kLowerBarrier = 1;  // named barrier of the four warps on TMEM lanes 0-63
+
+// VT state columns (v) per CTA: 64, or 32 when a 64-wide split would leave
+// SMs idle (few sequences x v-heads).  The B operands S, Y and Delta~ have
+// N = VT and are MN-major: 128-byte swizzle for 64 columns, 64-byte for 32.
+template <int VT>
+struct Cfg {
+    static constexpr int HALF = VT / 2;                     // columns per thread
+    static constexpr uint32_t VROW = VT * 2 + 16;           // raw v row stride (padded)
+    static constexpr uint32_t S_BYTES = VT * kDim * 2;      // S f16 tile
+    static constexpr uint32_t YD_BYTES = VT * C * 2;        // Y / Delta~ f16 tiles
+    static constexpr uint32_t OFF_KQ = 0;                         // [K ; Q] (workspace copy), 3 bufs
+    static constexpr uint32_t OFF_TP = OFF_KQ + NBUF * kTileKQ;   // [T ; P'] (workspace copy), 3 bufs
+    static constexpr uint32_t OFF_SH = OFF_TP + NBUF * kTileTP;   // S, MN-major (v x k)
+    static constexpr uint32_t OFF_Y = OFF_SH + S_BYTES;           // Y, MN-major (v x token)
+    static constexpr uint32_t OFF_DL = OFF_Y + YD_BYTES;          // Delta~, MN-major (v x token)
+    static constexpr uint32_t OFF_RV = OFF_DL + YD_BYTES;         // v rows bf16 [3][64][VROW]
+    static constexpr uint32_t OFF_GB = OFF_RV + NBUF * C * VROW;  // gate records, 3 bufs
+    static constexpr uint32_t SMEM_BYTES = OFF_GB + NBUF * kGateBytes + 1024;
+    static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
+    static_assert(OFF_Y % 1024 == 0 && OFF_DL % 1024 == 0 && OFF_RV % 16 == 0, "tile alignment");
+
+    // byte offset of element (v, k) of an MN-major B tile whose K extent is kext
+    static __device__ __forceinline__ uint32_t b_off(uint32_t v, uint32_t k, uint32_t kext) {
+        if constexpr (VT == 32) return umma::mnmaj64_off(v, k);
+        else return umma::mnmaj_off(v, k, kext);
+    }
+    static __device__ __forceinline__ uint64_t b_desc(uint32_t tile, uint32_t kext, uint32_t k0) {
+        if constexpr (VT == 32) return umma::desc_mnmaj64(tile, k0);
+        else return umma::desc_mnmaj(tile, kext, k0);
+    }
+    static __device__ __forceinline__ void ld(uint32_t taddr, float (&v)[HALF]) {
+        if constexpr (HALF == 16) umma::tmem_ld16(taddr, v);
+        else umma::tmem_ld32(taddr, v);
+    }
+    static __device__ __forceinline__ void ld2(uint32_t ta, uint32_t tb, float (&va)[HALF], float (&vb)[HALF]) {
+        if constexpr (HALF == 16) umma::tmem_ld16x2(ta, tb, va, vb);
+        else umma::tmem_ld32x2(ta, tb, va, vb);
+    }
+    static __device__ __forceinline__ void st(uint32_t taddr, const float (&v)[HALF]) {
+        if constexpr (HALF == 16) umma::tmem_st16(taddr, v);
+        else umma::tmem_st32(taddr, v);
+    }
+};
 
 __device__ __forceinline__ void lower_sync() {
     asm volatile("bar.sync %0, %1;" ::"r"(kLowerBarrier), "r"(128) : "memory");
@@ -458,23 +485,27 @@ __device__ __forceinline__ void lower_sync() {
 // the loader warp starts three bulk copies of the [K ; Q] and [T ; P'] tiles
 // and the gates, completing on `bar`; every thread copies its share of the v
 // rows with cp.async (rows past len zero-filled) as one commit group.
+template <int VT>
 __device__ __forceinline__ void issue_loads(const PrefillParams& p, const unsigned char* ws, unsigned char* sm,
                                             uint64_t* bar, int buf, long long tc, int len, long long slot,
                                             int hq, int hv, int v0, int tid, bool loader) {
     if (loader) {
         const int lane = tid & 31;
+        using G = Cfg<VT>;
         if (lane == 0) umma::mbar_arrive_expect_tx(bar, kTileKQ + kTileTP + kGateBytes);
         __syncwarp();
         const unsigned char* rec = ws + ((size_t)slot * p.HV + hv) * kSlotBytes;
         const unsigned char* kq = ws_kq(p, ws) + ((size_t)slot * p.H + hq) * kTileKQ;
-        if (lane == 0) umma::bulk_g2s(umma::smem_u32(sm + OFF_KQ + buf * kTileKQ), kq, kTileKQ / 2, bar);
+        if (lane == 0) umma::bulk_g2s(umma::smem_u32(sm + G::OFF_KQ + buf * kTileKQ), kq, kTileKQ / 2, bar);
         if (lane == 1)
-            umma::bulk_g2s(umma::smem_u32(sm + OFF_KQ + buf * kTileKQ + kTileKQ / 2), kq + kTileKQ / 2,
+            umma::bulk_g2s(umma::smem_u32(sm + G::OFF_KQ + buf * kTileKQ + kTileKQ / 2), kq + kTileKQ / 2,
                            kTileKQ / 2, bar);
-        if (lane == 2) umma::bulk_g2s(umma::smem_u32(sm + OFF_TP + buf * kTileTP), rec, kTileTP, bar);
-        if (lane == 3) umma::bulk_g2s(umma::smem_u32(sm + OFF_GB + buf * kGateBytes), rec + kTileTP, kGateBytes, bar);
+        if (lane == 2) umma::bulk_g2s(umma::smem_u32(sm + G::OFF_TP + buf * kTileTP), rec, kTileTP, bar);
+        if (lane == 3)
+            umma::bulk_g2s(umma::smem_u32(sm + G::OFF_GB + buf * kGateBytes), rec + kTileTP, kGateBytes, bar);
     }
-    const uint32_t rv = umma::smem_u32(sm + OFF_RV) + buf * (C * VROW);
+    constexpr uint32_t VROW = Cfg<VT>::VROW;
+    const uint32_t rv = umma::smem_u32(sm + Cfg<VT>::OFF_RV) + buf * (C * VROW);
 #pragma unroll
     for (int it = 0; it < C * (VT / 8) / NT; ++it) {
         const int idx = tid + it * NT, r = idx / (VT / 8), c = idx % (VT / 8);
@@ -485,8 +516,14 @@ __device__ __forceinline__ void issue_loads(const PrefillParams& p, const unsign
     cp_async_commit();
 }
 
+template <int VT>
 __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const PrefillParams p,
                                                                         const unsigned char* ws) {
+    using G = Cfg<VT>;
+    constexpr int HALF = G::HALF;
+    constexpr uint32_t VROW = G::VROW;
+    constexpr uint32_t OFF_KQ = G::OFF_KQ, OFF_TP = G::OFF_TP, OFF_SH = G::OFF_SH, OFF_Y = G::OFF_Y;
+    constexpr uint32_t OFF_DL = G::OFF_DL, OFF_RV = G::OFF_RV, OFF_GB = G::OFF_GB;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -531,9 +568,9 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
         umma::fence_mbar_init();
     }
     __syncthreads();
-    issue_loads(p, ws, sm, &ldbar[0], 0, t0, chunk_len(0), slot0, hq, hv, v0, tid, warp == kLoader);
+    issue_loads<VT>(p, ws, sm, &ldbar[0], 0, t0, chunk_len(0), slot0, hq, hv, v0, tid, warp == kLoader);
     if (nchunks > 1)
-        issue_loads(p, ws, sm, &ldbar[1], 1, t0 + C, chunk_len(1), slot0 + 1, hq, hv, v0, tid, warp == kLoader);
+        issue_loads<VT>(p, ws, sm, &ldbar[1], 1, t0 + C, chunk_len(1), slot0 + 1, hq, hv, v0, tid, warp == kLoader);
     umma::fence_after_sync();
     const uint32_t tmem = tmem_base_sh;
     const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);  // this warp's lane quarter
@@ -543,9 +580,9 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
         float sv[HALF];
 #pragma unroll
         for (int e = 0; e < HALF; ++e) sv[e] = p.state ? p.state[state_off + (size_t)(cb + e) * kDim + row] : 0.f;
-        umma::tmem_st32(tl + TM_S + cb, sv);
+        G::st(tl + TM_S + cb, sv);
 #pragma unroll
-        for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c8, row, kDim), sv + c8);
+        for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, G::b_off(cb + c8, row, kDim), sv + c8);
     }
     // chunk 0's v rows (copied by all threads) become visible at the barrier
     if (nchunks > 1) cp_async_wait_n<1>(); else cp_async_wait_n<0>();
@@ -573,13 +610,13 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
             umma::fence_after_sync();
 #pragma unroll
             for (int k0 = 0; k0 < kDim; k0 += 16)
-                umma::mma_f16(tmem + TM_1, umma::desc_kmaj(sKQ, 128, k0), umma::desc_mnmaj(sSH, kDim, k0), ID_S,
+                umma::mma_f16(tmem + TM_1, umma::desc_kmaj(sKQ, 128, k0), G::b_desc(sSH, kDim, k0), ID_S,
                               k0 > 0);
             umma::mma_commit(&mbar[0]);
         }
         // while MMA_1 runs: stream in chunk j + 2 (its buffer was chunk j - 1's)
         if (j + 2 < nchunks)
-            issue_loads(p, ws, sm, &ldbar[(j + 2) % NBUF], (int)((j + 2) % NBUF), tc + 2 * C, chunk_len(j + 2),
+            issue_loads<VT>(p, ws, sm, &ldbar[(j + 2) % NBUF], (int)((j + 2) % NBUF), tc + 2 * C, chunk_len(j + 2),
                         slot0 + j + 2, hq, hv, v0, tid, warp == kLoader);
         wait_local(&mbar[0], par, failed);
         umma::fence_after_sync();
@@ -588,7 +625,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
         float qs[HALF];
         {
             float d[HALF];
-            umma::tmem_ld32(tl + TM_1 + cb, d);
+            G::ld(tl + TM_1 + cb, d);
             if (lower) {
                 const int i = row;
                 const bool live = i < len;
@@ -600,7 +637,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
                     unpack_bf16x8(*reinterpret_cast<const uint4*>(vrow + c8 * 2), vv);
 #pragma unroll
                     for (int e = 0; e < 8; ++e) y[e] = live ? fmaf(-beg, d[c8 + e], b_i * vv[e]) : 0.f;
-                    st_f16x8(sm + OFF_Y, umma::mnmaj_off(cb + c8, i, C), y);
+                    st_f16x8(sm + OFF_Y, G::b_off(cb + c8, i, C), y);
                 }
                 umma::fence_proxy_async_smem();
                 umma::fence_before_sync();
@@ -610,7 +647,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
                     const uint32_t sTP = sTP0 + b * kTileTP;
 #pragma unroll
                     for (int k0 = 0; k0 < C; k0 += 16)
-                        umma::mma_f16(tmem + TM_2, umma::desc_kmaj(sTP, 128, k0), umma::desc_mnmaj(sY, C, k0), ID_Y,
+                        umma::mma_f16(tmem + TM_2, umma::desc_kmaj(sTP, 128, k0), G::b_desc(sY, C, k0), ID_Y,
                                       k0 > 0);
                     umma::mma_commit(&mbar[1]);
                 }
@@ -625,13 +662,13 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
         // ---- lower: Delta~ = e^{gamma_C - gamma} Delta -> MMA_3;  upper: outputs ----
         {
             float d[HALF];
-            umma::tmem_ld32(tl + TM_2 + cb, d);
+            G::ld(tl + TM_2 + cb, d);
             if (lower) {
                 const float fk = gr[GR_FK + row];
 #pragma unroll
                 for (int e = 0; e < HALF; ++e) d[e] *= fk;
 #pragma unroll
-                for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_DL, umma::mnmaj_off(cb + c8, row, C), d + c8);
+                for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_DL, G::b_off(cb + c8, row, C), d + c8);
                 umma::fence_proxy_async_smem();
                 umma::fence_before_sync();
                 lower_sync();
@@ -642,7 +679,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
 #pragma unroll
                     for (int k0 = 0; k0 < C; k0 += 16)
                         umma::mma_f16(tmem + TM_3, umma::desc_sw128(sKQ + (k0 >> 3) * 1024u, 16384u, 1024u),
-                                      umma::desc_mnmaj(sDL, C, k0), ID_D, k0 > 0);
+                                      G::b_desc(sDL, C, k0), ID_D, k0 > 0);
                     umma::mma_commit(&mbar[2]);
                 }
             } else {
@@ -669,12 +706,12 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
         {
             const float decay = gr[GR_DECAY];
             float sv[HALF], d[HALF];
-            umma::tmem_ld32x2(tl + TM_S + cb, tl + TM_3 + cb, sv, d);
+            G::ld2(tl + TM_S + cb, tl + TM_3 + cb, sv, d);
 #pragma unroll
             for (int e = 0; e < HALF; ++e) sv[e] = fmaf(decay, sv[e], d[e]);
-            umma::tmem_st32(tl + TM_S + cb, sv);
+            G::st(tl + TM_S + cb, sv);
 #pragma unroll
-            for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, umma::mnmaj_off(cb + c8, row, kDim), sv + c8);
+            for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, G::b_off(cb + c8, row, kDim), sv + c8);
         }
         // the next chunk's v rows (copied by all threads) become visible at this barrier;
         // the CTA stops here if any wait of this chunk timed out
@@ -688,7 +725,7 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
     // final state (fp32, k-last): for each v, consecutive threads write consecutive k
     {
         float sv[HALF];
-        umma::tmem_ld32(tl + TM_S + cb, sv);
+        G::ld(tl + TM_S + cb, sv);
 #pragma unroll
         for (int e = 0; e < HALF; ++e) __stcs(p.new_state + state_off + (size_t)(cb + e) * kDim + row, sv[e]);
     }
@@ -709,20 +746,34 @@ size_t prefill_workspace_bytes(int N, int T, int H, int HV) {
 
 void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st) {
     static bool attr_set = false;
+    static int num_sms = 148;
     if (!attr_set) {
         cudaFuncSetAttribute(chunk::prep::gdn_prefill_chunk_prep_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::prep::SMEM_BYTES);
-        cudaFuncSetAttribute(chunk::chain::gdn_prefill_chunk_chain_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain::SMEM_BYTES);
+        cudaFuncSetAttribute(chunk::chain::gdn_prefill_chunk_chain_kernel<64>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain::Cfg<64>::SMEM_BYTES);
+        cudaFuncSetAttribute(chunk::chain::gdn_prefill_chunk_chain_kernel<32>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain::Cfg<32>::SMEM_BYTES);
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0)
+            num_sms = sms;
         attr_set = true;
     }
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     const long long slots = chunk::ws_slots(p.N, p.T);
     chunk::prep::gdn_prefill_chunk_prep_kernel<<<(unsigned)(slots * p.HV), chunk::prep::NT,
                                                  chunk::prep::SMEM_BYTES, st>>>(p, ws);
-    const long long blocks = (long long)p.N * p.HV * (kDim / chunk::chain::VT);
-    chunk::chain::gdn_prefill_chunk_chain_kernel<<<(unsigned)blocks, chunk::chain::NT, chunk::chain::SMEM_BYTES,
-                                                   st>>>(p, ws);
+    // one chain per (sequence, v-head, V tile): split V into 32-wide tiles when
+    // 64-wide ones would not cover the SMs (e.g. a single long sequence)
+    const long long chains64 = (long long)p.N * p.HV * (kDim / 64);
+    if (chains64 < num_sms) {
+        chunk::chain::gdn_prefill_chunk_chain_kernel<32><<<(unsigned)(chains64 * 2), chunk::chain::NT,
+                                                           chunk::chain::Cfg<32>::SMEM_BYTES, st>>>(p, ws);
+    } else {
+        chunk::chain::gdn_prefill_chunk_chain_kernel<64><<<(unsigned)chains64, chunk::chain::NT,
+                                                           chunk::chain::Cfg<64>::SMEM_BYTES, st>>>(p, ws);
+    }
 }
 
 }  // namespace gdn

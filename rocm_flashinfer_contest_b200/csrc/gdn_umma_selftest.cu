@@ -38,9 +38,10 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const float* A, cons
         uint32_t off = a_mn ? umma::mnmaj_off(m, k, K) : umma::kmaj_off(m, k, 128);
         *reinterpret_cast<T*>(sA + off) = cvt<T>(A[i]);
     }
+    const bool b_sw64 = b_mn && N == 32;  // an MN extent of 32 uses the 64-byte swizzle
     for (int i = tid; i < N * K; i += 128) {
         int n = i / K, k = i % K;
-        uint32_t off = b_mn ? umma::mnmaj_off(n, k, K) : umma::kmaj_off(n, k, N);
+        uint32_t off = b_sw64 ? umma::mnmaj64_off(n, k) : (b_mn ? umma::mnmaj_off(n, k, K) : umma::kmaj_off(n, k, N));
         *reinterpret_cast<T*>(sB + off) = cvt<T>(B[i]);
     }
     if (warp == 0) {
@@ -61,7 +62,8 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(const float* A, cons
         const uint32_t a0 = umma::smem_u32(sA), b0 = umma::smem_u32(sB);
         for (int k0 = 0; k0 < K; k0 += 16) {
             uint64_t ad = a_mn ? umma::desc_mnmaj(a0, K, k0) : umma::desc_kmaj(a0, 128, k0);
-            uint64_t bd = b_mn ? umma::desc_mnmaj(b0, K, k0) : umma::desc_kmaj(b0, N, k0);
+            uint64_t bd = b_sw64 ? umma::desc_mnmaj64(b0, k0)
+                                 : (b_mn ? umma::desc_mnmaj(b0, K, k0) : umma::desc_kmaj(b0, N, k0));
             umma::mma_f16(tmem, ad, bd, idesc, k0 > 0);
         }
         umma::mma_commit(&mbar);
@@ -87,7 +89,7 @@ extern "C" int gdn_umma_selftest(const float* A, const float* B, float* D, int N
     if (!A || !B || !D) return GDN_ERR_INVALID;
     if (N < 16 || N > 128 || N % 16 || K < 16 || K > 128 || K % 16) return GDN_ERR_UNSUPPORTED;
     if ((a_mn | b_mn | fmt) & ~1) return GDN_ERR_INVALID;
-    if (b_mn && N % 64) return GDN_ERR_UNSUPPORTED;  // MN-major tiles are whole 64-wide blocks
+    if (b_mn && N % 64 && N != 32) return GDN_ERR_UNSUPPORTED;  // MN-major: 64-wide blocks, or one 32-wide
     const size_t smem = 2 * 128 * 128 * 2 + 1024;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (fmt) {

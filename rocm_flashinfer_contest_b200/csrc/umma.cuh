@@ -51,6 +51,14 @@ __host__ __device__ constexpr uint32_t mnmaj_off(uint32_t mn, uint32_t k, uint32
            ((((mn & 63u) >> 3) ^ (k & 7u)) << 4) + ((mn & 7u) << 1);
 }
 
+// MN-major, 16-bit elements, 64-byte swizzle (for an MN extent of 32):
+// element (mn < 32, k) — 32 elements = 64 B per k line, 8 lines per 512-B
+// group; 16-byte chunk c of line r sits at c ^ ((r >> 1) & 3).  Tile bases
+// must be 512-byte aligned.
+__host__ __device__ constexpr uint32_t mnmaj64_off(uint32_t mn, uint32_t k) {
+    return (k >> 3) * 512u + (k & 7u) * 64u + ((((mn & 31u) >> 3) ^ ((k >> 1) & 3u)) << 4) + ((mn & 7u) << 1);
+}
+
 // Shared-memory matrix descriptor (SWIZZLE_128B, version 1, base offset 0).
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
     uint64_t d = 0;
@@ -60,6 +68,22 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr, uint32_t lbo_byte
     d |= (uint64_t)1u << 46;  // descriptor version (sm_100)
     d |= (uint64_t)2u << 61;  // layout: 128-byte swizzle
     return d;
+}
+
+// Same with the 64-byte swizzle (layout type 4).
+__device__ __forceinline__ uint64_t desc_sw64(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)4u << 61;  // layout: 64-byte swizzle
+    return d;
+}
+
+// MN-major operand with an MN extent of 32 (64-byte swizzle), K step at k0.
+__device__ __forceinline__ uint64_t desc_mnmaj64(uint32_t tile_saddr, uint32_t k0) {
+    return desc_sw64(tile_saddr + (k0 >> 3) * 512u, 1024u, 512u);
 }
 
 // K-major operand, K step starting at element k0 (multiple of 16).
@@ -230,6 +254,22 @@ __device__ __forceinline__ void tmem_ld32x2(uint32_t ta, uint32_t tb, float (&va
     for (int i = 0; i < 32; ++i) {
         va[i] = __uint_as_float(r[i]);
         vb[i] = __uint_as_float(r[32 + i]);
+    }
+}
+
+// Two 16-column loads from two addresses under a single wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float (&va)[16], float (&vb)[16]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%33];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(ta), "r"(tb) : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        va[i] = __uint_as_float(r[i]);
+        vb[i] = __uint_as_float(r[16 + i]);
     }
 }
 
