@@ -5,7 +5,9 @@
 Headline metric: GDN decode at B = 64 (H = 16, HV = 32,
 K = V = 128, state read and written in place), reported as state GB/s with
 us/step beside it; the prefill tokens/s at one 8192-token sequence (zero
-initial state) rides along in the same line under "prefill".
+initial state) and the pool-indexed multi-token decode (B = 64, T = 4 draft
+tokens, per-token state snapshots, in-place pool) ride along in the same line
+under "prefill" and "mtp".
 
 * ``value``: whole-job state GB/s, device-timed with CUDA events around each
   step's kernel, inputs resident in HBM, L2 flushed (a 256 MiB write) before
@@ -58,6 +60,18 @@ def decode_alg_bytes(B):
     q and k (bf16), v in and o out (bf16), a and b (bf16), A_log and dt_bias."""
     return (decode_state_bytes(B) + 2 * B * H * D * 2 + 2 * B * HV * D * 2 + 2 * B * HV * 2
             + 2 * HV * 4)
+
+
+MTP_B, MTP_T = 64, 4
+
+
+def mtp_alg_bytes(B, T):
+    """Algorithmic HBM bytes of one MTP launch with snapshots: each pool row
+    read once and written once, one snapshot per token (fp32), plus q, k
+    (bf16), v in and o out (bf16), a and b (bf16) for every token."""
+    head = D * D * 4
+    return (B * HV * head * (2 + T) + T * (2 * B * H * D * 2 + 2 * B * HV * D * 2 + 2 * B * HV * 2)
+            + B * 4 + 2 * HV * 4)
 
 
 def prefill_alg_flops(T):
@@ -204,7 +218,7 @@ def timed_steps(fn, steps, flush, stream):
 
 
 def bench_ours(args, rank, world, local):
-    from rocm_flashinfer_contest_b200 import gdn_decode, gdn_prefill, inputs, partition
+    from rocm_flashinfer_contest_b200 import gdn_decode, gdn_mtp, gdn_prefill, inputs, partition
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -255,7 +269,24 @@ def bench_ours(args, rank, world, local):
         barrier(world)
         pre_ms = timed_steps(pre_step, args.steps, flush, stream)
         barrier(world)
+
+        # ---- mtp: B = 64 entries x 4 tokens over a 128-slot pool, in place ----
+        margs = inputs.mtp_inputs(MTP_B, MTP_T, 2 * MTP_B, H, HV, seed=3000 + rank, device=dev,
+                                  intermediate=True)
+        mout = torch.empty((MTP_B, MTP_T, HV, D), dtype=torch.bfloat16, device=dev)
+        mpool = margs[3]
+
+        def mtp_step():
+            gdn_mtp.run_into(*margs[:10], mout, mpool, intermediate_states_buffer=margs[10])
+
+        for _ in range(max(3, args.warmup)):
+            mtp_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        mtp_ms = timed_steps(mtp_step, args.steps, flush, stream)
+        barrier(world)
     clocks = clk.summary()
+    mtp_step_ms = max_over_ranks(statistics.mean(mtp_ms), world, dev)
 
     dec_step_ms = max_over_ranks(statistics.mean(dec_ms), world, dev)
     pre_step_ms = max_over_ranks(statistics.mean(pre_ms), world, dev)
@@ -339,8 +370,8 @@ def bench_ours(args, rank, world, local):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "gdn_decode.run, pinned host inputs -> device -> pinned host outputs"},
         # one kernel per decode / prefill call; counted over every timed region
-        "gpu_launches": 2 * args.steps + e2e_steps + pe2e_steps,
-        "gpu_launches_by_region": {"decode": args.steps, "prefill": args.steps,
+        "gpu_launches": 3 * args.steps + e2e_steps + pe2e_steps,
+        "gpu_launches_by_region": {"decode": args.steps, "prefill": args.steps, "mtp": args.steps,
                                    "decode_e2e": e2e_steps, "prefill_e2e": pe2e_steps},
         "clocks": clocks,
         "prefill": {
@@ -354,6 +385,18 @@ def bench_ours(args, rank, world, local):
                          "alg_flops_per_launch": pre_flops, "peak_src": peaks["src"]},
             "e2e": {"value": round(PREFILL_T * world / (pe2e_step_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h},
+        },
+        "mtp": {
+            "metric": f"gdn_mtp GB/s at B={MTP_B}, T={MTP_T} (pool 128 slots, snapshots, in place)",
+            "value": round(mtp_alg_bytes(MTP_B, MTP_T) * world / (mtp_step_ms * 1e-3) / 1e9, 2),
+            "unit": "GB/s", "ms_per_step": round(mtp_step_ms, 5),
+            "roofline": {"bound": "hbm",
+                         "achieved": round(mtp_alg_bytes(MTP_B, MTP_T) / (statistics.mean(mtp_ms) * 1e-3) / 1e9, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(mtp_alg_bytes(MTP_B, MTP_T) / (statistics.mean(mtp_ms) * 1e-3) / 1e9
+                                       / peaks["hbm_gbs"], 4),
+                         "traffic": profile_traffic("gdn_mtp_B64_T4_ncu.txt"),
+                         "alg_bytes_per_launch": mtp_alg_bytes(MTP_B, MTP_T), "peak_src": peaks["src"]},
         },
     }
     if world == 1 and not args.no_cpu_baseline:

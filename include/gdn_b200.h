@@ -16,6 +16,9 @@
  *   prefill: q,k [T,H,K] bf16; v [T,HV,V] bf16; a,b [T,HV] bf16;
  *            cu_seqlens [N+1] int32 or int64; state/new_state [N,HV,V,K] fp32;
  *            out [T,HV,V] bf16
+ *   mtp    : q,k [B,T,H,K] bf16; v [B,T,HV,V] bf16; a,b [B,T,HV] bf16;
+ *            pool [pool_size,HV,V,K] fp32; indices [B] int32 or int64;
+ *            intermediate [inter_slots,cache_steps,HV,V,K] fp32; out [B,T,HV,V] bf16
  * Supported sizes: K == V == 128, H >= 1, HV % H == 0 (v-head h reads q/k head
  * h / (HV/H)).  `state` may be NULL (zero initial state).  `scale` == 0 means
  * 1/sqrt(K).  Decode: pointers to q and k must be 8-byte aligned; prefill:
@@ -39,7 +42,8 @@ extern "C" {
 #define GDN_ERR_DEVICE 5      /* a kernel reported an error (bounded wait timed out) */
 #define GDN_ERR_TOO_LARGE 6   /* needs more than gdn_prefill_fwd_noalloc's fixed scratch */
 
-/* Version of this ABI (bumped on any signature change). */
+/* Version of this ABI (bumped on any signature change or addition; 3 adds
+ * gdn_mtp_fwd). */
 int gdn_abi_version(void);
 
 /* Human-readable text for a status code. */
@@ -138,6 +142,39 @@ int gdn_prefill_fwd_noalloc(const void *q, const void *k, const void *v, const f
                             const void *cu_seqlens, int cu_seqlens_is_int64, int N, int T,
                             float scale, int H, int HV, int K, int V, void *out, float *new_state,
                             void *stream);
+
+/*
+ * Pool-indexed multi-token decode (speculative-decoding verification; T == 1
+ * is pool-indexed single-token decode): batch entry i advances the state in
+ * pool slot indices[i] over its T tokens.
+ *
+ * Replaces flashinfer's `gated_delta_rule_mtp` (flashinfer/gdn_decode.py:557-745,
+ * whose CuTe DSL kernel needs sm_90) under the same Python API; the maths is
+ * the contest's MTP definition (flashinfer/trace/templates/gdn.py:378-465).
+ *
+ *   pool_out == pool_in : final states written in place (disable_state_update
+ *                         = False in flashinfer's API);
+ *   pool_out == NULL    : no final state written (disable_state_update = True);
+ *   other pool_out      : a new pool (the definition's `final_state`): the whole
+ *                         pool is copied first (cudaMemcpyAsync on `stream`),
+ *                         then the named slots are overwritten.  It must not
+ *                         overlap pool_in.
+ * An index outside [0, pool_size) marks padding (flashinfer's -1): its output
+ * rows are written as zeros and no state is read or written.  The indices of
+ * the other entries must be distinct.  When `intermediate` is not NULL the
+ * state after token t of the entry in slot s is written to intermediate[s, t]
+ * for s < inter_slots (cache_steps >= T).  qk_l2norm == 1 normalises every q
+ * and k head vector in the kernel as x * rsqrt(sum(x^2) + 1e-6)
+ * (`use_qk_l2norm`); 0 takes them as given (the contest definition).
+ * Alignment as decode: q, k 8 bytes; pool and intermediate 16 bytes; indices
+ * their own size.  B == 0 or T == 0 launches no kernel (only the pool copy).
+ */
+int gdn_mtp_fwd(const void *q, const void *k, const void *v, const float *pool_in,
+                float *pool_out, const void *indices, int indices_int64,
+                const float *A_log, const void *a, const float *dt_bias, const void *b,
+                float scale, int B, int T, int H, int HV, int K, int V, int pool_size,
+                int qk_l2norm, void *out, float *intermediate, int inter_slots,
+                int cache_steps, void *stream);
 
 #ifdef __cplusplus
 }

@@ -167,3 +167,64 @@ int gdn_oracle_prefill(const float *q, const float *k, const float *v, const flo
     }
     return 0;
 }
+
+/* Multi-token decode over a state pool: the contest's MTP definition
+ * (flashinfer/trace/templates/gdn.py:378-460, _gdn_mtp_reference).  pool_out
+ * starts as a copy of pool_in (gdn.py:425); batch entry i advances the state
+ * pool_in[idx[i]] over its T tokens (gdn.py:427-455), writing the bf16 output
+ * of every token and, when `inter` is given, the state after every token to
+ * inter[idx[i], t] (gdn.py:457-460); the final state goes to pool_out[idx[i]]
+ * (gdn.py:463).  An index outside [0, pool_size) marks a padding entry: its
+ * output is zero and no state is touched (the serving kernels' -1 padding
+ * convention; the torch template would wrap negative indices instead).
+ * `inter` has `cache_steps` (>= T) token slots per pool slot.
+ * qk_l2norm != 0 first normalises each q and k head vector as
+ * x / sqrt(sum(x^2) + 1e-6), the in-kernel option `use_qk_l2norm` of
+ * flashinfer's gated_delta_rule_mtp (flashinfer/gdn_decode.py:571; the
+ * kernel's rsqrt(sum + 1e-6), gdn_kernels/gdn_decode_mtp.py:359-360). */
+static void l2norm_copy(float *dst, const float *src, int K, int on) {
+    float ss = 0.0f;
+    for (int i = 0; i < K; ++i) ss += src[i] * src[i];
+    float inv = on ? 1.0f / sqrtf(ss + 1e-6f) : 1.0f;
+    for (int i = 0; i < K; ++i) dst[i] = src[i] * inv;
+}
+
+int gdn_oracle_mtp(const float *q, const float *k, const float *v, const float *pool_in,
+                   float *pool_out, const int64_t *idx, const float *A_log, const float *a,
+                   const float *dt_bias, const float *b, float scale, int B, int T, int H, int HV,
+                   int K, int V, int pool_size, int qk_l2norm, uint16_t *out_bf16, float *inter,
+                   int cache_steps, int nthreads) {
+    if (B < 0 || T < 0 || H <= 0 || HV <= 0 || K <= 0 || V <= 0 || HV % H || pool_size < 0) return 1;
+    if (inter && cache_steps < T) return 1;
+    if (scale == 0.0f) scale = 1.0f / sqrtf((float)K);
+    const int rep = HV / H;
+    const size_t head = (size_t)V * K;
+    if (pool_out != pool_in) memcpy(pool_out, pool_in, sizeof(float) * (size_t)pool_size * HV * head);
+    memset(out_bf16, 0, sizeof(uint16_t) * (size_t)B * T * HV * V);
+    nthreads = resolve_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nthreads)
+    for (long long bh = 0; bh < (long long)B * HV; ++bh) {
+        int bi = (int)(bh / HV), h = (int)(bh % HV), hq = h / rep;
+        int64_t slot = idx[bi];
+        if (slot < 0 || slot >= pool_size) continue;
+        float *S = (float *)malloc(sizeof(float) * head);
+        memcpy(S, pool_in + ((size_t)slot * HV + h) * head, sizeof(float) * head);
+        float *o = (float *)malloc(sizeof(float) * (V + 2 * K));
+        float *qn = o + V, *kn = o + V + K;
+        for (int t = 0; t < T; ++t) {
+            size_t bt = (size_t)bi * T + t;
+            float g, beta;
+            gates(A_log[h], a[bt * HV + h], dt_bias[h], b[bt * HV + h], &g, &beta);
+            l2norm_copy(qn, q + (bt * H + hq) * K, K, qk_l2norm);
+            l2norm_copy(kn, k + (bt * H + hq) * K, K, qk_l2norm);
+            step_head(S, qn, kn, v + (bt * HV + h) * V, g, beta, scale, K, V, o);
+            for (int vi = 0; vi < V; ++vi) out_bf16[(bt * HV + h) * V + vi] = f32_to_bf16_rne(o[vi]);
+            if (inter)
+                memcpy(inter + (((size_t)slot * cache_steps + t) * HV + h) * head, S, sizeof(float) * head);
+        }
+        memcpy(pool_out + ((size_t)slot * HV + h) * head, S, sizeof(float) * head);
+        free(o);
+        free(S);
+    }
+    return 0;
+}

@@ -9,6 +9,10 @@ can hand the same seeded inputs to the oracle and to the CUDA path:
   ``run`` signature (solutions/gdn_decode/main.py:117).
 * ``prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale)`` mirrors
   ``gdn_prefill_*_k_last`` (gdn.py:189-273; solutions/gdn_prefill/main.py:31).
+* ``mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b,
+  scale, intermediate_states_buffer=None)`` mirrors the multi-token decode
+  definition ``gdn_mtp`` (gdn.py:378-465), with out-of-range indices as
+  padding.
 
 Both return ``(output bf16, new_state fp32)``.  ``threads`` <= 0 uses every core.
 """
@@ -55,6 +59,12 @@ def _load():
         ctypes.c_int, ctypes.c_int, ctypes.c_float,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
         _u16p, _f32p, ctypes.c_int,
+    ]
+    lib.gdn_oracle_mtp.restype = ctypes.c_int
+    lib.gdn_oracle_mtp.argtypes = [
+        _f32p, _f32p, _f32p, _f32p, _f32p, _i64p, _f32p, _f32p, _f32p, _f32p, ctypes.c_float,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, _u16p, _f32p, ctypes.c_int, ctypes.c_int,
     ]
     _lib = lib
     return lib
@@ -116,3 +126,34 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: in
     if rc != 0:
         raise ValueError(f"gdn_oracle_prefill rejected its arguments (rc={rc})")
     return out.view(torch.bfloat16), new_state
+
+
+def mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale,
+        intermediate_states_buffer=None, qk_l2norm: bool = False, threads: int = 0):
+    """Returns (output [B,T,HV,V] bf16, final_state [pool,HV,V,K] fp32) and
+    fills intermediate_states_buffer ([pool,cache_steps>=T,HV,V,K] fp32) in
+    place when given."""
+    lib = _load()
+    B, T, H, K = q.shape
+    HV, V = v.shape[2], v.shape[3]
+    pool = initial_state.shape[0]
+    qf, kf, vf = _f32(q), _f32(k), _f32(v)
+    pin = _f32(initial_state)
+    idx = initial_state_indices.detach().to("cpu", torch.int64).contiguous()
+    Af, af, dtf, bf = _f32(A_log), _f32(a), _f32(dt_bias), _f32(b)
+    out = torch.empty((B, T, HV, V), dtype=torch.int16)
+    pout = torch.empty_like(pin)
+    inter, steps = None, T
+    if intermediate_states_buffer is not None:
+        inter = _f32(intermediate_states_buffer).clone()
+        steps = inter.shape[1]
+    rc = lib.gdn_oracle_mtp(
+        _ptr(qf, _f32p), _ptr(kf, _f32p), _ptr(vf, _f32p), _ptr(pin, _f32p), _ptr(pout, _f32p),
+        _ptr(idx, _i64p), _ptr(Af, _f32p), _ptr(af, _f32p), _ptr(dtf, _f32p), _ptr(bf, _f32p),
+        _scale(scale, K), B, T, H, HV, K, V, pool, int(bool(qk_l2norm)), _ptr(out, _u16p),
+        _ptr(inter, _f32p), steps, int(threads))
+    if rc != 0:
+        raise ValueError(f"gdn_oracle_mtp rejected its arguments (rc={rc})")
+    if inter is not None:
+        intermediate_states_buffer.copy_(inter)
+    return out.view(torch.bfloat16), pout

@@ -92,3 +92,26 @@ def to_device(args, device):
 
 def to_cpu(args):
     return [x.cpu() if isinstance(x, torch.Tensor) else x for x in args]
+
+
+def mtp_inputs(B: int, T: int, pool_size: int, H: int = 16, HV: int = 32, K: int = D, V: int = D,
+               seed: int = 0, device="cpu", state_std: float = 0.1, indices=None,
+               idx_dtype=torch.int32, intermediate: bool = False):
+    """Arguments of gdn_mtp.run, in order: (q, k, v, initial_state,
+    initial_state_indices, A_log, a, dt_bias, b, scale, intermediate_states_buffer).
+    Indices default to a seeded permutation of distinct pool slots."""
+    g = _gen(seed, device)
+    q = _l2norm_bf16(_normal((B, T, H, K), g, device))
+    k = _l2norm_bf16(_normal((B, T, H, K), g, device))
+    v = _normal((B, T, HV, V), g, device).to(torch.bfloat16)
+    A_log = _uniform((HV,), 0.0, math.log(16.0), g, device)
+    a = _normal((B, T, HV), g, device).to(torch.bfloat16)
+    dt_bias = _uniform((HV,), -1.0, 1.0, g, device)
+    b = _normal((B, T, HV), g, device).to(torch.bfloat16)
+    pool = _normal((pool_size, HV, V, K), g, device, state_std)
+    if indices is None:
+        perm = torch.randperm(pool_size, generator=_gen(seed + 1, "cpu"))[:B]
+        indices = perm
+    idx = torch.as_tensor(indices, dtype=torch.int64).to(idx_dtype).to(device)
+    inter = torch.zeros((pool_size, T, HV, V, K), device=device) if intermediate else None
+    return [q, k, v, pool, idx, A_log, a, dt_bias, b, 1.0 / math.sqrt(K), inter]

@@ -14,12 +14,12 @@ import argparse
 
 import torch
 
-from . import gdn_decode, gdn_prefill, inputs
+from . import gdn_decode, gdn_mtp, gdn_prefill, inputs
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["decode", "prefill"])
+    ap.add_argument("op", choices=["decode", "prefill", "mtp"])
     ap.add_argument("--B", type=int, default=64)
     ap.add_argument("--T", type=int, default=8192)
     ap.add_argument("--seqs", type=int, default=1)
@@ -28,6 +28,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--iters", type=int, default=1)
     ap.add_argument("--no-state", action="store_true")
+    ap.add_argument("--steps", type=int, default=4, help="mtp: tokens per batch entry")
+    ap.add_argument("--no-snapshots", action="store_true", help="mtp: no intermediate states")
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     if a.op == "decode":
@@ -35,6 +37,12 @@ def main(argv=None):
         out = torch.empty((a.B, 1, a.HV, 128), dtype=torch.bfloat16, device=dev)
         ns = args[3] if args[3] is not None else torch.empty((a.B, a.HV, 128, 128), device=dev)
         fn = lambda: gdn_decode.run_into(*args, output=out, new_state=ns)  # noqa: E731
+    elif a.op == "mtp":
+        args = inputs.mtp_inputs(a.B, a.steps, 2 * a.B, a.H, a.HV, seed=0, device=dev,
+                                 intermediate=not a.no_snapshots)
+        out = torch.empty((a.B, a.steps, a.HV, 128), dtype=torch.bfloat16, device=dev)
+        fn = lambda: gdn_mtp.run_into(*args[:10], out, args[3],  # noqa: E731
+                                      intermediate_states_buffer=args[10])
     else:
         lens = [a.T // a.seqs] * a.seqs
         lens[-1] += a.T - sum(lens)

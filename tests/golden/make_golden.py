@@ -28,7 +28,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
-from rocm_flashinfer_contest_b200.inputs import decode_inputs, prefill_inputs  # noqa: E402
+from rocm_flashinfer_contest_b200.inputs import decode_inputs, mtp_inputs, prefill_inputs  # noqa: E402
 
 # (name, B, H, HV, K, with_state, scale, seed, gate_override)
 DECODE_CASES = [
@@ -44,6 +44,17 @@ PREFILL_CASES = [
     ("pre_nostate", [70], 1, 2, 32, False, 0.3, 12, torch.int32),
     ("pre_k128", [40, 90], 1, 2, 128, True, 0.0, 13, torch.int32),
     ("pre_gva4_extreme", [9, 3], 1, 4, 16, True, 1.0, 14, torch.int64),
+]
+
+# (name, B, T, pool, H, HV, K, scale, seed, intermediate buffer, qk_l2norm)
+# qk_l2norm cases feed raw (unnormalised) q/k and normalise them the way
+# flashinfer's gated_delta_rule_mtp kernel does (x * rsqrt(sum(x^2) + 1e-6),
+# flashinfer/gdn_kernels/gdn_decode_mtp.py:359-360) before the template runs.
+MTP_CASES = [
+    ("mtp_small", 3, 4, 5, 2, 4, 16, 0.0, 21, True, False),
+    ("mtp_k128", 2, 3, 3, 1, 2, 128, 0.0, 22, False, False),
+    ("mtp_gva4", 2, 2, 4, 1, 4, 32, 0.4, 23, True, False),
+    ("mtp_l2norm", 2, 3, 3, 1, 2, 32, 0.0, 24, True, True),
 ]
 
 
@@ -101,6 +112,29 @@ def main():
         out[f"{name}/scale"] = np.float32(scale)
         out[f"{name}/out"] = _np(o)
         out[f"{name}/new_state"] = _np(s)
+    from flashinfer.trace.templates.gdn import _gdn_mtp_reference
+    for name, B, T, pool, H, HV, K, scale, seed, inter, l2 in MTP_CASES:
+        args = mtp_inputs(B, T, pool, H, HV, K, K, seed=seed, intermediate=inter)
+        args[9] = scale
+        run_args = list(args[:10])
+        if l2:
+            g = torch.Generator().manual_seed(seed + 100)
+            for i in (0, 1):
+                raw = (torch.randn(args[i].shape, generator=g) * 3.0).to(torch.bfloat16)
+                args[i] = raw
+                xf = raw.float()
+                run_args[i] = xf * torch.rsqrt((xf * xf).sum(-1, keepdim=True) + 1e-6)
+        keys = ["q", "k", "v", "initial_state", "initial_state_indices", "A_log", "a", "dt_bias", "b"]
+        for kname, t in zip(keys, args[:9]):
+            out[f"{name}/{kname}"] = _np(t)
+        out[f"{name}/qk_l2norm"] = np.int32(l2)
+        buf = args[10]
+        o, s = _gdn_mtp_reference(*run_args, intermediate_states_buffer=buf)
+        out[f"{name}/scale"] = np.float32(scale)
+        out[f"{name}/out"] = _np(o)
+        out[f"{name}/new_state"] = _np(s)
+        if buf is not None:
+            out[f"{name}/intermediate"] = _np(buf)
     path = os.path.join(HERE, "gdn_golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path}: {len(out)} arrays, {os.path.getsize(path)} bytes")

@@ -25,7 +25,8 @@ def _declared():
 
 
 def test_header_declares_the_abi():
-    assert {"gdn_decode_fwd", "gdn_prefill_fwd", "gdn_abi_version", "gdn_strerror"} <= _declared()
+    assert {"gdn_decode_fwd", "gdn_prefill_fwd", "gdn_mtp_fwd", "gdn_abi_version",
+            "gdn_strerror"} <= _declared()
 
 
 def test_library_exports_every_declared_symbol():
@@ -44,7 +45,7 @@ def test_python_signatures_cover_the_header():
 
 def test_version_and_strerror():
     lib = _lib.lib()
-    assert lib.gdn_abi_version() >= 1
+    assert lib.gdn_abi_version() == 3
     for code in (0, 1, 2, 3, 4):
         assert lib.gdn_strerror(code)
     assert b"unknown" in lib.gdn_strerror(99)
@@ -98,6 +99,36 @@ def test_decode_rejects_bad_arguments(over, code):
 ])
 def test_prefill_rejects_bad_arguments(over, code):
     assert _prefill(**over) == code
+
+
+def _mtp(**over):
+    d = dict(q=16, k=16, v=16, pool_in=4096, pool_out=4096, idx=16, idx64=0, A_log=16, a=16,
+             dt_bias=16, b=16, scale=0.0, B=2, T=3, H=1, HV=2, K=128, V=128, pool=4, l2=0,
+             out=16, inter=None, inter_slots=0, steps=0, stream=None)
+    d.update(over)
+    return _lib.lib().gdn_mtp_fwd(*d.values())
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(K=64), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(H=3, HV=4), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(B=-1), _lib.GDN_ERR_INVALID),
+    (dict(T=-1), _lib.GDN_ERR_INVALID),
+    (dict(pool=-1), _lib.GDN_ERR_INVALID),
+    (dict(idx64=2), _lib.GDN_ERR_INVALID),
+    (dict(l2=3), _lib.GDN_ERR_INVALID),
+    (dict(idx=None), _lib.GDN_ERR_INVALID),
+    (dict(out=None), _lib.GDN_ERR_INVALID),
+    (dict(inter=4096, inter_slots=4, steps=2), _lib.GDN_ERR_INVALID),   # cache_steps < T
+    (dict(pool_out=4096 + 1024), _lib.GDN_ERR_INVALID),                 # partial overlap
+    (dict(idx=20, idx64=1), _lib.GDN_ERR_ALIGN),
+    (dict(q=18), _lib.GDN_ERR_ALIGN),
+    (dict(inter=4104, inter_slots=4, steps=3), _lib.GDN_ERR_ALIGN),
+    (dict(B=0), _lib.GDN_OK),                       # in place, nothing to do: no CUDA call
+    (dict(T=0, pool_out=None), _lib.GDN_OK),
+])
+def test_mtp_rejects_bad_arguments(over, code):
+    assert _mtp(**over) == code
 
 
 def test_prefill_workspace_size(monkeypatch):

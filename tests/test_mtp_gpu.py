@@ -1,0 +1,168 @@
+"""Parity of the sm_100a pool-indexed multi-token decode kernel (gdn_mtp_fwd,
+through the C ABI) with the CPU oracle and the golden fixtures.
+
+Cases: the golden K = 128 fixture; the contest shape and the benchmark heads
+at T = 1..8; int32 and int64 indices; padding entries (-1 and pool_size);
+intermediate-state buffers with cache_steps > T and fewer slots than the
+pool; untouched pool slots; the in-place / no-update / L2-norm modes of the
+flashinfer-style API; T = 1 against the single-token decode kernel.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from parity import assert_output_close, assert_state_close, bf16_from_u16
+from rocm_flashinfer_contest_b200 import gdn_decode, gdn_mtp, inputs
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden", "gdn_golden.npz")
+FIELDS = ("q", "k", "v", "initial_state", "initial_state_indices", "A_log", "a", "dt_bias", "b")
+
+
+def _oracle(args, buf=None, l2=False):
+    cpu = inputs.to_cpu(args[:10])
+    rb = None if buf is None else torch.zeros(buf.shape)
+    ro, rs = oracle.mtp(*cpu, rb, qk_l2norm=l2)
+    return ro, rs, rb
+
+
+def test_mtp_matches_golden(cuda_device):
+    z = np.load(GOLD)
+    name = "mtp_k128"
+    args = []
+    for f in FIELDS:
+        a = z[f"{name}/{f}"]
+        args.append(bf16_from_u16(a) if f in ("q", "k", "v", "a", "b") else torch.from_numpy(np.array(a)))
+    dargs = inputs.to_device(args, cuda_device)
+    o, s = gdn_mtp.run(*dargs, float(z[f"{name}/scale"]))
+    torch.cuda.synchronize()
+    assert_output_close(o.cpu(), bf16_from_u16(z[f"{name}/out"]))
+    assert_state_close(s.cpu(), torch.from_numpy(z[f"{name}/new_state"]))
+
+
+@pytest.mark.parametrize("B,T,pool,H,HV,idx_dtype,inter,seed", [
+    (8, 4, 16, 4, 8, torch.int32, True, 0),      # contest heads, spec-decode T = 4
+    (8, 2, 8, 4, 8, torch.int64, False, 1),
+    (64, 4, 128, 16, 32, torch.int32, True, 2),  # benchmark heads, B = 64
+    (3, 1, 5, 16, 32, torch.int64, True, 3),     # T = 1: pool-indexed decode
+    (5, 8, 9, 1, 4, torch.int32, False, 4),      # GVA 4, long draft
+    (40, 3, 40, 16, 32, torch.int64, False, 5),  # above the small-grid threshold
+])
+def test_mtp_matches_oracle(cuda_device, B, T, pool, H, HV, idx_dtype, inter, seed):
+    args = inputs.mtp_inputs(B, T, pool, H, HV, seed=seed, idx_dtype=idx_dtype, intermediate=inter)
+    dargs = inputs.to_device(args, cuda_device)
+    pool_before = dargs[3].clone()
+    o, s = gdn_mtp.run(*dargs[:10], intermediate_states_buffer=dargs[10])
+    torch.cuda.synchronize()
+    assert torch.equal(dargs[3], pool_before)  # the definition does not modify its inputs
+    ro, rs, rb = _oracle(args, args[10])
+    assert o.shape == (B, T, HV, 128) and o.dtype == torch.bfloat16
+    assert_output_close(o.cpu(), ro)
+    assert_state_close(s.cpu(), rs)
+    used = set(args[4].tolist())
+    for slot in range(pool):
+        if slot not in used:
+            assert torch.equal(s[slot].cpu(), args[3][slot])
+    if inter:
+        for slot in used:
+            assert_state_close(dargs[10][slot].cpu(), rb[slot], what=f"intermediate[{slot}]")
+
+
+def test_mtp_padding(cuda_device):
+    B, T, pool = 6, 3, 8
+    idx = [3, -1, 0, 8, 5, -7]  # -1, pool_size and another negative are padding
+    args = inputs.mtp_inputs(B, T, pool, 4, 8, seed=20, indices=idx, idx_dtype=torch.int64,
+                             intermediate=True)
+    dargs = inputs.to_device(args, cuda_device)
+    dargs[10].fill_(7.0)
+    out = torch.full((B, T, 8, 128), 3.0, dtype=torch.bfloat16, device=cuda_device)
+    fs = torch.empty_like(dargs[3])
+    gdn_mtp.run_into(*dargs[:10], out, fs, intermediate_states_buffer=dargs[10])
+    torch.cuda.synchronize()
+    ro, rs, _ = _oracle(args)
+    assert_output_close(out.cpu(), ro)
+    for b in (1, 3, 5):
+        assert not out[b].float().any()
+    assert_state_close(fs.cpu(), rs)
+    for slot in (1, 2, 4, 6, 7):  # not named: pool copied, buffer untouched
+        assert torch.equal(fs[slot].cpu(), args[3][slot])
+        assert bool((dargs[10][slot] == 7.0).all())
+
+
+def test_mtp_intermediate_layout(cuda_device):
+    """cache_steps > T and a buffer with fewer slots than the pool."""
+    B, T, pool = 4, 3, 6
+    idx = [5, 1, 3, 0]
+    args = inputs.mtp_inputs(B, T, pool, 4, 8, seed=21, indices=idx)
+    dargs = inputs.to_device(args, cuda_device)
+    buf = torch.full((4, T + 2, 8, 128, 128), -1.0, device=cuda_device)  # slots 0..3 only
+    o, s = gdn_mtp.run(*dargs[:10], intermediate_states_buffer=buf)
+    torch.cuda.synchronize()
+    ro, rs, _ = _oracle(args)
+    assert_output_close(o.cpu(), ro)
+    assert_state_close(s.cpu(), rs)
+    ref_buf = torch.zeros((pool, T + 2, 8, 128, 128))
+    oracle.mtp(*inputs.to_cpu(args[:10]), ref_buf)
+    for slot in (0, 1, 3):
+        assert_state_close(buf[slot, :T].cpu(), ref_buf[slot, :T])
+        assert bool((buf[slot, T:] == -1.0).all())
+    assert bool((buf[2] == -1.0).all())
+    # the last snapshot is the final state
+    assert torch.equal(buf[1, T - 1], s[1])
+
+
+def test_mtp_flashinfer_api_modes(cuda_device):
+    B, T, pool, H, HV = 6, 4, 10, 4, 8
+    args = inputs.mtp_inputs(B, T, pool, H, HV, seed=30)
+    # raw (unnormalised) q, k for use_qk_l2norm
+    g = torch.Generator().manual_seed(31)
+    args[0] = (torch.randn(args[0].shape, generator=g) * 2.5).to(torch.bfloat16)
+    args[1] = (torch.randn(args[1].shape, generator=g) * 2.5).to(torch.bfloat16)
+    dargs = inputs.to_device(args, cuda_device)
+    ro, rs, _ = _oracle(args, l2=True)
+
+    pool_dev = dargs[3].clone()
+    o, ret = gdn_mtp.gated_delta_rule_mtp(*dargs[:3], pool_dev, *dargs[4:10],
+                                          disable_state_update=True, use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert ret is pool_dev and torch.equal(pool_dev, dargs[3])
+    assert_output_close(o.cpu(), ro)
+
+    out = torch.empty((B, T, HV, 128), dtype=torch.bfloat16, device=cuda_device)
+    o2, ret = gdn_mtp.gated_delta_rule_mtp(*dargs[:3], pool_dev, *dargs[4:9], scale=None, output=out,
+                                           disable_state_update=False, use_qk_l2norm=True)
+    torch.cuda.synchronize()
+    assert o2 is out and ret is pool_dev
+    assert_output_close(out.cpu(), ro)
+    assert_state_close(pool_dev.cpu(), rs)
+
+
+def test_mtp_t1_equals_decode(cuda_device):
+    """T = 1 with the identity slot map is the single-token decode step: same
+    formula and summation order, so the results agree to rounding."""
+    B, H, HV = 16, 16, 32
+    d = inputs.to_device(inputs.decode_inputs(B, H, HV, seed=40), cuda_device)
+    o_dec, s_dec = gdn_decode.run(*d)
+    idx = torch.arange(B, dtype=torch.int32, device=cuda_device)
+    o_mtp, s_mtp = gdn_mtp.run(*d[:3], d[3], idx, *d[4:8], d[8])
+    torch.cuda.synchronize()
+    assert float((o_dec.float() - o_mtp.float()).abs().max()) <= 2 ** -7 * float(o_dec.float().abs().max())
+    assert torch.allclose(s_dec, s_mtp, rtol=1e-6, atol=1e-7)
+
+
+def test_mtp_empty_and_bad_args(cuda_device):
+    args = inputs.to_device(inputs.mtp_inputs(0, 2, 4, 4, 8, seed=50), cuda_device)
+    o, s = gdn_mtp.run(*args[:10])
+    torch.cuda.synchronize()
+    assert o.shape == (0, 2, 8, 128)
+    assert torch.equal(s, args[3])  # the new pool is a copy
+    args = inputs.to_device(inputs.mtp_inputs(2, 2, 4, 4, 8, seed=51), cuda_device)
+    with pytest.raises(ValueError):
+        gdn_mtp.run(*args[:4], args[4].float(), *args[5:10])
+    with pytest.raises(ValueError):
+        gdn_mtp.run(*args[:10], intermediate_states_buffer=torch.zeros((4, 1, 8, 128, 128),
+                                                                       device=cuda_device))

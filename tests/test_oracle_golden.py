@@ -57,6 +57,7 @@ def _check(o, s, case):
 def test_golden_file_present():
     assert len([c for c in CASES if c.startswith("dec_")]) >= 4
     assert len([c for c in CASES if c.startswith("pre_")]) >= 4
+    assert len([c for c in CASES if c.startswith("mtp_")]) >= 4
 
 
 @pytest.mark.parametrize("name", sorted(c for c in CASES if c.startswith("dec_")))
@@ -73,6 +74,49 @@ def test_oracle_prefill_matches_reference(name):
     args = [_t(c, f) for f in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens")]
     o, s = oracle.prefill(*args, float(c["scale"]))
     _check(o, s, c)
+
+
+MTP_FIELDS = ("q", "k", "v", "initial_state", "initial_state_indices", "A_log", "a", "dt_bias", "b")
+
+
+def _mtp_args(c):
+    return [_t(c, f) for f in MTP_FIELDS]
+
+
+@pytest.mark.parametrize("name", sorted(c for c in CASES if c.startswith("mtp_")))
+def test_oracle_mtp_matches_reference(name):
+    c = CASES[name]
+    buf = torch.zeros_like(_t(c, "intermediate")) if "intermediate" in c else None
+    o, s = oracle.mtp(*_mtp_args(c), float(c["scale"]), buf, qk_l2norm=bool(c["qk_l2norm"]))
+    _check(o, s, c)
+    if buf is not None:
+        ref = _t(c, "intermediate")
+        assert float((buf - ref).abs().max()) <= 1e-5 * float(ref.abs().max()) + 1e-6
+    # slots no batch entry names are passed through unchanged
+    used = set(int(i) for i in c["initial_state_indices"])
+    for slot in range(s.shape[0]):
+        if slot not in used:
+            assert torch.equal(s[slot], _t(c, "initial_state")[slot])
+
+
+def test_oracle_mtp_padding_rule():
+    """An index outside [0, pool) is padding: zero output, no state touched;
+    the other entries are unaffected by it."""
+    c = CASES["mtp_small"]
+    args = _mtp_args(c)
+    idx = args[4].clone()
+    idx_pad = idx.clone()
+    idx_pad[1] = -1
+    o_ref, s_ref = oracle.mtp(*args[:4], idx, *args[5:], float(c["scale"]))
+    o, s = oracle.mtp(*args[:4], idx_pad, *args[5:], float(c["scale"]))
+    assert not o[1].float().any()
+    assert torch.equal(o[0], o_ref[0]) and torch.equal(o[2], o_ref[2])
+    pool = args[3]
+    assert torch.equal(s[int(idx[1])], pool[int(idx[1])])
+    assert torch.equal(s[int(idx[0])], s_ref[int(idx[0])])
+    idx_pad[1] = pool.shape[0]  # one past the end is padding too
+    o2, s2 = oracle.mtp(*args[:4], idx_pad, *args[5:], float(c["scale"]))
+    assert torch.equal(o2, o) and torch.equal(s2, s)
 
 
 def test_golden_covers_edge_cases():
