@@ -285,8 +285,25 @@ def bench_ours(args, rank, world, local):
         barrier(world)
         mtp_ms = timed_steps(mtp_step, args.steps, flush, stream)
         barrier(world)
+
+        # ---- bf16-state decode: B = 64, state pool in bf16, in place ----
+        bargs = inputs.mtp_inputs(DECODE_B, 1, DECODE_B, H, HV, seed=4000 + rank, device=dev,
+                                  indices=list(range(DECODE_B)))
+        bpool = bargs[3].to(torch.bfloat16)
+        bout = torch.empty((DECODE_B, 1, HV, D), dtype=torch.bfloat16, device=dev)
+
+        def bf16_step():
+            gdn_mtp.run_into(*bargs[:3], bpool, *bargs[4:10], bout, bpool)
+
+        for _ in range(max(3, args.warmup)):
+            bf16_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        bf16_ms = timed_steps(bf16_step, args.steps, flush, stream)
+        barrier(world)
     clocks = clk.summary()
     mtp_step_ms = max_over_ranks(statistics.mean(mtp_ms), world, dev)
+    bf16_step_ms = max_over_ranks(statistics.mean(bf16_ms), world, dev)
 
     dec_step_ms = max_over_ranks(statistics.mean(dec_ms), world, dev)
     pre_step_ms = max_over_ranks(statistics.mean(pre_ms), world, dev)
@@ -342,6 +359,7 @@ def bench_ours(args, rank, world, local):
     alg = decode_alg_bytes(DECODE_B)
     achieved = alg / (statistics.mean(dec_ms) * 1e-3) / 1e9
     pre_flops = prefill_alg_flops(PREFILL_T)
+    bf16_alg = decode_alg_bytes(DECODE_B) - decode_state_bytes(DECODE_B) // 2 + DECODE_B * 4
     pre_achieved = pre_flops / (statistics.mean(pre_ms) * 1e-3) / 1e12
     line = {
         "metric": METRIC,
@@ -370,8 +388,9 @@ def bench_ours(args, rank, world, local):
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "gdn_decode.run, pinned host inputs -> device -> pinned host outputs"},
         # one kernel per decode / prefill call; counted over every timed region
-        "gpu_launches": 3 * args.steps + e2e_steps + pe2e_steps,
+        "gpu_launches": 4 * args.steps + e2e_steps + pe2e_steps,
         "gpu_launches_by_region": {"decode": args.steps, "prefill": args.steps, "mtp": args.steps,
+                                   "decode_bf16_state": args.steps,
                                    "decode_e2e": e2e_steps, "prefill_e2e": pe2e_steps},
         "clocks": clocks,
         "prefill": {
@@ -397,6 +416,16 @@ def bench_ours(args, rank, world, local):
                                        / peaks["hbm_gbs"], 4),
                          "traffic": profile_traffic("gdn_mtp_B64_T4_ncu.txt"),
                          "alg_bytes_per_launch": mtp_alg_bytes(MTP_B, MTP_T), "peak_src": peaks["src"]},
+        },
+        "decode_bf16_state": {
+            "metric": "gdn decode with a bf16 state pool, B=64 (H=16, HV=32), in place: us/step",
+            "value": round(bf16_step_ms * 1e3, 2), "unit": "us/step", "higher_is_better": False,
+            "state_gbs": round(decode_state_bytes(DECODE_B) / 2 * world / (bf16_step_ms * 1e-3) / 1e9, 1),
+            "roofline": {"bound": "hbm",
+                         "achieved": round(bf16_alg / (statistics.mean(bf16_ms) * 1e-3) / 1e9, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(bf16_alg / (statistics.mean(bf16_ms) * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                         "alg_bytes_per_launch": bf16_alg, "peak_src": peaks["src"]},
         },
     }
     if world == 1 and not args.no_cpu_baseline:

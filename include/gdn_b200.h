@@ -17,7 +17,7 @@
  *            cu_seqlens [N+1] int32 or int64; state/new_state [N,HV,V,K] fp32;
  *            out [T,HV,V] bf16
  *   mtp    : q,k [B,T,H,K] bf16; v [B,T,HV,V] bf16; a,b [B,T,HV] bf16;
- *            pool [pool_size,HV,V,K] fp32; indices [B] int32 or int64;
+ *            pool [pool_size,HV,V,K] fp32 or bf16; indices [B] int32 or int64;
  *            intermediate [inter_slots,cache_steps,HV,V,K] fp32; out [B,T,HV,V] bf16
  * Supported sizes: K == V == 128, H >= 1, HV % H == 0 (v-head h reads q/k head
  * h / (HV/H)).  `state` may be NULL (zero initial state).  `scale` == 0 means
@@ -148,32 +148,39 @@ int gdn_prefill_fwd_noalloc(const void *q, const void *k, const void *v, const f
  * is pool-indexed single-token decode): batch entry i advances the state in
  * pool slot indices[i] over its T tokens.
  *
- * Replaces flashinfer's `gated_delta_rule_mtp` (flashinfer/gdn_decode.py:557-745,
- * whose CuTe DSL kernel needs sm_90) under the same Python API; the maths is
- * the contest's MTP definition (flashinfer/trace/templates/gdn.py:378-465).
+ * Replaces flashinfer's `gated_delta_rule_mtp` (flashinfer/gdn_decode.py:557-745)
+ * and the pool / bf16-state forms of `gated_delta_rule_decode_pretranspose`
+ * (gdn_decode.py:118-330), whose CuTe DSL kernels need sm_90; the maths is the
+ * contest's MTP definition (flashinfer/trace/templates/gdn.py:378-465).
  *
  *   pool_out == pool_in : final states written in place (disable_state_update
  *                         = False in flashinfer's API);
  *   pool_out == NULL    : no final state written (disable_state_update = True);
  *   other pool_out      : a new pool (the definition's `final_state`): the whole
  *                         pool is copied first (cudaMemcpyAsync on `stream`),
- *                         then the named slots are overwritten.  It must not
+ *                         then the written slots are overwritten.  It must not
  *                         overlap pool_in.
- * An index outside [0, pool_size) marks padding (flashinfer's -1): its output
- * rows are written as zeros and no state is read or written.  The indices of
- * the other entries must be distinct.  When `intermediate` is not NULL the
- * state after token t of the entry in slot s is written to intermediate[s, t]
- * for s < inter_slots (cache_steps >= T).  qk_l2norm == 1 normalises every q
- * and k head vector in the kernel as x * rsqrt(sum(x^2) + 1e-6)
- * (`use_qk_l2norm`); 0 takes them as given (the contest definition).
- * Alignment as decode: q, k 8 bytes; pool and intermediate 16 bytes; indices
- * their own size.  B == 0 or T == 0 launches no kernel (only the pool copy).
+ * state_bf16 == 0: the pools hold fp32; 1: they hold bf16 — the state is
+ * widened on load, advanced in fp32 over all T tokens and rounded to bf16
+ * (nearest-even) once, when stored.  out_indices (NULL: same as indices, same
+ * integer type) names the slot each entry's final state is written to
+ * (`output_state_indices`); an out-of-range output slot skips the write.
+ * An index outside [0, pool_size) in `indices` marks padding (flashinfer's
+ * -1): its output rows are written as zeros and no state is read or written.
+ * No slot may be written by one entry and read or written by another.  When
+ * `intermediate` is not NULL (fp32 pools only) the state after token t of the
+ * entry read from slot s is written to intermediate[s, t] for s < inter_slots
+ * (cache_steps >= T).  qk_l2norm == 1 normalises every q and k head vector in
+ * the kernel as x * rsqrt(sum(x^2) + 1e-6) (`use_qk_l2norm`); 0 takes them as
+ * given (the contest definition).  Alignment as decode: q, k 8 bytes; pools
+ * and intermediate 16 bytes; indices their own size.  B == 0 or T == 0
+ * launches no kernel (only the pool copy).
  */
-int gdn_mtp_fwd(const void *q, const void *k, const void *v, const float *pool_in,
-                float *pool_out, const void *indices, int indices_int64,
-                const float *A_log, const void *a, const float *dt_bias, const void *b,
-                float scale, int B, int T, int H, int HV, int K, int V, int pool_size,
-                int qk_l2norm, void *out, float *intermediate, int inter_slots,
+int gdn_mtp_fwd(const void *q, const void *k, const void *v, const void *pool_in,
+                void *pool_out, int state_bf16, const void *indices, const void *out_indices,
+                int indices_int64, const float *A_log, const void *a, const float *dt_bias,
+                const void *b, float scale, int B, int T, int H, int HV, int K, int V,
+                int pool_size, int qk_l2norm, void *out, float *intermediate, int inter_slots,
                 int cache_steps, void *stream);
 
 #ifdef __cplusplus

@@ -181,7 +181,12 @@ int gdn_oracle_prefill(const float *q, const float *k, const float *v, const flo
  * qk_l2norm != 0 first normalises each q and k head vector as
  * x / sqrt(sum(x^2) + 1e-6), the in-kernel option `use_qk_l2norm` of
  * flashinfer's gated_delta_rule_mtp (flashinfer/gdn_decode.py:571; the
- * kernel's rsqrt(sum + 1e-6), gdn_kernels/gdn_decode_mtp.py:359-360). */
+ * kernel's rsqrt(sum + 1e-6), gdn_kernels/gdn_decode_mtp.py:359-360).
+ * out_idx (NULL: idx) names the slot each entry's final state is written to
+ * (`output_state_indices`, flashinfer/gdn_decode.py:176-181); an out-of-range
+ * output slot skips the write.  round_bf16 != 0 is the bf16-state form
+ * (gdn_decode.py:206-260): pool_in holds bf16 values (widened), the state is
+ * advanced in fp32 and rounded to bf16 (nearest even) once, when stored. */
 static void l2norm_copy(float *dst, const float *src, int K, int on) {
     float ss = 0.0f;
     for (int i = 0; i < K; ++i) ss += src[i] * src[i];
@@ -189,11 +194,18 @@ static void l2norm_copy(float *dst, const float *src, int K, int on) {
     for (int i = 0; i < K; ++i) dst[i] = src[i] * inv;
 }
 
+static float round_bf16(float f) {
+    uint32_t u = (uint32_t)f32_to_bf16_rne(f) << 16;
+    float r;
+    memcpy(&r, &u, 4);
+    return r;
+}
+
 int gdn_oracle_mtp(const float *q, const float *k, const float *v, const float *pool_in,
-                   float *pool_out, const int64_t *idx, const float *A_log, const float *a,
-                   const float *dt_bias, const float *b, float scale, int B, int T, int H, int HV,
-                   int K, int V, int pool_size, int qk_l2norm, uint16_t *out_bf16, float *inter,
-                   int cache_steps, int nthreads) {
+                   float *pool_out, const int64_t *idx, const int64_t *out_idx, const float *A_log,
+                   const float *a, const float *dt_bias, const float *b, float scale, int B, int T,
+                   int H, int HV, int K, int V, int pool_size, int round_bf16_state, int qk_l2norm,
+                   uint16_t *out_bf16, float *inter, int cache_steps, int nthreads) {
     if (B < 0 || T < 0 || H <= 0 || HV <= 0 || K <= 0 || V <= 0 || HV % H || pool_size < 0) return 1;
     if (inter && cache_steps < T) return 1;
     if (scale == 0.0f) scale = 1.0f / sqrtf((float)K);
@@ -222,7 +234,11 @@ int gdn_oracle_mtp(const float *q, const float *k, const float *v, const float *
             if (inter)
                 memcpy(inter + (((size_t)slot * cache_steps + t) * HV + h) * head, S, sizeof(float) * head);
         }
-        memcpy(pool_out + ((size_t)slot * HV + h) * head, S, sizeof(float) * head);
+        int64_t oslot = out_idx ? out_idx[bi] : slot;
+        if (oslot >= 0 && oslot < pool_size) {
+            float *dst = pool_out + ((size_t)oslot * HV + h) * head;
+            for (size_t e = 0; e < head; ++e) dst[e] = round_bf16_state ? round_bf16(S[e]) : S[e];
+        }
         free(o);
         free(S);
     }

@@ -62,9 +62,9 @@ def _load():
     ]
     lib.gdn_oracle_mtp.restype = ctypes.c_int
     lib.gdn_oracle_mtp.argtypes = [
-        _f32p, _f32p, _f32p, _f32p, _f32p, _i64p, _f32p, _f32p, _f32p, _f32p, ctypes.c_float,
+        _f32p, _f32p, _f32p, _f32p, _f32p, _i64p, _i64p, _f32p, _f32p, _f32p, _f32p, ctypes.c_float,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-        ctypes.c_int, ctypes.c_int, _u16p, _f32p, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, _u16p, _f32p, ctypes.c_int, ctypes.c_int,
     ]
     _lib = lib
     return lib
@@ -129,10 +129,12 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: in
 
 
 def mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale,
-        intermediate_states_buffer=None, qk_l2norm: bool = False, threads: int = 0):
-    """Returns (output [B,T,HV,V] bf16, final_state [pool,HV,V,K] fp32) and
-    fills intermediate_states_buffer ([pool,cache_steps>=T,HV,V,K] fp32) in
-    place when given."""
+        intermediate_states_buffer=None, qk_l2norm: bool = False, output_state_indices=None,
+        threads: int = 0):
+    """Returns (output [B,T,HV,V] bf16, final_state [pool,HV,V,K]) and fills
+    intermediate_states_buffer ([pool,cache_steps>=T,HV,V,K] fp32) in place
+    when given.  A bf16 initial_state selects the bf16-state form and gives a
+    bf16 final_state."""
     lib = _load()
     B, T, H, K = q.shape
     HV, V = v.shape[2], v.shape[3]
@@ -140,6 +142,10 @@ def mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, sca
     qf, kf, vf = _f32(q), _f32(k), _f32(v)
     pin = _f32(initial_state)
     idx = initial_state_indices.detach().to("cpu", torch.int64).contiguous()
+    oidx = None
+    if output_state_indices is not None:
+        oidx = output_state_indices.detach().to("cpu", torch.int64).contiguous()
+    bf16_state = initial_state.dtype == torch.bfloat16
     Af, af, dtf, bf = _f32(A_log), _f32(a), _f32(dt_bias), _f32(b)
     out = torch.empty((B, T, HV, V), dtype=torch.int16)
     pout = torch.empty_like(pin)
@@ -149,11 +155,13 @@ def mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, sca
         steps = inter.shape[1]
     rc = lib.gdn_oracle_mtp(
         _ptr(qf, _f32p), _ptr(kf, _f32p), _ptr(vf, _f32p), _ptr(pin, _f32p), _ptr(pout, _f32p),
-        _ptr(idx, _i64p), _ptr(Af, _f32p), _ptr(af, _f32p), _ptr(dtf, _f32p), _ptr(bf, _f32p),
-        _scale(scale, K), B, T, H, HV, K, V, pool, int(bool(qk_l2norm)), _ptr(out, _u16p),
-        _ptr(inter, _f32p), steps, int(threads))
+        _ptr(idx, _i64p), _ptr(oidx, _i64p), _ptr(Af, _f32p), _ptr(af, _f32p), _ptr(dtf, _f32p),
+        _ptr(bf, _f32p), _scale(scale, K), B, T, H, HV, K, V, pool, int(bf16_state),
+        int(bool(qk_l2norm)), _ptr(out, _u16p), _ptr(inter, _f32p), steps, int(threads))
     if rc != 0:
         raise ValueError(f"gdn_oracle_mtp rejected its arguments (rc={rc})")
     if inter is not None:
         intermediate_states_buffer.copy_(inter)
+    if bf16_state:
+        pout = pout.to(torch.bfloat16)  # exact: every stored value is bf16-rounded
     return out.view(torch.bfloat16), pout

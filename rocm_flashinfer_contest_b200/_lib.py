@@ -33,7 +33,7 @@ SIGNATURES = {
     "gdn_prefill_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i]),
     "gdn_prefill_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                                      _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp]),
-    "gdn_mtp_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _f,
+    "gdn_mtp_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _vp, _vp, _vp, _vp, _f,
                          _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp]),
     "gdn_umma_selftest": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
 }

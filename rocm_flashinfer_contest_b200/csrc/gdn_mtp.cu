@@ -10,7 +10,13 @@
 //   * optional per-token state snapshots into inter[slot, t] (gdn.py:457-460),
 //     `cache_steps` >= T token slots per pool slot (gdn_decode.py:686-692);
 //   * optional in-kernel q/k L2 normalisation, x * rsqrt(sum(x^2) + 1e-6)
-//     (`use_qk_l2norm`, gdn_decode.py:571).
+//     (`use_qk_l2norm`, gdn_decode.py:571);
+//   * the pool in fp32 or in bf16 (the bf16-state decode of
+//     gdn_decode.py:206-260): a bf16 state is widened on load, advanced in
+//     fp32 over all T tokens and rounded to bf16 (nearest-even) once, when the
+//     final state is stored;
+//   * optional output slots (`output_state_indices`, gdn_decode.py:176-181):
+//     the final state of entry i goes to slot out_idx[i] instead of idx[i].
 //
 // Per token, with the state row S[v, :] held in registers across all T tokens
 // (the same row split as the single-token decode kernel: 8 lanes per 512-byte
@@ -28,9 +34,10 @@ struct MtpParams {
     const __nv_bfloat16* q;  // [B, T, H, 128]
     const __nv_bfloat16* k;
     const __nv_bfloat16* v;  // [B, T, HV, 128]
-    const float* pool_in;    // [pool, HV, 128, 128]
-    float* pool_out;         // nullable: final state not written
+    const void* pool_in;     // [pool, HV, 128, 128] fp32 or bf16
+    void* pool_out;          // nullable: final state not written
     const void* idx;         // [B] int32 or int64
+    const void* out_idx;     // nullable: final state to slot idx[i]
     const float* A_log;
     const __nv_bfloat16* a;  // [B, T, HV]
     const float* dt_bias;
@@ -45,6 +52,51 @@ __device__ __forceinline__ float mtp_dot4(float4 x, float4 y) {
     return x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
 }
 
+// Column layout of a lane's 16 values of a row (4 groups of 4).  fp32 state:
+// group j at columns 4*sub + 32*j (one 16-byte access per group).  bf16 state:
+// groups 2p, 2p+1 at columns 8*sub + 64*p (+4), so one 16-byte access moves
+// two groups and a row needs two accesses per lane.
+template <typename StateT>
+__device__ __forceinline__ int mtp_col(int sub, int j) {
+    return sizeof(StateT) == 4 ? 4 * sub + 32 * j : 8 * sub + 64 * (j >> 1) + 4 * (j & 1);
+}
+
+__device__ __forceinline__ float4 mtp_widen4(uint2 raw);
+
+// One row's 16 values for this lane (row base `off`, in elements), widened.
+__device__ __forceinline__ void mtp_load_row(const float* base, size_t off, int sub, float4 (&r)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[j] = __ldcs(reinterpret_cast<const float4*>(base + off + mtp_col<float>(sub, j)));
+}
+__device__ __forceinline__ void mtp_load_row(const __nv_bfloat16* base, size_t off, int sub, float4 (&r)[4]) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        uint4 raw = __ldcs(reinterpret_cast<const uint4*>(base + off + mtp_col<__nv_bfloat16>(sub, 2 * p)));
+        r[2 * p] = mtp_widen4(make_uint2(raw.x, raw.y));
+        r[2 * p + 1] = mtp_widen4(make_uint2(raw.z, raw.w));
+    }
+}
+__device__ __forceinline__ void mtp_store_row(float* base, size_t off, int sub, const float4 (&r)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) __stcs(reinterpret_cast<float4*>(base + off + mtp_col<float>(sub, j)), r[j]);
+}
+__device__ __forceinline__ uint32_t mtp_pack2(float x, float y) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void mtp_store_row(__nv_bfloat16* base, size_t off, int sub, const float4 (&r)[4]) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        const float4 a = r[2 * p], b = r[2 * p + 1];
+        uint4 raw = make_uint4(mtp_pack2(a.x, a.y), mtp_pack2(a.z, a.w), mtp_pack2(b.x, b.y), mtp_pack2(b.z, b.w));
+        __stcs(reinterpret_cast<uint4*>(base + off + mtp_col<__nv_bfloat16>(sub, 2 * p)), raw);
+    }
+}
+
+__device__ __forceinline__ long long mtp_index(const void* idx, int idx64, int i) {
+    return idx64 ? static_cast<const long long*>(idx)[i] : (long long)static_cast<const int*>(idx)[i];
+}
+
 __device__ __forceinline__ float row8_sum(float x) {
     x += __shfl_xor_sync(0xffffffffu, x, 1);
     x += __shfl_xor_sync(0xffffffffu, x, 2);
@@ -52,23 +104,30 @@ __device__ __forceinline__ float row8_sum(float x) {
     return x;
 }
 
-// Everything one token contributes to one lane.
+// Everything one token contributes to one lane (q, k still packed bf16).
 template <int kPasses>
 struct MtpToken {
-    float4 q[4], k[4];
+    uint2 q[4], k[4];
     float v[kPasses];
     float a, b;
 };
 
-template <int kPasses>
+__device__ __forceinline__ float4 mtp_widen4(uint2 raw) {
+    __nv_bfloat162 lo = *reinterpret_cast<__nv_bfloat162*>(&raw.x);
+    __nv_bfloat162 hi = *reinterpret_cast<__nv_bfloat162*>(&raw.y);
+    float2 x = __bfloat1622float2(lo), y = __bfloat1622float2(hi);
+    return make_float4(x.x, x.y, y.x, y.y);
+}
+
+template <typename StateT, int kPasses>
 __device__ __forceinline__ void mtp_load_token(MtpToken<kPasses>& tk, const MtpParams& p, size_t bt,
                                                int hq, int hv, int sub, int row_base) {
-    const __nv_bfloat16* qh = p.q + (bt * p.H + hq) * kDim + 4 * sub;
-    const __nv_bfloat16* kh = p.k + (bt * p.H + hq) * kDim + 4 * sub;
+    const __nv_bfloat16* qh = p.q + (bt * p.H + hq) * kDim;
+    const __nv_bfloat16* kh = p.k + (bt * p.H + hq) * kDim;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        tk.q[j] = load_bf16x4(qh + 32 * j);
-        tk.k[j] = load_bf16x4(kh + 32 * j);
+        tk.q[j] = *reinterpret_cast<const uint2*>(qh + mtp_col<StateT>(sub, j));
+        tk.k[j] = *reinterpret_cast<const uint2*>(kh + mtp_col<StateT>(sub, j));
     }
     const size_t vh = bt * p.HV + hv;
 #pragma unroll
@@ -77,8 +136,9 @@ __device__ __forceinline__ void mtp_load_token(MtpToken<kPasses>& tk, const MtpP
     tk.b = bf16_to_f32(p.b[vh]);
 }
 
-// ROWS_PER_CTA rows of one (batch entry, v-head) per CTA of 4 warps.
-template <int ROWS_PER_CTA>
+// ROWS_PER_CTA rows of one (batch entry, v-head) per CTA of 4 warps; the pool
+// holds StateT (float or __nv_bfloat16).
+template <int ROWS_PER_CTA, typename StateT>
 __global__ void __launch_bounds__(128) gdn_mtp_kernel(const MtpParams p) {
     constexpr int kRowsPerWarp = ROWS_PER_CTA / 4;
     constexpr int kPasses = kRowsPerWarp / 4;
@@ -95,8 +155,7 @@ __global__ void __launch_bounds__(128) gdn_mtp_kernel(const MtpParams p) {
     const int row_base = rb * ROWS_PER_CTA + warp * kRowsPerWarp + rsub;
     const int T = p.T;
 
-    const long long slot = p.idx64 ? static_cast<const long long*>(p.idx)[bi]
-                                   : (long long)static_cast<const int*>(p.idx)[bi];
+    const long long slot = mtp_index(p.idx, p.idx64, bi);
     if (slot < 0 || slot >= p.pool_size) {  // padding entry
         if (sub == 0) {
             for (int t = 0; t < T; ++t) {
@@ -108,43 +167,47 @@ __global__ void __launch_bounds__(128) gdn_mtp_kernel(const MtpParams p) {
         return;
     }
 
-    const size_t row_off = (size_t)row_base * kDim + 4 * sub;
+    const size_t row_off = (size_t)row_base * kDim;
     const size_t sbase = ((size_t)slot * p.HV + hv) * kDim * kDim + row_off;
+    const StateT* pin = static_cast<const StateT*>(p.pool_in);
     float4 s[kPasses][4];
 #pragma unroll
-    for (int ps = 0; ps < kPasses; ++ps)
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            s[ps][j] = __ldcs(reinterpret_cast<const float4*>(p.pool_in + sbase + (size_t)ps * 4 * kDim + 32 * j));
+    for (int ps = 0; ps < kPasses; ++ps) mtp_load_row(pin, sbase + (size_t)ps * 4 * kDim, sub, s[ps]);
 
     const bool snap = p.inter != nullptr && slot < p.inter_slots;
     const bool upper = (sub & 4) != 0;
     MtpToken<kPasses> cur, nxt;
-    mtp_load_token(cur, p, (size_t)bi * T, hq, hv, sub, row_base);
+    mtp_load_token<StateT>(cur, p, (size_t)bi * T, hq, hv, sub, row_base);
 
     for (int t = 0; t < T; ++t) {
         const size_t bt = (size_t)bi * T + t;
-        mtp_load_token(nxt, p, t + 1 < T ? bt + 1 : bt, hq, hv, sub, row_base);
+        mtp_load_token<StateT>(nxt, p, t + 1 < T ? bt + 1 : bt, hq, hv, sub, row_base);
 
+        float4 qf[4], kf[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            qf[j] = mtp_widen4(cur.q[j]);
+            kf[j] = mtp_widen4(cur.k[j]);
+        }
         const float g = expf(log_gate(p.A_log[hv], cur.a, p.dt_bias[hv]));
         const float beta = sigmoidf_(cur.b);
         if (p.l2norm) {
             float qq = 0.f, kk = 0.f;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                qq += mtp_dot4(cur.q[j], cur.q[j]);
-                kk += mtp_dot4(cur.k[j], cur.k[j]);
+                qq += mtp_dot4(qf[j], qf[j]);
+                kk += mtp_dot4(kf[j], kf[j]);
             }
             const float iq = rsqrtf(row8_sum(qq) + 1e-6f), ik = rsqrtf(row8_sum(kk) + 1e-6f);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                cur.q[j] = make_float4(cur.q[j].x * iq, cur.q[j].y * iq, cur.q[j].z * iq, cur.q[j].w * iq);
-                cur.k[j] = make_float4(cur.k[j].x * ik, cur.k[j].y * ik, cur.k[j].z * ik, cur.k[j].w * ik);
+                qf[j] = make_float4(qf[j].x * iq, qf[j].y * iq, qf[j].z * iq, qf[j].w * iq);
+                kf[j] = make_float4(kf[j].x * ik, kf[j].y * ik, kf[j].z * ik, kf[j].w * ik);
             }
         }
         float kq = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) kq += mtp_dot4(cur.k[j], cur.q[j]);
+        for (int j = 0; j < 4; ++j) kq += mtp_dot4(kf[j], qf[j]);
         kq = row8_sum(kq);
 
         const size_t ob = (bt * p.HV + hv) * kDim + row_base;
@@ -155,8 +218,8 @@ __global__ void __launch_bounds__(128) gdn_mtp_kernel(const MtpParams p) {
             float sk = 0.f, sq = 0.f;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                sk += mtp_dot4(s[ps][j], cur.k[j]);
-                sq += mtp_dot4(s[ps][j], cur.q[j]);
+                sk += mtp_dot4(s[ps][j], kf[j]);
+                sq += mtp_dot4(s[ps][j], qf[j]);
             }
             float give = upper ? sk : sq;
             float keep = upper ? sq : sk;
@@ -169,65 +232,207 @@ __global__ void __launch_bounds__(128) gdn_mtp_kernel(const MtpParams p) {
             if (sub == 4) p.out[ob + ps * 4] = __float2bfloat16_rn(p.scale * (g * keep + delta * kq));
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                s[ps][j].x = fmaf(g, s[ps][j].x, delta * cur.k[j].x);
-                s[ps][j].y = fmaf(g, s[ps][j].y, delta * cur.k[j].y);
-                s[ps][j].z = fmaf(g, s[ps][j].z, delta * cur.k[j].z);
-                s[ps][j].w = fmaf(g, s[ps][j].w, delta * cur.k[j].w);
+                s[ps][j].x = fmaf(g, s[ps][j].x, delta * kf[j].x);
+                s[ps][j].y = fmaf(g, s[ps][j].y, delta * kf[j].y);
+                s[ps][j].z = fmaf(g, s[ps][j].z, delta * kf[j].z);
+                s[ps][j].w = fmaf(g, s[ps][j].w, delta * kf[j].w);
             }
-            if (snap) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    __stcs(reinterpret_cast<float4*>(snap_dst + (size_t)ps * 4 * kDim + 32 * j), s[ps][j]);
+            if constexpr (sizeof(StateT) == 4) {  // snapshots exist for fp32 pools only
+                if (snap) mtp_store_row(snap_dst, (size_t)ps * 4 * kDim, sub, s[ps]);
             }
         }
         cur = nxt;
     }
 
-    if (p.pool_out != nullptr) {
+    const long long oslot = p.out_idx != nullptr ? mtp_index(p.out_idx, p.idx64, bi) : slot;
+    if (p.pool_out != nullptr && oslot >= 0 && oslot < p.pool_size) {
+        StateT* pout = static_cast<StateT*>(p.pool_out);
+        const size_t obase = ((size_t)oslot * p.HV + hv) * kDim * kDim + row_off;
 #pragma unroll
-        for (int ps = 0; ps < kPasses; ++ps)
+        for (int ps = 0; ps < kPasses; ++ps) mtp_store_row(pout, obase + (size_t)ps * 4 * kDim, sub, s[ps]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Single-token form (T == 1: pool-indexed decode).  Nothing carries over to a
+// next token, so each lane keeps its rows as loaded (packed: bf16 stays two
+// bytes per value in registers) and widens one row pass at a time.  That
+// keeps the register count near the batch decode kernel's and with it the
+// bytes in flight per SM, which is what bounds an HBM stream.
+
+template <typename StateT>
+struct RowPack;
+template <>
+struct RowPack<float> {
+    float4 w[4];
+};
+template <>
+struct RowPack<__nv_bfloat16> {
+    uint4 w[2];
+};
+
+__device__ __forceinline__ void pack_load(RowPack<float>& r, const float* base, size_t off, int sub) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-                __stcs(reinterpret_cast<float4*>(p.pool_out + sbase + (size_t)ps * 4 * kDim + 32 * j), s[ps][j]);
+    for (int j = 0; j < 4; ++j) r.w[j] = __ldcs(reinterpret_cast<const float4*>(base + off + mtp_col<float>(sub, j)));
+}
+__device__ __forceinline__ void pack_load(RowPack<__nv_bfloat16>& r, const __nv_bfloat16* base, size_t off, int sub) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+        r.w[p] = __ldcs(reinterpret_cast<const uint4*>(base + off + mtp_col<__nv_bfloat16>(sub, 2 * p)));
+}
+__device__ __forceinline__ void pack_widen(const RowPack<float>& r, float4 (&x)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = r.w[j];
+}
+__device__ __forceinline__ void pack_widen(const RowPack<__nv_bfloat16>& r, float4 (&x)[4]) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        x[2 * p] = mtp_widen4(make_uint2(r.w[p].x, r.w[p].y));
+        x[2 * p + 1] = mtp_widen4(make_uint2(r.w[p].z, r.w[p].w));
+    }
+}
+
+template <int ROWS_PER_CTA, typename StateT>
+__global__ void __launch_bounds__(128) gdn_pool_decode_kernel(const MtpParams p) {
+    constexpr int kRowsPerWarp = ROWS_PER_CTA / 4;
+    constexpr int kPasses = kRowsPerWarp / 4;
+    constexpr int kBlocksPerHead = kDim / ROWS_PER_CTA;
+    static_assert(kPasses >= 1 && kRowsPerWarp % 4 == 0, "4 rows per warp pass");
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int sub = lane & 7;
+    const int rsub = lane >> 3;
+    const long long head = blockIdx.x / kBlocksPerHead;  // bi * HV + hv
+    const int rb = blockIdx.x % kBlocksPerHead;
+    const int bi = (int)(head / p.HV), hv = (int)(head % p.HV);
+    const int hq = hv / p.rep;
+    const int row_base = rb * ROWS_PER_CTA + warp * kRowsPerWarp + rsub;
+    const size_t ob = (size_t)head * kDim + row_base;  // [B, 1, HV, V]
+
+    const long long slot = mtp_index(p.idx, p.idx64, bi);
+    if (slot < 0 || slot >= p.pool_size) {  // padding entry
+        if (sub == 0) {
+#pragma unroll
+            for (int ps = 0; ps < kPasses; ++ps) p.out[ob + ps * 4] = __float2bfloat16_rn(0.0f);
+        }
+        return;
+    }
+
+    const size_t row_off = (size_t)row_base * kDim;
+    const size_t sbase = ((size_t)slot * p.HV + hv) * kDim * kDim + row_off;
+    const StateT* pin = static_cast<const StateT*>(p.pool_in);
+    RowPack<StateT> rows[kPasses];
+#pragma unroll
+    for (int ps = 0; ps < kPasses; ++ps) pack_load(rows[ps], pin, sbase + (size_t)ps * 4 * kDim, sub);
+
+    MtpToken<kPasses> tk;
+    mtp_load_token<StateT>(tk, p, (size_t)bi, hq, hv, sub, row_base);
+    float4 qf[4], kf[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        qf[j] = mtp_widen4(tk.q[j]);
+        kf[j] = mtp_widen4(tk.k[j]);
+    }
+    const float g = expf(log_gate(p.A_log[hv], tk.a, p.dt_bias[hv]));
+    const float beta = sigmoidf_(tk.b);
+    if (p.l2norm) {
+        float qq = 0.f, kk = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            qq += mtp_dot4(qf[j], qf[j]);
+            kk += mtp_dot4(kf[j], kf[j]);
+        }
+        const float iq = rsqrtf(row8_sum(qq) + 1e-6f), ik = rsqrtf(row8_sum(kk) + 1e-6f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            qf[j] = make_float4(qf[j].x * iq, qf[j].y * iq, qf[j].z * iq, qf[j].w * iq);
+            kf[j] = make_float4(kf[j].x * ik, kf[j].y * ik, kf[j].z * ik, kf[j].w * ik);
+        }
+    }
+    float kq = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) kq += mtp_dot4(kf[j], qf[j]);
+    kq = row8_sum(kq);
+
+    const long long oslot = p.out_idx != nullptr ? mtp_index(p.out_idx, p.idx64, bi) : slot;
+    StateT* pout = (p.pool_out != nullptr && oslot >= 0 && oslot < p.pool_size) ? static_cast<StateT*>(p.pool_out)
+                                                                                : nullptr;
+    const size_t obase = ((size_t)oslot * p.HV + hv) * kDim * kDim + row_off;
+    float* snap_dst = (p.inter != nullptr && slot < p.inter_slots)
+                          ? p.inter + ((size_t)slot * p.cache_steps * p.HV + hv) * kDim * kDim + row_off
+                          : nullptr;
+    const bool upper = (sub & 4) != 0;
+#pragma unroll
+    for (int ps = 0; ps < kPasses; ++ps) {
+        float4 x[4];
+        pack_widen(rows[ps], x);
+        float sk = 0.f, sq = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            sk += mtp_dot4(x[j], kf[j]);
+            sq += mtp_dot4(x[j], qf[j]);
+        }
+        float give = upper ? sk : sq;
+        float keep = upper ? sq : sk;
+        keep += __shfl_xor_sync(0xffffffffu, give, 4);
+        keep += __shfl_xor_sync(0xffffffffu, keep, 1);
+        keep += __shfl_xor_sync(0xffffffffu, keep, 2);
+        const float sk_all = __shfl_sync(0xffffffffu, keep, lane & ~4);
+        const float delta = beta * (tk.v[ps] - g * sk_all);
+        if (sub == 4) p.out[ob + ps * 4] = __float2bfloat16_rn(p.scale * (g * keep + delta * kq));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            x[j].x = fmaf(g, x[j].x, delta * kf[j].x);
+            x[j].y = fmaf(g, x[j].y, delta * kf[j].y);
+            x[j].z = fmaf(g, x[j].z, delta * kf[j].z);
+            x[j].w = fmaf(g, x[j].w, delta * kf[j].w);
+        }
+        if constexpr (sizeof(StateT) == 4) {  // snapshots exist for fp32 pools only
+            if (snap_dst != nullptr) mtp_store_row(snap_dst, (size_t)ps * 4 * kDim, sub, x);
+        }
+        if (pout != nullptr) mtp_store_row(pout, obase + (size_t)ps * 4 * kDim, sub, x);
     }
 }
 
 }  // namespace gdn
 
-extern "C" int gdn_mtp_fwd(const void* q, const void* k, const void* v, const float* pool_in,
-                           float* pool_out, const void* indices, int indices_int64,
-                           const float* A_log, const void* a, const float* dt_bias, const void* b,
-                           float scale, int B, int T, int H, int HV, int K, int V, int pool_size,
-                           int qk_l2norm, void* out, float* intermediate, int inter_slots,
+extern "C" int gdn_mtp_fwd(const void* q, const void* k, const void* v, const void* pool_in,
+                           void* pool_out, int state_bf16, const void* indices, const void* out_indices,
+                           int indices_int64, const float* A_log, const void* a, const float* dt_bias,
+                           const void* b, float scale, int B, int T, int H, int HV, int K, int V,
+                           int pool_size, int qk_l2norm, void* out, float* intermediate, int inter_slots,
                            int cache_steps, void* stream) {
     if (B < 0 || T < 0 || H <= 0 || HV <= 0 || pool_size < 0) return GDN_ERR_INVALID;
-    if ((indices_int64 != 0 && indices_int64 != 1) || (qk_l2norm != 0 && qk_l2norm != 1))
+    if ((indices_int64 != 0 && indices_int64 != 1) || (qk_l2norm != 0 && qk_l2norm != 1) ||
+        (state_bf16 != 0 && state_bf16 != 1))
         return GDN_ERR_INVALID;
     if (K != gdn::kDim || V != gdn::kDim || HV % H != 0) return GDN_ERR_UNSUPPORTED;
-    if (intermediate && (inter_slots < 0 || cache_steps < T)) return GDN_ERR_INVALID;
-    const size_t head_bytes = sizeof(float) * gdn::kDim * gdn::kDim;
+    if (intermediate && (inter_slots < 0 || cache_steps < T || state_bf16)) return GDN_ERR_INVALID;
+    const size_t elem = state_bf16 ? 2 : 4;
+    const size_t head_bytes = elem * gdn::kDim * gdn::kDim;
     const size_t pool_bytes = (size_t)pool_size * HV * head_bytes;
     const bool copy_pool = pool_out != nullptr && pool_out != pool_in && pool_size > 0;
     if (copy_pool) {
         if (!pool_in) return GDN_ERR_INVALID;
-        const char* i0 = reinterpret_cast<const char*>(pool_in);
-        const char* o0 = reinterpret_cast<const char*>(pool_out);
+        const char* i0 = static_cast<const char*>(pool_in);
+        const char* o0 = static_cast<const char*>(pool_out);
         if (o0 < i0 + pool_bytes && i0 < o0 + pool_bytes) return GDN_ERR_INVALID;  // partial overlap
         if (!gdn_aligned(pool_out, 16) || !gdn_aligned(pool_in, 16)) return GDN_ERR_ALIGN;
     }
     if ((long long)B * T > 0) {
         if (!q || !k || !v || !pool_in || !indices || !A_log || !a || !dt_bias || !b || !out)
             return GDN_ERR_INVALID;
+        const uintptr_t ia = indices_int64 ? 8 : 4;
         if (!gdn_aligned(q, 8) || !gdn_aligned(k, 8) || !gdn_aligned(pool_in, 16) ||
             (pool_out && !gdn_aligned(pool_out, 16)) || (intermediate && !gdn_aligned(intermediate, 16)) ||
             !gdn_aligned(v, 2) || !gdn_aligned(out, 2) || !gdn_aligned(a, 2) || !gdn_aligned(b, 2) ||
-            !gdn_aligned(A_log, 4) || !gdn_aligned(dt_bias, 4) ||
-            !gdn_aligned(indices, indices_int64 ? 8 : 4))
+            !gdn_aligned(A_log, 4) || !gdn_aligned(dt_bias, 4) || !gdn_aligned(indices, ia) ||
+            (out_indices && !gdn_aligned(out_indices, ia)))
             return GDN_ERR_ALIGN;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (copy_pool) {
-        // slots no batch entry names keep their value in the new pool
+        // slots no batch entry writes keep their value in the new pool
         if (cudaMemcpyAsync(pool_out, pool_in, pool_bytes, cudaMemcpyDeviceToDevice, st) != cudaSuccess)
             return GDN_ERR_CUDA;
     }
@@ -241,6 +446,7 @@ extern "C" int gdn_mtp_fwd(const void* q, const void* k, const void* v, const fl
     p.pool_in = pool_in;
     p.pool_out = pool_out;
     p.idx = indices;
+    p.out_idx = out_indices;
     p.idx64 = indices_int64;
     p.A_log = A_log;
     p.a = static_cast<const __nv_bfloat16*>(a);
@@ -258,10 +464,32 @@ extern "C" int gdn_mtp_fwd(const void* q, const void* k, const void* v, const fl
     p.cache_steps = cache_steps;
     p.l2norm = qk_l2norm;
     const long long heads = (long long)B * HV;
-    if (heads * (gdn::kDim / 32) < 4 * 148) {
-        gdn::gdn_mtp_kernel<16><<<(unsigned)(heads * (gdn::kDim / 16)), 128, 0, st>>>(p);
+    const bool small = heads * (gdn::kDim / 32) < 4 * 148;
+    if (T == 1) {
+        // bf16 rows are half as long: twice the rows per CTA for the same bytes in flight
+        const int rows = small ? 16 : state_bf16 ? 64 : 32;
+        const unsigned grid = (unsigned)(heads * (gdn::kDim / rows));
+        if (state_bf16) {
+            if (rows == 16) gdn::gdn_pool_decode_kernel<16, __nv_bfloat16><<<grid, 128, 0, st>>>(p);
+            else gdn::gdn_pool_decode_kernel<64, __nv_bfloat16><<<grid, 128, 0, st>>>(p);
+        } else {
+            if (rows == 16) gdn::gdn_pool_decode_kernel<16, float><<<grid, 128, 0, st>>>(p);
+            else gdn::gdn_pool_decode_kernel<32, float><<<grid, 128, 0, st>>>(p);
+        }
+        return gdn_launch_status();
+    }
+    if (state_bf16) {
+        // half the bytes per row: 64 rows per CTA keep as many bytes in flight
+        const bool large = heads * (gdn::kDim / 64) >= 8 * 148;
+        const int rows = small ? 16 : large ? 64 : 32;
+        const unsigned grid = (unsigned)(heads * (gdn::kDim / rows));
+        if (rows == 16) gdn::gdn_mtp_kernel<16, __nv_bfloat16><<<grid, 128, 0, st>>>(p);
+        else if (rows == 32) gdn::gdn_mtp_kernel<32, __nv_bfloat16><<<grid, 128, 0, st>>>(p);
+        else gdn::gdn_mtp_kernel<64, __nv_bfloat16><<<grid, 128, 0, st>>>(p);
     } else {
-        gdn::gdn_mtp_kernel<32><<<(unsigned)(heads * (gdn::kDim / 32)), 128, 0, st>>>(p);
+        const unsigned grid = (unsigned)(heads * (gdn::kDim / (small ? 16 : 32)));
+        if (small) gdn::gdn_mtp_kernel<16, float><<<grid, 128, 0, st>>>(p);
+        else gdn::gdn_mtp_kernel<32, float><<<grid, 128, 0, st>>>(p);
     }
     return gdn_launch_status();
 }

@@ -13,7 +13,13 @@ solution (solutions/gdn_decode/main.py:117-135) and the contest definition
     output   [B, 1, HV, 128]  bf16        new_state [B, HV, 128, 128] fp32
 
 Inputs are never modified: ``new_state`` is a fresh tensor, as in the
-reference (main.py:104).  ``run_into`` is the destination-passing form; it
+reference (main.py:104).
+
+``gated_delta_rule_decode_pretranspose(...)`` is flashinfer's serving decode
+API (flashinfer/gdn_decode.py:118-330): state fp32 or bf16 ([B, HV, V, K],
+updated in place) or a slot pool (``initial_state`` + ``initial_state_indices``,
+optional ``output_state_indices``, ``-1`` padding), T >= 1 tokens per entry,
+in-kernel q/k L2-norm by default.  It runs the pool kernel of gdn_mtp.  ``run_into`` is the destination-passing form; it
 accepts ``new_state is state`` for an in-place update with identical traffic.
 One kernel launch on the current stream of the inputs' device; no host sync
 unless ``scale`` is a device tensor (the reference reads it with ``.item()``).
@@ -80,3 +86,44 @@ def run(q, k, v, state, A_log, a, dt_bias, b, scale):
     output = torch.empty((B, 1, HV, V), dtype=torch.bfloat16, device=dev)
     new_state = torch.empty((B, HV, V, K), dtype=torch.float32, device=dev)
     return run_into(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)
+
+
+def gated_delta_rule_decode_pretranspose(q, k, v, state, A_log, a, dt_bias, b, scale=None,
+                                         output=None, use_qk_l2norm: bool = True,
+                                         initial_state=None, initial_state_indices=None,
+                                         output_state_indices=None):
+    """flashinfer's ``gated_delta_rule_decode_pretranspose``: returns
+    ``(output [B, T, HV, V], state or initial_state)``, the state updated in
+    place.  Padding entries (index outside the pool) get a zero output and
+    leave every slot untouched, for fp32 and bf16 states alike."""
+    from . import gdn_mtp
+
+    use_pool = initial_state is not None
+    if use_pool != (initial_state_indices is not None):
+        raise ValueError("initial_state and initial_state_indices must be provided together")
+    if output_state_indices is not None and not use_pool:
+        raise ValueError("output_state_indices can only be used with initial_state (pool mode)")
+    dev = C.cuda_device_of(q)
+    if q.dim() != 4:
+        raise ValueError(f"q must be [B, T, H, K], got {tuple(q.shape)}")
+    B, T = q.shape[0], q.shape[1]
+    if use_pool:
+        pool, idx = initial_state, initial_state_indices
+    else:
+        if state is None:
+            raise ValueError("either state or initial_state must be provided")
+        pool, idx = state, torch.arange(B, dtype=torch.int32, device=dev)
+    if not pool.is_contiguous():
+        raise ValueError("the state must be contiguous (k-last [.., HV, V, K])")
+    HV, V = v.shape[2], v.shape[3]
+    target = output
+    out = output if (output is not None and output.dtype == torch.bfloat16 and output.is_contiguous()
+                     and tuple(output.shape) == (B, T, HV, V)) else None
+    if out is None:
+        out = torch.empty((B, T, HV, V), dtype=torch.bfloat16, device=dev)
+    gdn_mtp.run_into(q, k, v, pool, idx, A_log, a, dt_bias, b, scale, out, pool,
+                     qk_l2norm=use_qk_l2norm, output_state_indices=output_state_indices)
+    if target is not None and target is not out:
+        target.copy_(out.view(target.shape))
+        out = target
+    return out, (initial_state if use_pool else state)

@@ -18,9 +18,11 @@ disable_state_update=None, use_qk_l2norm=True) -> (output, initial_state)``
     ``disable_state_update=None`` means True with a one-time warning.
 
 Shapes: q, k [B, T, H, 128] bf16; v [B, T, HV, 128] bf16; a, b [B, T, HV]
-bf16; A_log, dt_bias [HV] fp32; initial_state [pool, HV, 128, 128] fp32
-(k-last); initial_state_indices [B] int32/int64; intermediate_states_buffer
-[>= max slot + 1, >= T, HV, 128, 128] fp32; output [B, T, HV, 128] bf16.
+bf16; A_log, dt_bias [HV] fp32; initial_state [pool, HV, 128, 128] fp32 or
+bf16 (k-last; bf16 = the bf16-state form: advanced in fp32, rounded once when
+stored); initial_state_indices [B] int32/int64; intermediate_states_buffer
+[>= max slot + 1, >= T, HV, 128, 128] fp32 (fp32 pools only); output
+[B, T, HV, 128] bf16.
 
 An index outside [0, pool) is padding (flashinfer's -1): zero output, no state
 touched.  The other indices must be distinct.
@@ -59,9 +61,9 @@ def _validate(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, 
                          ("A_log", A_log, (HV,)), ("dt_bias", dt_bias, (HV,))):
         if tuple(t.shape) != shp:
             raise ValueError(f"{name} must be {shp}, got {tuple(t.shape)}")
-    if not isinstance(initial_state, torch.Tensor) or initial_state.dtype != f32 \
+    if not isinstance(initial_state, torch.Tensor) or initial_state.dtype not in (f32, bf) \
             or initial_state.device != dev:
-        raise TypeError("initial_state must be an fp32 tensor on the inputs' device")
+        raise TypeError("initial_state must be an fp32 or bf16 tensor on the inputs' device")
     if initial_state.dim() != 4 or tuple(initial_state.shape[1:]) != (HV, V, K):
         raise ValueError(f"initial_state must be [pool, {HV}, {V}, {K}], got {tuple(initial_state.shape)}")
     idx = initial_state_indices
@@ -70,6 +72,8 @@ def _validate(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, 
         raise ValueError(f"initial_state_indices must be an int32/int64 [{B}] tensor on {dev}")
     idx = idx.contiguous()
     steps = slots = 0
+    if buf is not None and initial_state.dtype != f32:
+        raise ValueError("intermediate_states_buffer needs an fp32 state pool")
     if buf is not None:
         if not isinstance(buf, torch.Tensor) or buf.dtype != f32 or buf.device != dev \
                 or not buf.is_contiguous():
@@ -81,11 +85,22 @@ def _validate(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, 
     return dev, (q, k, v, idx, A_log, a, dt_bias, b), (B, T, H, HV, K, V), (slots, steps)
 
 
-def _launch(dev, tensors, dims, pool_in, pool_out, scale, output, buf, slots, steps, l2norm):
+def _out_indices(out_idx, idx, B, dev):
+    if out_idx is None:
+        return None
+    if not isinstance(out_idx, torch.Tensor) or out_idx.device != dev or tuple(out_idx.shape) != (B,) \
+            or out_idx.dtype not in (torch.int32, torch.int64):
+        raise ValueError(f"output_state_indices must be an int32/int64 [{B}] tensor on {dev}")
+    return out_idx.to(idx.dtype).contiguous()
+
+
+def _launch(dev, tensors, dims, pool_in, pool_out, scale, output, buf, slots, steps, l2norm,
+            out_idx=None):
     q, k, v, idx, A_log, a, dt_bias, b = tensors
     B, T, H, HV, K, V = dims
     st = lib().gdn_mtp_fwd(
-        C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(pool_in), C.ptr(pool_out), C.ptr(idx),
+        C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(pool_in), C.ptr(pool_out),
+        int(pool_in.dtype == torch.bfloat16), C.ptr(idx), C.ptr(out_idx),
         int(idx.dtype == torch.int64), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias), C.ptr(b),
         C.normalize_scale(scale, K), B, T, H, HV, K, V, pool_in.shape[0], int(bool(l2norm)),
         C.ptr(output), C.ptr(buf), slots, steps, C.stream_handle(dev))
@@ -99,22 +114,25 @@ def _check_output(output, B, T, HV, V, dev):
 
 
 def run_into(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale,
-             output, final_state, intermediate_states_buffer=None, qk_l2norm: bool = False):
+             output, final_state, intermediate_states_buffer=None, qk_l2norm: bool = False,
+             output_state_indices=None):
     """Destination-passing form: writes ``output`` and ``final_state``
     (``final_state`` may be ``initial_state`` for an in-place update, or None
-    to leave every state as it is)."""
+    to leave every state as it is); ``output_state_indices`` redirects each
+    entry's final state to another slot."""
     dev, tensors, dims, (slots, steps) = _validate(
         q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, intermediate_states_buffer)
     B, T, H, HV, K, V = dims
     _check_output(output, B, T, HV, V, dev)
     if not initial_state.is_contiguous():
         raise ValueError("initial_state must be contiguous")
-    if final_state is not None and (final_state.dtype != torch.float32 or final_state.device != dev
+    if final_state is not None and (final_state.dtype != initial_state.dtype or final_state.device != dev
                                     or tuple(final_state.shape) != tuple(initial_state.shape)
                                     or not final_state.is_contiguous()):
-        raise ValueError("final_state must be a contiguous fp32 tensor shaped like initial_state")
+        raise ValueError("final_state must be a contiguous tensor shaped and typed like initial_state")
+    oidx = _out_indices(output_state_indices, tensors[3], B, dev)
     _launch(dev, tensors, dims, initial_state, final_state, scale, output,
-            intermediate_states_buffer, slots, steps, qk_l2norm)
+            intermediate_states_buffer, slots, steps, qk_l2norm, oidx)
     return output, final_state
 
 

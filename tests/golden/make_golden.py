@@ -46,15 +46,20 @@ PREFILL_CASES = [
     ("pre_gva4_extreme", [9, 3], 1, 4, 16, True, 1.0, 14, torch.int64),
 ]
 
-# (name, B, T, pool, H, HV, K, scale, seed, intermediate buffer, qk_l2norm)
+# (name, B, T, pool, H, HV, K, scale, seed, intermediate buffer, qk_l2norm, bf16 state)
 # qk_l2norm cases feed raw (unnormalised) q/k and normalise them the way
 # flashinfer's gated_delta_rule_mtp kernel does (x * rsqrt(sum(x^2) + 1e-6),
 # flashinfer/gdn_kernels/gdn_decode_mtp.py:359-360) before the template runs.
+# bf16-state cases (flashinfer/gdn_decode.py:206-260) hold the pool in bf16:
+# the template runs on the widened pool and its final state is rounded to
+# bf16 (nearest even), the state being fp32 in between.
 MTP_CASES = [
-    ("mtp_small", 3, 4, 5, 2, 4, 16, 0.0, 21, True, False),
-    ("mtp_k128", 2, 3, 3, 1, 2, 128, 0.0, 22, False, False),
-    ("mtp_gva4", 2, 2, 4, 1, 4, 32, 0.4, 23, True, False),
-    ("mtp_l2norm", 2, 3, 3, 1, 2, 32, 0.0, 24, True, True),
+    ("mtp_small", 3, 4, 5, 2, 4, 16, 0.0, 21, True, False, False),
+    ("mtp_k128", 2, 3, 3, 1, 2, 128, 0.0, 22, False, False, False),
+    ("mtp_gva4", 2, 2, 4, 1, 4, 32, 0.4, 23, True, False, False),
+    ("mtp_l2norm", 2, 3, 3, 1, 2, 32, 0.0, 24, True, True, False),
+    ("mtp_bf16state_t1", 3, 1, 4, 1, 2, 128, 0.0, 25, False, False, True),
+    ("mtp_bf16state_t3", 2, 3, 5, 2, 4, 32, 0.0, 26, False, False, True),
 ]
 
 
@@ -113,10 +118,14 @@ def main():
         out[f"{name}/out"] = _np(o)
         out[f"{name}/new_state"] = _np(s)
     from flashinfer.trace.templates.gdn import _gdn_mtp_reference
-    for name, B, T, pool, H, HV, K, scale, seed, inter, l2 in MTP_CASES:
+    for name, B, T, pool, H, HV, K, scale, seed, inter, l2, bf16_state in MTP_CASES:
         args = mtp_inputs(B, T, pool, H, HV, K, K, seed=seed, intermediate=inter)
         args[9] = scale
+        if bf16_state:
+            args[3] = args[3].to(torch.bfloat16)
         run_args = list(args[:10])
+        if bf16_state:
+            run_args[3] = args[3].float()
         if l2:
             g = torch.Generator().manual_seed(seed + 100)
             for i in (0, 1):
@@ -132,7 +141,7 @@ def main():
         o, s = _gdn_mtp_reference(*run_args, intermediate_states_buffer=buf)
         out[f"{name}/scale"] = np.float32(scale)
         out[f"{name}/out"] = _np(o)
-        out[f"{name}/new_state"] = _np(s)
+        out[f"{name}/new_state"] = _np(s.to(torch.bfloat16) if bf16_state else s)
         if buf is not None:
             out[f"{name}/intermediate"] = _np(buf)
     path = os.path.join(HERE, "gdn_golden.npz")

@@ -102,9 +102,9 @@ def test_prefill_rejects_bad_arguments(over, code):
 
 
 def _mtp(**over):
-    d = dict(q=16, k=16, v=16, pool_in=4096, pool_out=4096, idx=16, idx64=0, A_log=16, a=16,
-             dt_bias=16, b=16, scale=0.0, B=2, T=3, H=1, HV=2, K=128, V=128, pool=4, l2=0,
-             out=16, inter=None, inter_slots=0, steps=0, stream=None)
+    d = dict(q=16, k=16, v=16, pool_in=4096, pool_out=4096, bf16=0, idx=16, out_idx=None, idx64=0,
+             A_log=16, a=16, dt_bias=16, b=16, scale=0.0, B=2, T=3, H=1, HV=2, K=128, V=128, pool=4,
+             l2=0, out=16, inter=None, inter_slots=0, steps=0, stream=None)
     d.update(over)
     return _lib.lib().gdn_mtp_fwd(*d.values())
 
@@ -124,6 +124,10 @@ def _mtp(**over):
     (dict(idx=20, idx64=1), _lib.GDN_ERR_ALIGN),
     (dict(q=18), _lib.GDN_ERR_ALIGN),
     (dict(inter=4104, inter_slots=4, steps=3), _lib.GDN_ERR_ALIGN),
+    (dict(bf16=2), _lib.GDN_ERR_INVALID),
+    (dict(bf16=1, inter=4096, inter_slots=4, steps=3), _lib.GDN_ERR_INVALID),  # snapshots need fp32
+    (dict(out_idx=18), _lib.GDN_ERR_ALIGN),
+    (dict(pool_out=4096 + 512, bf16=1), _lib.GDN_ERR_INVALID),       # bf16 pool: 256 KiB, overlaps
     (dict(B=0), _lib.GDN_OK),                       # in place, nothing to do: no CUDA call
     (dict(T=0, pool_out=None), _lib.GDN_OK),
 ])

@@ -166,3 +166,109 @@ def test_mtp_empty_and_bad_args(cuda_device):
     with pytest.raises(ValueError):
         gdn_mtp.run(*args[:10], intermediate_states_buffer=torch.zeros((4, 1, 8, 128, 128),
                                                                        device=cuda_device))
+
+
+# ---- bf16 state, output slots and flashinfer's decode API ----
+
+def _bf16_tol(sol, ref):
+    """bf16 state: within one bf16 rounding step of the oracle's bf16 value."""
+    s, r = sol.float().cpu(), ref.float()
+    d = (s - r).abs()
+    assert sol.dtype == torch.bfloat16
+    assert bool((d <= 1e-7 + 2 ** -7 * r.abs()).all()), float(d.max())
+    assert float((d == 0).float().mean()) >= 0.97
+
+
+@pytest.mark.parametrize("B,T,pool,H,HV,seed", [
+    (64, 1, 96, 16, 32, 60),   # bf16-state decode at the benchmark heads
+    (8, 4, 12, 4, 8, 61),      # bf16-state MTP, contest heads
+    (5, 2, 5, 1, 4, 62),       # GVA 4, small grid
+])
+def test_mtp_bf16_state_matches_oracle(cuda_device, B, T, pool, H, HV, seed):
+    args = inputs.mtp_inputs(B, T, pool, H, HV, seed=seed)
+    args[3] = args[3].to(torch.bfloat16)
+    dargs = inputs.to_device(args, cuda_device)
+    o, s = gdn_mtp.run(*dargs[:10])
+    torch.cuda.synchronize()
+    ro, rs = oracle.mtp(*inputs.to_cpu(args[:10]))
+    assert s.dtype == torch.bfloat16 and rs.dtype == torch.bfloat16
+    assert_output_close(o.cpu(), ro)
+    _bf16_tol(s, rs)
+
+
+def test_mtp_golden_bf16_state(cuda_device):
+    z = np.load(GOLD)
+    name = "mtp_bf16state_t1"
+    args = []
+    for f in FIELDS:
+        a = z[f"{name}/{f}"]
+        bf = f in ("q", "k", "v", "a", "b", "initial_state")
+        args.append(bf16_from_u16(a) if bf else torch.from_numpy(np.array(a)))
+    o, s = gdn_mtp.run(*inputs.to_device(args, cuda_device), float(z[f"{name}/scale"]))
+    torch.cuda.synchronize()
+    assert_output_close(o.cpu(), bf16_from_u16(z[f"{name}/out"]))
+    _bf16_tol(s, bf16_from_u16(z[f"{name}/new_state"]))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_mtp_output_state_indices(cuda_device, dtype):
+    B, T, pool = 4, 2, 10
+    idx = [1, 3, -1, 6]
+    oidx = [7, 2, 5, 11]          # entry 3 writes out of range: no state write
+    args = inputs.mtp_inputs(B, T, pool, 4, 8, seed=63, indices=idx, idx_dtype=torch.int64)
+    args[3] = args[3].to(dtype)
+    dargs = inputs.to_device(args, cuda_device)
+    out_idx = torch.tensor(oidx, dtype=torch.int32, device=cuda_device)
+    pool_dev = dargs[3].clone()
+    out = torch.empty((B, T, 8, 128), dtype=torch.bfloat16, device=cuda_device)
+    gdn_mtp.run_into(*dargs[:3], pool_dev, *dargs[4:10], out, pool_dev, output_state_indices=out_idx)
+    torch.cuda.synchronize()
+    ro, rs = oracle.mtp(*inputs.to_cpu(args[:10]), output_state_indices=out_idx.cpu())
+    assert_output_close(out.cpu(), ro)
+    if dtype == torch.bfloat16:
+        _bf16_tol(pool_dev, rs)
+    else:
+        assert_state_close(pool_dev.cpu(), rs)
+    for slot in (0, 1, 3, 4, 6, 8, 9):   # read-only or untouched slots keep their value
+        assert torch.equal(pool_dev[slot].cpu(), args[3][slot])
+
+
+@pytest.mark.parametrize("dtype,T", [(torch.float32, 1), (torch.bfloat16, 1), (torch.bfloat16, 3)])
+def test_decode_pretranspose_api(cuda_device, dtype, T):
+    B, H, HV = 6, 4, 8
+    args = inputs.mtp_inputs(B, T, B, H, HV, seed=64, indices=list(range(B)))
+    g = torch.Generator().manual_seed(65)
+    args[0] = (torch.randn(args[0].shape, generator=g) * 2.0).to(torch.bfloat16)
+    args[1] = (torch.randn(args[1].shape, generator=g) * 2.0).to(torch.bfloat16)
+    args[3] = args[3].to(dtype)
+    ro, rs = oracle.mtp(*inputs.to_cpu(args[:10]), qk_l2norm=True)
+    d = inputs.to_device(args, cuda_device)
+    state = d[3].clone()
+    o, ret = gdn_decode.gated_delta_rule_decode_pretranspose(
+        d[0], d[1], d[2], state, d[5], d[6], d[7], d[8])        # scale=None, use_qk_l2norm=True
+    torch.cuda.synchronize()
+    assert ret is state and o.shape == (B, T, HV, 128)
+    assert_output_close(o.cpu(), ro)
+    if dtype == torch.bfloat16:
+        _bf16_tol(state, rs)
+    else:
+        assert_state_close(state.cpu(), rs)
+
+
+def test_decode_pretranspose_pool_mode(cuda_device):
+    B, pool, H, HV = 5, 9, 16, 32
+    idx = [4, -1, 0, 7, 2]
+    args = inputs.mtp_inputs(B, 1, pool, H, HV, seed=66, indices=idx, idx_dtype=torch.int64)
+    args[3] = args[3].to(torch.bfloat16)
+    d = inputs.to_device(args, cuda_device)
+    pool_dev = d[3].clone()
+    out = torch.empty((B, 1, HV, 128), dtype=torch.bfloat16, device=cuda_device)
+    o, ret = gdn_decode.gated_delta_rule_decode_pretranspose(
+        d[0], d[1], d[2], None, d[5], d[6], d[7], d[8], scale=0.0, output=out, use_qk_l2norm=False,
+        initial_state=pool_dev, initial_state_indices=d[4])
+    torch.cuda.synchronize()
+    assert o is out and ret is pool_dev
+    ro, rs = oracle.mtp(*inputs.to_cpu(args[:10]))
+    assert_output_close(out.cpu(), ro)
+    assert not out[1].float().any()
+    _bf16_tol(pool_dev, rs)

@@ -24,27 +24,39 @@ def _load():
     cases = {}
     for key in z.files:
         name, field = key.split("/")
-        cases.setdefault(name, {})[field] = z[key]
+        cases.setdefault(name, {"__name__": name})[field] = z[key]
     return cases
 
 
 CASES = _load()
 BF16_FIELDS = {"q", "k", "v", "a", "b", "out"}
+BF16_STATE_CASES = {"mtp_bf16state_t1", "mtp_bf16state_t3"}
 
 
 def _t(case, field):
     if field not in case:
         return None
     arr = case[field]
-    if field in BF16_FIELDS:
+    if field in BF16_FIELDS or (field in ("initial_state", "new_state") and _name(case) in BF16_STATE_CASES):
         return bf16_from_u16(arr)
     return torch.from_numpy(np.array(arr))
+
+
+def _name(case):
+    return case.get("__name__")
 
 
 def _check(o, s, case):
     ref_o = _t(case, "out").float()
     ref_s = _t(case, "new_state")
     o = o.float()
+    if ref_s.dtype == torch.bfloat16:
+        # bf16 state: identical except where the fp32 value sits on a rounding boundary
+        d = (s.float() - ref_s.float()).abs()
+        assert s.dtype == torch.bfloat16
+        assert float((d <= 1e-7 + 2 ** -7 * ref_s.float().abs()).float().mean()) == 1.0
+        assert float((d == 0).float().mean()) >= 0.98
+        s, ref_s = ref_s.float(), ref_s.float()
     # state: fp32 vs fp32 in another summation order
     err = (s - ref_s).abs()
     assert float(err.max()) <= 1e-5 * float(ref_s.abs().max()) + 1e-6, float(err.max())
