@@ -43,7 +43,7 @@ extern "C" {
 #define GDN_ERR_TOO_LARGE 6   /* needs more than gdn_prefill_fwd_noalloc's fixed scratch */
 
 /* Version of this ABI (bumped on any signature change or addition; 3 adds
- * gdn_mtp_fwd). */
+ * gdn_mtp_fwd and gdn_prefill_fwd_checkpointed). */
 int gdn_abi_version(void);
 
 /* Human-readable text for a status code. */
@@ -95,6 +95,26 @@ int gdn_prefill_fwd(const void *q, const void *k, const void *v, const float *st
                     const void *cu_seqlens, int cu_seqlens_is_int64, int N, int T,
                     float scale, int H, int HV, int K, int V, void *out, float *new_state,
                     void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * gdn_prefill_fwd that also stores state checkpoints: the state of sequence n
+ * after its first every, 2*every, ... tokens (every = checkpoint_every_n_tokens,
+ * a positive multiple of 64) goes to
+ * state_checkpoints[checkpoint_cu_starts[n] + i] ([num_checkpoints, HV, V, K]
+ * fp32, k-last, 16-byte aligned), i = 0 .. len_n / every - 1, so
+ * checkpoint_cu_starts ([N + 1] int64, device) must give sequence n
+ * len_n / every slots.  These are the arguments and the layout of flashinfer's
+ * chunk_gated_delta_rule (flashinfer/gdn_prefill.py:113-115,161-174), whose
+ * Blackwell kernel stores the same states.  An index outside a sequence's
+ * range or the buffer skips the store.  Workspace as gdn_prefill_fwd.
+ */
+int gdn_prefill_fwd_checkpointed(const void *q, const void *k, const void *v, const float *state,
+                                 const float *A_log, const void *a, const float *dt_bias, const void *b,
+                                 const void *cu_seqlens, int cu_seqlens_is_int64, int N, int T,
+                                 float scale, int H, int HV, int K, int V, void *out, float *new_state,
+                                 float *state_checkpoints, const int64_t *checkpoint_cu_starts,
+                                 long long num_checkpoints, int checkpoint_every_n_tokens,
+                                 void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Workspace bytes gdn_prefill_fwd needs for (N, T, H, HV): 0 when the call

@@ -128,11 +128,15 @@ int gdn_oracle_decode(const float *q, const float *k, const float *v, const floa
     return 0;
 }
 
+/* ckpt (optional): the state after tokens every, 2*every, ... of sequence n
+ * is copied to ckpt[ckpt_cu[n] + i] (flashinfer's chunk_gated_delta_rule
+ * checkpoints, flashinfer/gdn_prefill.py:161-174). */
 int gdn_oracle_prefill(const float *q, const float *k, const float *v, const float *state,
                        const float *A_log, const float *a, const float *dt_bias,
                        const float *b, const int64_t *cu_seqlens, int N, int T, float scale,
                        int H, int HV, int K, int V, uint16_t *out_bf16, float *new_state,
-                       int nthreads) {
+                       float *ckpt, const int64_t *ckpt_cu, int every, int nthreads) {
+    if (ckpt && (every <= 0 || !ckpt_cu)) return 1;
     if (N < 0 || T < 0 || H <= 0 || HV <= 0 || K <= 0 || V <= 0 || HV % H) return 1;
     if (N > 0 && (cu_seqlens[0] < 0 || cu_seqlens[N] > T)) return 1;
     for (int n = 0; n < N; ++n)
@@ -162,6 +166,10 @@ int gdn_oracle_prefill(const float *q, const float *k, const float *v, const flo
                       v + ((size_t)t * HV + h) * V, g, beta, scale, K, V, o);
             for (int vi = 0; vi < V; ++vi)
                 out_bf16[((size_t)t * HV + h) * V + vi] = f32_to_bf16_rne(o[vi]);
+            if (ckpt && (t - t0 + 1) % every == 0) {
+                int64_t ci = ckpt_cu[n] + (t - t0 + 1) / every - 1;
+                memcpy(ckpt + ((size_t)ci * HV + h) * V * K, S, sizeof(float) * (size_t)V * K);
+            }
         }
         free(o);
     }

@@ -14,7 +14,9 @@ can hand the same seeded inputs to the oracle and to the CUDA path:
   definition ``gdn_mtp`` (gdn.py:378-465), with out-of-range indices as
   padding.
 
-Both return ``(output bf16, new_state fp32)``.  ``threads`` <= 0 uses every core.
+All return ``(output bf16, new_state fp32)``; ``prefill`` with
+``checkpoint_every_n_tokens > 0`` adds the state checkpoints.  ``threads``
+<= 0 uses every core.
 """
 from __future__ import annotations
 
@@ -58,7 +60,7 @@ def _load():
         _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i64p,
         ctypes.c_int, ctypes.c_int, ctypes.c_float,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-        _u16p, _f32p, ctypes.c_int,
+        _u16p, _f32p, _f32p, _i64p, ctypes.c_int, ctypes.c_int,
     ]
     lib.gdn_oracle_mtp.restype = ctypes.c_int
     lib.gdn_oracle_mtp.argtypes = [
@@ -107,7 +109,18 @@ def decode(q, k, v, state, A_log, a, dt_bias, b, scale, threads: int = 0, return
     return (o, new_state, out32) if return_f32 else (o, new_state)
 
 
-def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: int = 0):
+def checkpoint_cu_starts(cu_seqlens, every: int) -> torch.Tensor:
+    """[N + 1] int64 cumulative checkpoint counts: sequence n gets len_n // every."""
+    cu = cu_seqlens.detach().to("cpu", torch.int64)
+    out = torch.zeros(cu.numel(), dtype=torch.int64)
+    out[1:] = torch.cumsum((cu[1:] - cu[:-1]).clamp_min(0) // every, 0)
+    return out
+
+
+def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: int = 0,
+            checkpoint_every_n_tokens: int = 0):
+    """Returns (output, new_state), plus the checkpoints [total, HV, V, K] when
+    checkpoint_every_n_tokens > 0."""
     lib = _load()
     T, H, K = q.shape
     HV, V = v.shape[1], v.shape[2]
@@ -118,13 +131,21 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: in
     Af, af, dtf, bf = _f32(A_log), _f32(a), _f32(dt_bias), _f32(b)
     out = torch.empty((T, HV, V), dtype=torch.int16)
     new_state = torch.empty((N, HV, V, K), dtype=torch.float32)
+    every = int(checkpoint_every_n_tokens)
+    ckpt = ckpt_cu = None
+    if every > 0:
+        ckpt_cu = checkpoint_cu_starts(cu, every)
+        ckpt = torch.zeros((int(ckpt_cu[-1]), HV, V, K), dtype=torch.float32)
     rc = lib.gdn_oracle_prefill(
         _ptr(qf, _f32p), _ptr(kf, _f32p), _ptr(vf, _f32p), _ptr(sf, _f32p),
         _ptr(Af, _f32p), _ptr(af, _f32p), _ptr(dtf, _f32p), _ptr(bf, _f32p), _ptr(cu, _i64p),
         N, T, _scale(scale, K), H, HV, K, V,
-        _ptr(out, _u16p), _ptr(new_state, _f32p), int(threads))
+        _ptr(out, _u16p), _ptr(new_state, _f32p), _ptr(ckpt, _f32p), _ptr(ckpt_cu, _i64p), every,
+        int(threads))
     if rc != 0:
         raise ValueError(f"gdn_oracle_prefill rejected its arguments (rc={rc})")
+    if every > 0:
+        return out.view(torch.bfloat16), new_state, ckpt
     return out.view(torch.bfloat16), new_state
 
 

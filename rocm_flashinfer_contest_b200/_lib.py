@@ -30,6 +30,9 @@ SIGNATURES = {
                             _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "gdn_prefill_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                              _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "gdn_prefill_fwd_checkpointed": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
+                                          _i, _i, _f, _i, _i, _i, _i, _vp, _vp,
+                                          _vp, _vp, ctypes.c_longlong, _i, _vp, ctypes.c_size_t, _vp]),
     "gdn_prefill_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i]),
     "gdn_prefill_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                                      _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp]),

@@ -29,13 +29,16 @@ extern "C" size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV) {
     return gdn::prefill_workspace_bytes(N, T, H, HV);
 }
 
-extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state,
-                               const float* A_log, const void* a, const float* dt_bias,
-                               const void* b, const void* cu_seqlens, int cu_seqlens_is_int64,
-                               int N, int T, float scale, int H, int HV, int K, int V, void* out,
-                               float* new_state, void* workspace, size_t workspace_bytes,
-                               void* stream) {
+static int prefill_impl(const void* q, const void* k, const void* v, const float* state,
+                        const float* A_log, const void* a, const float* dt_bias, const void* b,
+                        const void* cu_seqlens, int cu_seqlens_is_int64, int N, int T, float scale,
+                        int H, int HV, int K, int V, void* out, float* new_state, float* ckpt,
+                        const int64_t* ckpt_cu, long long ckpt_total, int ckpt_every, void* workspace,
+                        size_t workspace_bytes, void* stream) {
     if (N < 0 || T < 0 || H <= 0 || HV <= 0) return GDN_ERR_INVALID;
+    if (ckpt != nullptr && (ckpt_every <= 0 || ckpt_every % 64 != 0 || !ckpt_cu || ckpt_total < 0))
+        return GDN_ERR_INVALID;
+    if (ckpt != nullptr && (!gdn_aligned(ckpt, 16) || !gdn_aligned(ckpt_cu, 8))) return GDN_ERR_ALIGN;
     if (cu_seqlens_is_int64 != 0 && cu_seqlens_is_int64 != 1) return GDN_ERR_INVALID;
     if (K != gdn::kDim || V != gdn::kDim || HV % H != 0) return GDN_ERR_UNSUPPORTED;
     if (N == 0 && T == 0) return GDN_OK;
@@ -68,6 +71,10 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
     p.H = H;
     p.HV = HV;
     p.rep = HV / H;
+    p.ckpt = ckpt;
+    p.ckpt_cu = reinterpret_cast<const long long*>(ckpt_cu);
+    p.ckpt_total = ckpt_total;
+    p.ckpt_every = ckpt != nullptr ? ckpt_every : 0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (N == 0) {
         // no sequence: every token is uncovered, its output is zero
@@ -83,4 +90,28 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
         gdn::launch_prefill_recurrent(p, st);
     }
     return gdn_launch_status();
+}
+
+extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state,
+                               const float* A_log, const void* a, const float* dt_bias,
+                               const void* b, const void* cu_seqlens, int cu_seqlens_is_int64,
+                               int N, int T, float scale, int H, int HV, int K, int V, void* out,
+                               float* new_state, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+    return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64, N, T, scale,
+                        H, HV, K, V, out, new_state, nullptr, nullptr, 0, 0, workspace, workspace_bytes, stream);
+}
+
+extern "C" int gdn_prefill_fwd_checkpointed(const void* q, const void* k, const void* v, const float* state,
+                                            const float* A_log, const void* a, const float* dt_bias,
+                                            const void* b, const void* cu_seqlens, int cu_seqlens_is_int64,
+                                            int N, int T, float scale, int H, int HV, int K, int V, void* out,
+                                            float* new_state, float* state_checkpoints,
+                                            const int64_t* checkpoint_cu_starts, long long num_checkpoints,
+                                            int checkpoint_every_n_tokens, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+    if (!state_checkpoints) return GDN_ERR_INVALID;
+    return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64, N, T, scale,
+                        H, HV, K, V, out, new_state, state_checkpoints, checkpoint_cu_starts, num_checkpoints,
+                        checkpoint_every_n_tokens, workspace, workspace_bytes, stream);
 }

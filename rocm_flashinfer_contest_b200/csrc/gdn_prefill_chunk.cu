@@ -712,6 +712,14 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
             G::st(tl + TM_S + cb, sv);
 #pragma unroll
             for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, G::b_off(cb + c8, row, kDim), sv + c8);
+            // checkpoint: a full chunk that ends on a multiple of ckpt_every
+            if (p.ckpt != nullptr && len == C && (C * (j + 1)) % p.ckpt_every == 0) {
+                float* cd = ckpt_dst(p, n, hv, C * (j + 1));
+                if (cd != nullptr) {
+#pragma unroll
+                    for (int e = 0; e < HALF; ++e) __stcs(cd + (size_t)(v0 + cb + e) * kDim + row, sv[e]);
+                }
+            }
         }
         // the next chunk's v rows (copied by all threads) become visible at this barrier;
         // the CTA stops here if any wait of this chunk timed out

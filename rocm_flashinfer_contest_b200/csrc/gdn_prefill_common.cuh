@@ -20,7 +20,25 @@ struct PrefillParams {
     float scale;
     int cu_is_int64;
     int N, T, H, HV, rep;    // rep = HV / H
+    // optional state checkpoints (flashinfer's chunk_gated_delta_rule,
+    // flashinfer/gdn_prefill.py:113-115,161-174): the state after tokens
+    // every, 2*every, ... of sequence n goes to ckpt[ckpt_cu[n] + i]
+    float* ckpt;               // [ckpt_total, HV, V, K] or null
+    const long long* ckpt_cu;  // [N + 1]
+    long long ckpt_total;
+    int ckpt_every;            // > 0, a multiple of 64, when ckpt is set
 };
+
+// Destination of the checkpoint after `done` tokens of sequence n (done a
+// multiple of ckpt_every), or null when the index falls outside the
+// sequence's range or the buffer (a malformed ckpt_cu cannot send a store
+// out of bounds).
+__device__ __forceinline__ float* ckpt_dst(const PrefillParams& p, int n, int hv, long long done) {
+    const long long first = p.ckpt_cu[n], end = p.ckpt_cu[n + 1];
+    const long long i = first + done / p.ckpt_every - 1;
+    if (i < first || i >= end || i < 0 || i >= p.ckpt_total) return nullptr;
+    return p.ckpt + ((size_t)i * p.HV + hv) * kDim * kDim;
+}
 
 __device__ __forceinline__ long long load_cu(const PrefillParams& p, int i) {
     return p.cu_is_int64 ? static_cast<const long long*>(p.cu_seqlens)[i]

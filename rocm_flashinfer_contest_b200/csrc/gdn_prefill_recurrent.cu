@@ -8,7 +8,8 @@
 // warps owns 16 rows (4 per warp, 8 lanes per 512-byte row, as in the decode
 // kernel), so a head is split over 8 CTAs and nothing but the inputs and the
 // outputs moves through memory.  The next token's q/k/v/gates are loaded
-// while the current token is processed.
+// while the current token is processed.  With checkpoints enabled the rows
+// are also stored after every `ckpt_every` tokens.
 #include "gdn_common.cuh"
 #include "gdn_prefill_common.cuh"
 
@@ -79,6 +80,7 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
 
     TokenRaw nxt;
     load_token(p, t0, hq, hv, row, sub, nxt);
+    int until_ckpt = p.ckpt_every;  // tokens left before the next checkpoint
     for (long long t = t0; t < t1; ++t) {
         TokenRaw cur = nxt;
         if (t + 1 < t1) load_token(p, t + 1, hq, hv, row, sub, nxt);
@@ -111,6 +113,15 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
             s[j].y = fmaf(g, s[j].y, delta * kf[j].y);
             s[j].z = fmaf(g, s[j].z, delta * kf[j].z);
             s[j].w = fmaf(g, s[j].w, delta * kf[j].w);
+        }
+        if (p.ckpt != nullptr && --until_ckpt == 0) {
+            until_ckpt = p.ckpt_every;
+            float* cd = ckpt_dst(p, n, hv, t - t0 + 1);
+            if (cd != nullptr) {
+                float* dst = cd + (size_t)row * kDim + 4 * sub;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) __stcs(reinterpret_cast<float4*>(dst + 32 * j), s[j]);
+            }
         }
     }
 #pragma unroll

@@ -14,6 +14,14 @@ solution (solutions/gdn_prefill/main.py:31-84) and the contest definition
     output   [T, HV, 128] bf16         new_state [N, HV, 128, 128] fp32
 
 A zero-length sequence gets an all-zero final state (gdn.py:234-235).
+
+State checkpoints (keyword-only, the names and rules of flashinfer's
+chunk_gated_delta_rule, flashinfer/gdn_prefill.py:113-115,161-214):
+``state_checkpoints`` [total, HV, 128, 128] fp32, ``checkpoint_cu_starts``
+[N + 1] int64 (sequence n owns ``len_n // every`` slots, see
+``checkpoint_cu_starts_for``) and ``checkpoint_every_n_tokens`` (a positive
+multiple of 64, 0 = off): the state after tokens every, 2*every, ... of each
+sequence is written to its slots.
 Inputs are never modified; ``run_into`` is the destination-passing form and
 accepts ``new_state is state``.  The chunked kernels' workspace
 (gdn_prefill_workspace_bytes) comes from torch's caching allocator, so a
@@ -64,10 +72,46 @@ def _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens):
     return dev, (q, k, v, state, A_log, a, dt_bias, b, cu_seqlens), (T, N, H, HV, K, V)
 
 
-def run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state):
+def checkpoint_cu_starts_for(cu_seqlens: torch.Tensor, every: int) -> torch.Tensor:
+    """``checkpoint_cu_starts`` for ``cu_seqlens``: [N + 1] int64 on the same
+    device, sequence n getting ``len_n // every`` slots."""
+    cu = cu_seqlens.to(torch.int64)
+    out = torch.zeros_like(cu)
+    out[1:] = torch.cumsum((cu[1:] - cu[:-1]).clamp_min(0) // every, 0)
+    return out
+
+
+def _validate_checkpoints(state_checkpoints, checkpoint_cu_starts, every, N, HV, K, dev):
+    every = int(every)
+    if every < 0:
+        raise ValueError(f"checkpoint_every_n_tokens must be non-negative, got {every}")
+    if every == 0:
+        if state_checkpoints is not None or checkpoint_cu_starts is not None:
+            raise ValueError("state_checkpoints and checkpoint_cu_starts must be None "
+                             "when checkpoint_every_n_tokens == 0")
+        return None
+    if every % 64 != 0:
+        raise ValueError(f"checkpoint_every_n_tokens must be a multiple of the chunk size (64), got {every}")
+    if state_checkpoints is None or checkpoint_cu_starts is None:
+        raise ValueError("state_checkpoints and checkpoint_cu_starts must both be provided "
+                         "when checkpoint_every_n_tokens > 0")
+    if state_checkpoints.dtype != torch.float32 or state_checkpoints.device != dev \
+            or state_checkpoints.dim() != 4 or tuple(state_checkpoints.shape[1:]) != (HV, K, K) \
+            or not state_checkpoints.is_contiguous():
+        raise ValueError(f"state_checkpoints must be a contiguous fp32 [*, {HV}, {K}, {K}] tensor on {dev}")
+    if checkpoint_cu_starts.dtype != torch.int64 or checkpoint_cu_starts.device != dev \
+            or tuple(checkpoint_cu_starts.shape) != (N + 1,):
+        raise ValueError(f"checkpoint_cu_starts must be an int64 [{N + 1}] tensor on {dev}")
+    return state_checkpoints, checkpoint_cu_starts.contiguous(), every
+
+
+def run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, *,
+             state_checkpoints=None, checkpoint_cu_starts=None, checkpoint_every_n_tokens: int = 0):
     """Destination-passing prefill into ``output`` [T,HV,V] bf16 and
     ``new_state`` [N,HV,V,K] fp32 (``new_state`` may be ``state``)."""
     dev, args, (T, N, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
+    ck = _validate_checkpoints(state_checkpoints, checkpoint_cu_starts, checkpoint_every_n_tokens,
+                               N, HV, K, dev)
     q, k, v, state, A_log, a, dt_bias, b, cu = args
     if output.dtype != torch.bfloat16 or tuple(output.shape) != (T, HV, V) \
             or not output.is_contiguous() or output.device != dev:
@@ -78,17 +122,29 @@ def run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, ne
     scale = C.normalize_scale(scale, K)
     ws_bytes = lib().gdn_prefill_workspace_bytes(N, T, H, HV)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
-    st = lib().gdn_prefill_fwd(
-        C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(state), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias),
-        C.ptr(b), C.ptr(cu), 1 if cu.dtype == torch.int64 else 0, N, T, scale, H, HV, K, V,
-        C.ptr(output), C.ptr(new_state), C.ptr(ws), ws_bytes, C.stream_handle(dev))
-    check("gdn_prefill_fwd", st)
+    if ck is None:
+        st = lib().gdn_prefill_fwd(
+            C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(state), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias),
+            C.ptr(b), C.ptr(cu), 1 if cu.dtype == torch.int64 else 0, N, T, scale, H, HV, K, V,
+            C.ptr(output), C.ptr(new_state), C.ptr(ws), ws_bytes, C.stream_handle(dev))
+        check("gdn_prefill_fwd", st)
+    else:
+        ckpt, ckpt_cu, every = ck
+        st = lib().gdn_prefill_fwd_checkpointed(
+            C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(state), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias),
+            C.ptr(b), C.ptr(cu), 1 if cu.dtype == torch.int64 else 0, N, T, scale, H, HV, K, V,
+            C.ptr(output), C.ptr(new_state), C.ptr(ckpt), C.ptr(ckpt_cu), ckpt.shape[0], every,
+            C.ptr(ws), ws_bytes, C.stream_handle(dev))
+        check("gdn_prefill_fwd_checkpointed", st)
     return output, new_state
 
 
-def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale):
+def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *,
+        state_checkpoints=None, checkpoint_cu_starts=None, checkpoint_every_n_tokens: int = 0):
     """Contest entry point; see the module docstring."""
     dev, _, (T, N, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
     output = torch.empty((T, HV, V), dtype=torch.bfloat16, device=dev)
     new_state = torch.empty((N, HV, V, K), dtype=torch.float32, device=dev)
-    return run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state)
+    return run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
+                    state_checkpoints=state_checkpoints, checkpoint_cu_starts=checkpoint_cu_starts,
+                    checkpoint_every_n_tokens=checkpoint_every_n_tokens)

@@ -46,6 +46,12 @@ PREFILL_CASES = [
     ("pre_gva4_extreme", [9, 3], 1, 4, 16, True, 1.0, 14, torch.int64),
 ]
 
+# (name, seqlens, checkpoint_every_n_tokens, seed); H = 1, HV = 2, K = V = 16
+CKPT_CASES = [
+    ("ckpt_every64", [130, 0, 200, 64], 64, 15),
+    ("ckpt_every128", [300, 127, 128], 128, 16),
+]
+
 # (name, B, T, pool, H, HV, K, scale, seed, intermediate buffer, qk_l2norm, bf16 state)
 # qk_l2norm cases feed raw (unnormalised) q/k and normalise them the way
 # flashinfer's gated_delta_rule_mtp kernel does (x * rsqrt(sum(x^2) + 1e-6),
@@ -117,6 +123,33 @@ def main():
         out[f"{name}/scale"] = np.float32(scale)
         out[f"{name}/out"] = _np(o)
         out[f"{name}/new_state"] = _np(s)
+    # state checkpoints (flashinfer's chunk_gated_delta_rule, gdn_prefill.py:161-174):
+    # checkpoint i of sequence n is the template's final state over the
+    # sequence's first (i + 1) * every tokens
+    for name, lens, every, seed in CKPT_CASES:
+        args = prefill_inputs(lens, 1, 2, 16, 16, seed=seed, with_state=True, cu_dtype=torch.int64)
+        args[9] = 0.0
+        keys = ["q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens"]
+        for kname, t in zip(keys, args[:9]):
+            out[f"{name}/{kname}"] = _np(t)
+        o, s = _gdn_prefill_reference(*args)
+        out[f"{name}/scale"] = np.float32(0.0)
+        out[f"{name}/out"] = _np(o)
+        out[f"{name}/new_state"] = _np(s)
+        cu = args[8].tolist()
+        ck, starts = [], [0]
+        for n in range(len(lens)):
+            t0 = cu[n]
+            for i in range(lens[n] // every):
+                t1 = t0 + (i + 1) * every
+                sub = [args[0][t0:t1], args[1][t0:t1], args[2][t0:t1], args[3][n:n + 1], args[4],
+                       args[5][t0:t1], args[6], args[7][t0:t1],
+                       torch.tensor([0, t1 - t0], dtype=torch.int64), 0.0]
+                ck.append(_gdn_prefill_reference(*sub)[1][0])
+            starts.append(len(ck))
+        out[f"{name}/checkpoints"] = _np(torch.stack(ck))
+        out[f"{name}/checkpoint_cu_starts"] = np.array(starts, dtype=np.int64)
+        out[f"{name}/every"] = np.int32(every)
     from flashinfer.trace.templates.gdn import _gdn_mtp_reference
     for name, B, T, pool, H, HV, K, scale, seed, inter, l2, bf16_state in MTP_CASES:
         args = mtp_inputs(B, T, pool, H, HV, K, K, seed=seed, intermediate=inter)

@@ -70,6 +70,7 @@ def test_golden_file_present():
     assert len([c for c in CASES if c.startswith("dec_")]) >= 4
     assert len([c for c in CASES if c.startswith("pre_")]) >= 4
     assert len([c for c in CASES if c.startswith("mtp_")]) >= 4
+    assert len([c for c in CASES if c.startswith("ckpt_")]) >= 2
 
 
 @pytest.mark.parametrize("name", sorted(c for c in CASES if c.startswith("dec_")))
@@ -129,6 +130,20 @@ def test_oracle_mtp_padding_rule():
     idx_pad[1] = pool.shape[0]  # one past the end is padding too
     o2, s2 = oracle.mtp(*args[:4], idx_pad, *args[5:], float(c["scale"]))
     assert torch.equal(o2, o) and torch.equal(s2, s)
+
+
+@pytest.mark.parametrize("name", sorted(c for c in CASES if c.startswith("ckpt_")))
+def test_oracle_prefill_checkpoints_match_reference(name):
+    c = CASES[name]
+    args = [_t(c, f) for f in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens")]
+    every = int(c["every"])
+    o, s, ck = oracle.prefill(*args, float(c["scale"]), checkpoint_every_n_tokens=every)
+    _check(o, s, c)
+    assert torch.equal(oracle.checkpoint_cu_starts(args[8], every),
+                       torch.from_numpy(c["checkpoint_cu_starts"]))
+    ref = _t(c, "checkpoints")
+    assert ck.shape == ref.shape
+    assert float((ck - ref).abs().max()) <= 1e-5 * float(ref.abs().max()) + 1e-6
 
 
 def test_golden_covers_edge_cases():

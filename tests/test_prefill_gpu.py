@@ -135,3 +135,45 @@ def test_prefill_strong_decay_and_saturated_gates(cuda_device, path):
     args[5] = pat_a.repeat(T).view(T, 8).to(torch.bfloat16)
     args[7] = pat_b.repeat(T).view(T, 8).to(torch.bfloat16)
     _check(args, cuda_device)
+
+
+# ---- state checkpoints (flashinfer's chunk_gated_delta_rule checkpoint arguments) ----
+
+@pytest.mark.parametrize("lens,H,HV,every", [
+    ([130, 0, 200, 64], 4, 8, 64),        # tails, an empty sequence, an exact multiple
+    ([300, 127, 128], 4, 8, 128),         # a sequence shorter than `every`
+    ([1000, 513], 16, 32, 192),           # benchmark heads, every = 3 chunks
+    ([640], 4, 8, 64),                    # last checkpoint == final state
+])
+def test_prefill_checkpoints(cuda_device, path, lens, H, HV, every):
+    args = inputs.prefill_inputs(lens, H, HV, seed=sum(lens) + every, with_state=True,
+                                 cu_dtype=torch.int64)
+    dargs = inputs.to_device(args, cuda_device)
+    starts = gdn_prefill.checkpoint_cu_starts_for(dargs[8], every)
+    total = int(starts[-1])
+    ck = torch.full((total, HV, 128, 128), 7.0, device=cuda_device)
+    o, s = gdn_prefill.run(*dargs, state_checkpoints=ck, checkpoint_cu_starts=starts,
+                           checkpoint_every_n_tokens=every)
+    torch.cuda.synchronize()
+    ro, rs, rck = oracle.prefill(*inputs.to_cpu(args), checkpoint_every_n_tokens=every)
+    assert total == rck.shape[0] == sum(L // every for L in lens)
+    assert_output_close(o.cpu(), ro)
+    assert_state_close(s.cpu(), rs)
+    assert_state_close(ck.cpu(), rck, what="checkpoints")
+    # a sequence whose length is a multiple of `every` ends on its final state
+    st = starts.tolist()
+    for n, L in enumerate(lens):
+        if L and L % every == 0:
+            assert torch.equal(ck[st[n + 1] - 1], s[n])
+
+
+def test_prefill_checkpoint_arguments(cuda_device):
+    args = inputs.to_device(inputs.prefill_inputs([128], 4, 8, seed=5), cuda_device)
+    starts = gdn_prefill.checkpoint_cu_starts_for(args[8], 64)
+    ck = torch.zeros((2, 8, 128, 128), device=cuda_device)
+    with pytest.raises(ValueError):
+        gdn_prefill.run(*args, state_checkpoints=ck, checkpoint_cu_starts=starts, checkpoint_every_n_tokens=96)
+    with pytest.raises(ValueError):
+        gdn_prefill.run(*args, state_checkpoints=ck, checkpoint_every_n_tokens=64)
+    with pytest.raises(ValueError):
+        gdn_prefill.run(*args, state_checkpoints=ck, checkpoint_cu_starts=starts)
