@@ -217,6 +217,12 @@ def timed_steps(fn, steps, flush, stream):
     return [s.elapsed_time(e) for s, e in evs]
 
 
+def _stats(ms):
+    """This rank's per-step device times: mean, median, min and max (ms)."""
+    return {"mean": round(statistics.mean(ms), 5), "median": round(statistics.median(ms), 5),
+            "min": round(min(ms), 5), "max": round(max(ms), 5), "n": len(ms)}
+
+
 def bench_ours(args, rank, world, local):
     from rocm_flashinfer_contest_b200 import gdn_decode, gdn_mtp, gdn_prefill, inputs, partition
 
@@ -369,6 +375,7 @@ def bench_ours(args, rank, world, local):
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(dec_step_ms, 5),
+        "step_ms_stats": _stats(dec_ms),
         "us_per_step": round(dec_step_ms * 1e3, 2),
         "higher_is_better": True,
         "scaling": "weak",
@@ -397,6 +404,7 @@ def bench_ours(args, rank, world, local):
             "metric": "gdn_prefill tokens/s at T=8192 (1 sequence, zero state)",
             "value": round(PREFILL_T * world / (pre_step_ms * 1e-3), 1), "unit": "tokens/s",
             "ms_per_step": round(pre_step_ms, 4),
+            "step_ms_stats": _stats(pre_ms),
             "roofline": {"bound": "tensor", "achieved": round(pre_achieved, 3),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(pre_achieved / peaks["bf16_tflops"], 5),
@@ -408,7 +416,7 @@ def bench_ours(args, rank, world, local):
         "mtp": {
             "metric": f"gdn_mtp GB/s at B={MTP_B}, T={MTP_T} (pool 128 slots, snapshots, in place)",
             "value": round(mtp_alg_bytes(MTP_B, MTP_T) * world / (mtp_step_ms * 1e-3) / 1e9, 2),
-            "unit": "GB/s", "ms_per_step": round(mtp_step_ms, 5),
+            "unit": "GB/s", "ms_per_step": round(mtp_step_ms, 5), "step_ms_stats": _stats(mtp_ms),
             "roofline": {"bound": "hbm",
                          "achieved": round(mtp_alg_bytes(MTP_B, MTP_T) / (statistics.mean(mtp_ms) * 1e-3) / 1e9, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",

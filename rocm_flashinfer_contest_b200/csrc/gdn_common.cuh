@@ -38,6 +38,26 @@ __device__ __forceinline__ float4 load_bf16x4(const __nv_bfloat16* p) {
     return make_float4(a.x, a.y, b.x, b.y);
 }
 
+// Packed fp32x2 arithmetic (sm_100 FFMA2/FMUL2: two independent, exactly
+// rounded fp32 operations per instruction) for the row loops of the
+// recurrent kernels.
+__device__ __forceinline__ float2 lo2(float4 v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); }
+
+// acc += x . y over four elements, as two interleaved partial sums.
+__device__ __forceinline__ float2 dot4_acc2(float4 x, float4 y, float2 acc) {
+    acc = __ffma2_rn(lo2(x), lo2(y), acc);
+    return __ffma2_rn(hi2(x), hi2(y), acc);
+}
+
+// g * s + d * k, elementwise.
+__device__ __forceinline__ float4 gs_plus_dk(float g, float4 s, float d, float4 k) {
+    const float2 g2 = make_float2(g, g), d2 = make_float2(d, d);
+    const float2 lo = __ffma2_rn(g2, lo2(s), __fmul2_rn(d2, lo2(k)));
+    const float2 hi = __ffma2_rn(g2, hi2(s), __fmul2_rn(d2, hi2(k)));
+    return make_float4(lo.x, lo.y, hi.x, hi.y);
+}
+
 __device__ __forceinline__ float warp_xor_sum(float x, int width_mask_bits) {
     // butterfly over the low `width_mask_bits` lane bits
     for (int m = 1; m < (1 << width_mask_bits); m <<= 1) x += __shfl_xor_sync(0xffffffffu, x, m);

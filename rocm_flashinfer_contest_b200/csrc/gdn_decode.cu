@@ -102,8 +102,13 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
     const bool upper = (sub & 4) != 0;  // after the exchange: lower half owns sk, upper owns sq
 #pragma unroll
     for (int ps = 0; ps < kPasses; ++ps) {
-        float sk = dot4(s[ps][0], kf[0]) + dot4(s[ps][1], kf[1]) + dot4(s[ps][2], kf[2]) + dot4(s[ps][3], kf[3]);
-        float sq = dot4(s[ps][0], qf[0]) + dot4(s[ps][1], qf[1]) + dot4(s[ps][2], qf[2]) + dot4(s[ps][3], qf[3]);
+        float2 sk2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            sk2 = dot4_acc2(s[ps][j], kf[j], sk2);
+            sq2 = dot4_acc2(s[ps][j], qf[j], sq2);
+        }
+        const float sk = sk2.x + sk2.y, sq = sq2.x + sq2.y;
         float give = upper ? sk : sq;
         float keep = upper ? sq : sk;
         keep += __shfl_xor_sync(0xffffffffu, give, 4);
@@ -118,14 +123,7 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(const DecodeParams p) {
         }
         float* dst = p.new_state + sbase + (size_t)ps * 4 * kDim;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            float4 r;
-            r.x = fmaf(g, s[ps][j].x, delta * kf[j].x);
-            r.y = fmaf(g, s[ps][j].y, delta * kf[j].y);
-            r.z = fmaf(g, s[ps][j].z, delta * kf[j].z);
-            r.w = fmaf(g, s[ps][j].w, delta * kf[j].w);
-            __stcs(reinterpret_cast<float4*>(dst + 32 * j), r);
-        }
+        for (int j = 0; j < 4; ++j) __stcs(reinterpret_cast<float4*>(dst + 32 * j), gs_plus_dk(g, s[ps][j], delta, kf[j]));
     }
 }
 

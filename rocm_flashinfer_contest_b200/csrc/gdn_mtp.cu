@@ -215,12 +215,13 @@ __global__ void __launch_bounds__(128) gdn_mtp_kernel(const MtpParams p) {
                                : nullptr;
 #pragma unroll
         for (int ps = 0; ps < kPasses; ++ps) {
-            float sk = 0.f, sq = 0.f;
+            float2 sk2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                sk += mtp_dot4(s[ps][j], kf[j]);
-                sq += mtp_dot4(s[ps][j], qf[j]);
+                sk2 = dot4_acc2(s[ps][j], kf[j], sk2);
+                sq2 = dot4_acc2(s[ps][j], qf[j], sq2);
             }
+            const float sk = sk2.x + sk2.y, sq = sq2.x + sq2.y;
             float give = upper ? sk : sq;
             float keep = upper ? sq : sk;
             keep += __shfl_xor_sync(0xffffffffu, give, 4);
@@ -231,12 +232,7 @@ __global__ void __launch_bounds__(128) gdn_mtp_kernel(const MtpParams p) {
             const float delta = beta * (cur.v[ps] - g * sk_all);
             if (sub == 4) p.out[ob + ps * 4] = __float2bfloat16_rn(p.scale * (g * keep + delta * kq));
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                s[ps][j].x = fmaf(g, s[ps][j].x, delta * kf[j].x);
-                s[ps][j].y = fmaf(g, s[ps][j].y, delta * kf[j].y);
-                s[ps][j].z = fmaf(g, s[ps][j].z, delta * kf[j].z);
-                s[ps][j].w = fmaf(g, s[ps][j].w, delta * kf[j].w);
-            }
+            for (int j = 0; j < 4; ++j) s[ps][j] = gs_plus_dk(g, s[ps][j], delta, kf[j]);
             if constexpr (sizeof(StateT) == 4) {  // snapshots exist for fp32 pools only
                 if (snap) mtp_store_row(snap_dst, (size_t)ps * 4 * kDim, sub, s[ps]);
             }
@@ -366,12 +362,13 @@ __global__ void __launch_bounds__(128) gdn_pool_decode_kernel(const MtpParams p)
     for (int ps = 0; ps < kPasses; ++ps) {
         float4 x[4];
         pack_widen(rows[ps], x);
-        float sk = 0.f, sq = 0.f;
+        float2 sk2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            sk += mtp_dot4(x[j], kf[j]);
-            sq += mtp_dot4(x[j], qf[j]);
+            sk2 = dot4_acc2(x[j], kf[j], sk2);
+            sq2 = dot4_acc2(x[j], qf[j], sq2);
         }
+        const float sk = sk2.x + sk2.y, sq = sq2.x + sq2.y;
         float give = upper ? sk : sq;
         float keep = upper ? sq : sk;
         keep += __shfl_xor_sync(0xffffffffu, give, 4);
@@ -381,12 +378,7 @@ __global__ void __launch_bounds__(128) gdn_pool_decode_kernel(const MtpParams p)
         const float delta = beta * (tk.v[ps] - g * sk_all);
         if (sub == 4) p.out[ob + ps * 4] = __float2bfloat16_rn(p.scale * (g * keep + delta * kq));
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            x[j].x = fmaf(g, x[j].x, delta * kf[j].x);
-            x[j].y = fmaf(g, x[j].y, delta * kf[j].y);
-            x[j].z = fmaf(g, x[j].z, delta * kf[j].z);
-            x[j].w = fmaf(g, x[j].w, delta * kf[j].w);
-        }
+        for (int j = 0; j < 4; ++j) x[j] = gs_plus_dk(g, x[j], delta, kf[j]);
         if constexpr (sizeof(StateT) == 4) {  // snapshots exist for fp32 pools only
             if (snap_dst != nullptr) mtp_store_row(snap_dst, (size_t)ps * 4 * kDim, sub, x);
         }

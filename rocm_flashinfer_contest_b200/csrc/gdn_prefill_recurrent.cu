@@ -93,8 +93,13 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
         const float g = expf(log_gate(A_log, bf16_to_f32(cur.a), dt_bias));
         const float beta = sigmoidf_(bf16_to_f32(cur.b));
         float kq = dot4r(kf[0], qf[0]) + dot4r(kf[1], qf[1]) + dot4r(kf[2], qf[2]) + dot4r(kf[3], qf[3]);
-        float sk = dot4r(s[0], kf[0]) + dot4r(s[1], kf[1]) + dot4r(s[2], kf[2]) + dot4r(s[3], kf[3]);
-        float sq = dot4r(s[0], qf[0]) + dot4r(s[1], qf[1]) + dot4r(s[2], qf[2]) + dot4r(s[3], qf[3]);
+        float2 sk2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            sk2 = dot4_acc2(s[j], kf[j], sk2);
+            sq2 = dot4_acc2(s[j], qf[j], sq2);
+        }
+        const float sk = sk2.x + sk2.y, sq = sq2.x + sq2.y;
         kq += __shfl_xor_sync(0xffffffffu, kq, 1);
         kq += __shfl_xor_sync(0xffffffffu, kq, 2);
         kq += __shfl_xor_sync(0xffffffffu, kq, 4);
@@ -108,12 +113,7 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
         if (sub == 4)
             p.out[((size_t)t * p.HV + hv) * kDim + row] = __float2bfloat16_rn(p.scale * (g * keep + delta * kq));
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            s[j].x = fmaf(g, s[j].x, delta * kf[j].x);
-            s[j].y = fmaf(g, s[j].y, delta * kf[j].y);
-            s[j].z = fmaf(g, s[j].z, delta * kf[j].z);
-            s[j].w = fmaf(g, s[j].w, delta * kf[j].w);
-        }
+        for (int j = 0; j < 4; ++j) s[j] = gs_plus_dk(g, s[j], delta, kf[j]);
         if (p.ckpt != nullptr && --until_ckpt == 0) {
             until_ckpt = p.ckpt_every;
             float* cd = ckpt_dst(p, n, hv, t - t0 + 1);

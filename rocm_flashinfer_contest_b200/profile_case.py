@@ -30,6 +30,7 @@ def main(argv=None):
     ap.add_argument("--no-state", action="store_true")
     ap.add_argument("--steps", type=int, default=4, help="mtp: tokens per batch entry")
     ap.add_argument("--no-snapshots", action="store_true", help="mtp: no intermediate states")
+    ap.add_argument("--bf16-state", action="store_true", help="mtp: bf16 state pool (no snapshots)")
     a = ap.parse_args(argv)
     dev = torch.device("cuda:0")
     if a.op == "decode":
@@ -39,7 +40,9 @@ def main(argv=None):
         fn = lambda: gdn_decode.run_into(*args, output=out, new_state=ns)  # noqa: E731
     elif a.op == "mtp":
         args = inputs.mtp_inputs(a.B, a.steps, 2 * a.B, a.H, a.HV, seed=0, device=dev,
-                                 intermediate=not a.no_snapshots)
+                                 intermediate=not (a.no_snapshots or a.bf16_state))
+        if a.bf16_state:
+            args[3] = args[3].to(torch.bfloat16)
         out = torch.empty((a.B, a.steps, a.HV, 128), dtype=torch.bfloat16, device=dev)
         fn = lambda: gdn_mtp.run_into(*args[:10], out, args[3],  # noqa: E731
                                       intermediate_states_buffer=args[10])
