@@ -121,8 +121,9 @@ int gdn_prefill_fwd_checkpointed(const void *q, const void *k, const void *v, co
  * will take the token-serial kernel.  For each of floor(T/64) + N chunk slots
  * the chunked kernels keep, per v-head, the chunk's [T ; P'] operand tile and
  * gates (17,424 bytes) and, per q/k head, its f16 [K ; Q] operand tile
- * (32,768 bytes).  No counterpart in the reference, whose AITER kernels
- * allocate their intermediates with torch.
+ * (32,768 bytes) and its cross-Gram tile [K ; Q] K_prev^T (16,384 bytes).
+ * No counterpart in the reference, whose AITER kernels allocate their
+ * intermediates with torch.
  */
 size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV);
 
@@ -142,9 +143,9 @@ size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV);
  * cudaFree or other allocating routine.
  *
  * Limit: gdn_prefill_workspace_bytes(N, T, H, HV) must not exceed 16 MiB
- * (16,777,216 bytes), i.e. (floor(T/64) + N) * (17,424 * HV + 32,768 * H)
- * <= 16 MiB when the chunked kernels run (for example T < 960 at N = 1,
- * H = 16, HV = 32, or T < 3,776 at N = 4, H = 4, HV = 8); larger problems
+ * (16,777,216 bytes), i.e. (floor(T/64) + N) * (17,424 * HV + 49,152 * H)
+ * <= 16 MiB when the chunked kernels run (for example T < 768 at N = 1,
+ * H = 16, HV = 32, or T < 2,944 at N = 4, H = 4, HV = 8); larger problems
  * return GDN_ERR_TOO_LARGE before anything is launched.  Problems below the
  * chunk threshold need no scratch at all.
  *

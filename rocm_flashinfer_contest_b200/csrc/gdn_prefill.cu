@@ -75,6 +75,7 @@ static int prefill_impl(const void* q, const void* k, const void* v, const float
     p.ckpt_cu = reinterpret_cast<const long long*>(ckpt_cu);
     p.ckpt_total = ckpt_total;
     p.ckpt_every = ckpt != nullptr ? ckpt_every : 0;
+    p.cross_gram = 0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (N == 0) {
         // no sequence: every token is uncovered, its output is zero

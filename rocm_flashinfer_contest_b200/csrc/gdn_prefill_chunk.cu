@@ -66,12 +66,17 @@ constexpr uint32_t kGateBytes = 4 * 256 + 16;
 constexpr int GR_BEG = 0, GR_BETA = 64, GR_FK = 128, GR_FQ = 192, GR_DECAY = 256;
 constexpr uint32_t kSlotBytes = kTileTP + kGateBytes;
 constexpr uint32_t kTileKQ = 32768;      // [K ; Q] f16, K-major 128 x 128
+constexpr uint32_t kTileG = 16384;       // G = [K ; Q]_j K_{j-1}^T f16, K-major 128 x 64
 
 // Workspace: (floor(T/64) + N) chunk slots; per slot HV (chunk, v-head)
-// records of kSlotBytes, then per slot H [K ; Q] tiles of kTileKQ.
+// records of kSlotBytes, then per slot H [K ; Q] tiles of kTileKQ, then per
+// slot H cross-Gram tiles of kTileG.
 __host__ __device__ inline long long ws_slots(int N, int T) { return (long long)(T / 64) + N; }
 __device__ __forceinline__ unsigned char* ws_kq(const PrefillParams& p, const unsigned char* ws) {
     return const_cast<unsigned char*>(ws) + (size_t)ws_slots(p.N, p.T) * p.HV * kSlotBytes;
+}
+__device__ __forceinline__ unsigned char* ws_g(const PrefillParams& p, const unsigned char* ws) {
+    return ws_kq(p, ws) + (size_t)ws_slots(p.N, p.T) * p.H * kTileKQ;
 }
 
 // Clock budget of one wait for MMA completion (~70 ms at 1.9 GHz; the MMAs of
@@ -144,7 +149,11 @@ constexpr uint32_t OFF_G = OFF_T + 64 * LDA * 4;   // gamma[64]
 constexpr uint32_t OFF_BETA = OFF_G + 256;         // beta[64]
 constexpr uint32_t SMEM_BYTES = OFF_BETA + 256 + 1024;  // + alignment slack
 static_assert(OFF_X + 48 * LDA * 4 <= OFF_TP, "A and X fit in the [K ; Q] tile");
-constexpr uint32_t TM_COLS = 64;
+// The previous chunk's K rows (bf16, K-major 64 x 128) for the cross-Gram
+// G_j = [K ; Q]_j K_{j-1}^T borrow the [T ; P] region, which is only written
+// after G has been computed.
+constexpr uint32_t OFF_KP = OFF_TP;
+constexpr uint32_t TM_COLS = 128;  // columns 0-63: [K ; Q] K^T, then P'; 64-127: G
 
 // Blocked T = (I + A)^-1 for the 64 x 64 strictly lower A in sA (fp32, row
 // stride LDA); writes T into sT, whose upper blocks must already be zero.
@@ -178,7 +187,8 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
 #pragma unroll 1
         for (int j = 0; j + d < 4; ++j) {
             const int i = j + d;
-            float acc0 = 0.f, acc1 = 0.f;
+            // two partial sums per output row: four independent FMA chains
+            float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll 1
             for (int k = j; k < i; ++k) {
                 const float* a0 = sA + (16 * i + r0) * LDA + 16 * k;
@@ -187,14 +197,16 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
                 for (int s4 = 0; s4 < 16; s4 += 4) {
                     const float4 x0 = *reinterpret_cast<const float4*>(a0 + s4);
                     const float4 x1 = *reinterpret_cast<const float4*>(a0 + LDA + s4);
-                    const float t0 = tk[(s4 + 0) * LDA], t1 = tk[(s4 + 1) * LDA];
-                    const float t2 = tk[(s4 + 2) * LDA], t3 = tk[(s4 + 3) * LDA];
-                    acc0 += x0.x * t0 + x0.y * t1 + x0.z * t2 + x0.w * t3;
-                    acc1 += x1.x * t0 + x1.y * t1 + x1.z * t2 + x1.w * t3;
+                    const float2 tlo = make_float2(tk[(s4 + 0) * LDA], tk[(s4 + 1) * LDA]);
+                    const float2 thi = make_float2(tk[(s4 + 2) * LDA], tk[(s4 + 3) * LDA]);
+                    acc0 = __ffma2_rn(lo2(x0), tlo, acc0);
+                    acc1 = __ffma2_rn(lo2(x1), tlo, acc1);
+                    acc0 = __ffma2_rn(hi2(x0), thi, acc0);
+                    acc1 = __ffma2_rn(hi2(x1), thi, acc1);
                 }
             }
-            sX[(16 * i + r0 - 16) * LDA + 16 * j + c] = acc0;
-            sX[(16 * i + r0 - 15) * LDA + 16 * j + c] = acc1;
+            sX[(16 * i + r0 - 16) * LDA + 16 * j + c] = acc0.x + acc0.y;
+            sX[(16 * i + r0 - 15) * LDA + 16 * j + c] = acc1.x + acc1.y;
         }
         __syncthreads();
 #pragma unroll 1
@@ -202,18 +214,20 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
             const int i = j + d;
             const float* t0r = sT + (16 * i + r0) * LDA + 16 * i;
             const float* xc = sX + (16 * i - 16) * LDA + 16 * j + c;
-            float acc0 = 0.f, acc1 = 0.f;
+            float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
             for (int s4 = 0; s4 < 16; s4 += 4) {
                 const float4 y0 = *reinterpret_cast<const float4*>(t0r + s4);
                 const float4 y1 = *reinterpret_cast<const float4*>(t0r + LDA + s4);
-                const float x0 = xc[(s4 + 0) * LDA], x1 = xc[(s4 + 1) * LDA];
-                const float x2 = xc[(s4 + 2) * LDA], x3 = xc[(s4 + 3) * LDA];
-                acc0 += y0.x * x0 + y0.y * x1 + y0.z * x2 + y0.w * x3;
-                acc1 += y1.x * x0 + y1.y * x1 + y1.z * x2 + y1.w * x3;
+                const float2 xlo = make_float2(xc[(s4 + 0) * LDA], xc[(s4 + 1) * LDA]);
+                const float2 xhi = make_float2(xc[(s4 + 2) * LDA], xc[(s4 + 3) * LDA]);
+                acc0 = __ffma2_rn(lo2(y0), xlo, acc0);
+                acc1 = __ffma2_rn(lo2(y1), xlo, acc1);
+                acc0 = __ffma2_rn(hi2(y0), xhi, acc0);
+                acc1 = __ffma2_rn(hi2(y1), xhi, acc1);
             }
-            sT[(16 * i + r0) * LDA + 16 * j + c] = -acc0;
-            sT[(16 * i + r0 + 1) * LDA + 16 * j + c] = -acc1;
+            sT[(16 * i + r0) * LDA + 16 * j + c] = -(acc0.x + acc0.y);
+            sT[(16 * i + r0 + 1) * LDA + 16 * j + c] = -(acc1.x + acc1.y);
         }
         __syncthreads();
     }
@@ -262,11 +276,21 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
         cp_async16(sKQ + umma::kmaj_off(r, c * 8, 128), p.k + row, ok);
         cp_async16(sKQ + umma::kmaj_off(64 + r, c * 8, 128), p.q + row, ok);
     }
-    cp_async_commit();
-    for (int idx = tid; idx < 64 * 64; idx += NT) {  // T's upper blocks are zero
-        const int i = idx >> 6, jj = idx & 63;
-        if ((jj >> 4) > (i >> 4)) sT[i * LDA + jj] = 0.f;
+    // the first v-head of a q/k head publishes the chunk's [K ; Q] tile and,
+    // for every chunk after the first, the cross-Gram tile G (the previous
+    // chunk is a full one, so all its rows are valid)
+    const bool publish = hv % p.rep == 0;
+    const bool gram = publish && p.cross_gram && j > 0;
+    if (gram) {
+        const uint32_t sKP = umma::smem_u32(sm + OFF_KP);
+#pragma unroll
+        for (int it = 0; it < C * 16 / NT; ++it) {
+            const int idx = tid + it * NT, r = idx >> 4, c = idx & 15;
+            cp_async16(sKP + umma::kmaj_off(r, c * 8, 64), p.k + ((size_t)(tc - C + r) * p.H + hq) * kDim + c * 8,
+                       true);
+        }
     }
+    cp_async_commit();
     // gates and the inclusive scan of log g (warps 0 and 1)
     float lg = 0.f, beta = 0.f;
     if (tid < len) {
@@ -299,20 +323,43 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
     const uint32_t tmem = tmem_base_sh;
     const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
 
-    // MMA_A: [K ; Q] K^T in bf16
+    // MMA_A: [K ; Q] K^T in bf16; MMA_G: [K ; Q] K_{j-1}^T
     if (tid == 0) {
         constexpr uint32_t ID = umma::idesc_f16(128, 64, 1, 1, 0, 0);
 #pragma unroll
         for (int k0 = 0; k0 < kDim; k0 += 16)
             umma::mma_f16(tmem, umma::desc_kmaj(sKQ, 128, k0), umma::desc_kmaj(sKQ, 128, k0), ID, k0 > 0);
+        if (gram) {
+            const uint32_t sKP = umma::smem_u32(sm + OFF_KP);
+#pragma unroll
+            for (int k0 = 0; k0 < kDim; k0 += 16)
+                umma::mma_f16(tmem + 64, umma::desc_kmaj(sKQ, 128, k0), umma::desc_kmaj(sKP, 64, k0), ID, k0 > 0);
+        }
         umma::mma_commit(&mbar[0]);
     }
     if (!wait_mma(&mbar[0], 0)) goto done;
     umma::fence_after_sync();
 
+    // G tile (f16, K-major 128 x 64, the layout of the chain's MMA operand):
+    // thread = row (TMEM lane), 64 columns
+    if (gram) {
+        unsigned char* gt = ws_g(p, ws) + ((size_t)s * p.H + hq) * kTileG;
+        const int row = tid;
+#pragma unroll 1
+        for (int c16 = 0; c16 < C; c16 += 16) {
+            float d[16];
+            umma::tmem_ld16(tmem + lane_base + 64 + c16, d);
+            __half2 h[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) h[e] = __floats2half2_rn(d[2 * e], d[2 * e + 1]);
+            *reinterpret_cast<uint4*>(gt + umma::kmaj_off(row, c16, 128)) = *reinterpret_cast<uint4*>(h);
+            *reinterpret_cast<uint4*>(gt + umma::kmaj_off(row, c16 + 8, 128)) = *reinterpret_cast<uint4*>(h + 4);
+        }
+    }
+
     // the first v-head of each q/k head also publishes the chunk's [K ; Q]
     // tile for the chain kernel: the same swizzled layout, converted to f16
-    if (hv % p.rep == 0) {
+    if (publish) {
         uint4* dst = reinterpret_cast<uint4*>(ws_kq(p, ws) + ((size_t)s * p.H + hq) * kTileKQ);
 #pragma unroll 4
         for (int idx = tid; idx < (int)(kTileKQ / 16); idx += NT) {
@@ -332,11 +379,29 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
         const float gi = sG[i];
         const float bi = sBeta[i];
 #pragma unroll 1
-        for (int c16 = 0; c16 < C; c16 += 16) {
-            float d[16];
-            umma::tmem_ld16(tmem + lane_base + c16, d);
+        for (int c32 = 0; c32 < C; c32 += 32) {
+            float d2[2][16];
+            umma::tmem_ld16x2(tmem + lane_base + c32, tmem + lane_base + c32 + 16, d2[0], d2[1]);
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+            const int c16 = c32 + 16 * hh;
+            const float (&d)[16] = d2[hh];
             float r[16];
-            if (tid < 64) {
+            // the warp's rows are 32 * (warp % 2) .. + 31: a block of columns
+            // past them is all zero (warp-uniform)
+            const bool zero_block = c16 > 32 * (warp & 1) + 31;
+            if (zero_block) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) r[e] = 0.f;
+                if (tid < 64) {
+#pragma unroll
+                    for (int e = 0; e < 16; e += 4)
+                        *reinterpret_cast<float4*>(sA + i * LDA + c16 + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+                } else {
+                    st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), r);
+                    st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), r + 8);
+                }
+            } else if (tid < 64) {
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     const int jj = c16 + e;
@@ -354,6 +419,7 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
                 st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), r);
                 st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), r + 8);
             }
+            }
         }
     }
     __syncthreads();
@@ -365,9 +431,14 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
         const float* tr = sT + i * LDA + h;
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
-            const float4 a = *reinterpret_cast<const float4*>(tr + c);
-            const float4 b = *reinterpret_cast<const float4*>(tr + c + 4);
-            const float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            // blocks above the diagonal are zero and are never stored in sT
+            float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (((h + c) >> 4) <= (i >> 4)) {
+                const float4 a = *reinterpret_cast<const float4*>(tr + c);
+                const float4 b = *reinterpret_cast<const float4*>(tr + c + 4);
+                x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+                x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+            }
             st_f16x8(sm + OFF_TP, umma::kmaj_off(i, h + c, 128), x);  // A rows: T[i][j]
             st_f16x8(sm + OFF_TB, umma::mnmaj_off(h + c, i, C), x);   // B: (n = m, k = j) = T[j][m]
         }
@@ -746,10 +817,453 @@ done:
 }
 
 }  // namespace chain
+
+// ============================================================================
+// chain kernel, split-path form (32-wide V tiles)
+// ============================================================================
+// The state reaches the next chunk's products only through
+//   R_{j+1} = [K;Q]_{j+1} S_{j+1} = [K;Q]_{j+1} (e^{gamma_C,j} S_j) + G_{j+1} Dt_j,
+// G_{j+1} = [K;Q]_{j+1} K_j^T (published by the prep), Dt_j = Delta~ of chunk
+// j.  The first term needs only S_j, so it is issued a chunk early (MMA_1a)
+// and the critical path per chunk is two tensor-core round trips:
+//   R_j -> Y_j -> MMA_2 = [T;P']_j Y_j -> Dt_j -> MMA_1b = G_{j+1} Dt_j -> R_{j+1}.
+// The state update S_{j+1} = e^{gamma_C} S_j + K_j^T Dt_j (MMA_3 plus an FMA
+// per element), the outputs and the loads run beside it.
+//
+// Warp roles (TMEM lane quarter = warp % 4):
+//   warps 0,1,4,5   lanes 0-63, 16 columns each: Y and Dt;
+//   warps 2,3,6,7   lanes 64-127, 16 columns each: the outputs;
+//   warps 8-11      all lanes, 32 columns each: the state, held in registers
+//                   for the whole sequence, and its f16 operand copies;
+//                   thread 256 also issues the bulk copies;
+//   warp 12         one thread issues every MMA, in one order per chunk:
+//                   MMA_2(j), MMA_1a(j+1), MMA_1b(j+1), MMA_3(j).  MMAs that
+//                   feed one accumulator are never issued from two threads.
+// Producers hand operands to the issuer through mbarriers they arrive on.
+// Every wait is bounded; a timeout raises a shared abort flag that every loop
+// checks, so no thread is left waiting on a barrier that will not complete.
+namespace chain2 {
+
+constexpr int VT = 32, HALF = 16;
+constexpr int NT = 416;                  // 13 warps
+constexpr int kLoader = 256;             // bulk-copy issuer (state warps)
+constexpr int kMma = 384;                // MMA issuer
+constexpr int kSW = 128;                 // state-warp threads
+constexpr int NB = 3;                    // chunk m's data in buffer m % 3
+constexpr uint32_t TM_R = 0;             // R[2]: columns 0-31 / 32-63
+constexpr uint32_t TM_2 = 64;            // MMA_2 results [2]: 64-95 / 96-127
+constexpr uint32_t TM_3 = 128, TM_COLS = 256;
+constexpr uint32_t VROW = VT * 2 + 16;
+constexpr uint32_t SH_BYTES = VT * kDim * 2;
+constexpr uint32_t YD_BYTES = VT * C * 2;
+constexpr uint32_t OFF_KQ = 0;                          // 3 x [K ; Q]
+constexpr uint32_t OFF_TP = OFF_KQ + NB * kTileKQ;      // 3 x [T ; P']
+constexpr uint32_t OFF_G = OFF_TP + NB * kTileTP;       // 2 x G
+constexpr uint32_t OFF_SH = OFF_G + 2 * kTileG;         // 2 x f16 e^{gamma_C} S (MN-major, 64-byte swizzle)
+constexpr uint32_t OFF_Y = OFF_SH + 2 * SH_BYTES;
+constexpr uint32_t OFF_DL = OFF_Y + YD_BYTES;
+constexpr uint32_t OFF_RV = OFF_DL + YD_BYTES;          // 3 x v rows
+constexpr uint32_t OFF_GB = OFF_RV + NB * C * VROW;     // 3 x gate records
+constexpr uint32_t SMEM_BYTES = OFF_GB + NB * kGateBytes + 1024;
+static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
+static_assert(OFF_G % 1024 == 0 && OFF_SH % 1024 == 0 && OFF_Y % 1024 == 0 && OFF_DL % 1024 == 0 &&
+              OFF_GB % 16 == 0, "tile alignment");
+
+constexpr uint32_t ID_S = umma::idesc_f16(128, VT, 0, 0, 0, 1);  // K-major A x MN-major B
+constexpr uint32_t ID_D = umma::idesc_f16(128, VT, 0, 0, 1, 1);  // K^T (MN-major) x Dt
+
+__device__ __forceinline__ uint32_t b_off(uint32_t v, uint32_t k) { return umma::mnmaj64_off(v, k); }
+
+// A descriptor advanced by `bytes` (a multiple of 16): the start address
+// field is bits 0-13 of the descriptor, in 16-byte units, and no shared
+// memory address carries out of it.
+__device__ __forceinline__ uint64_t dadd(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
+// K offsets of the three operand forms for the K step at element k0
+__host__ __device__ constexpr uint32_t koff_kmaj128(int k0) { return (k0 >> 6) * 128u * 128u + (k0 & 63) * 2u; }
+__host__ __device__ constexpr uint32_t koff_mn64(int k0) { return (k0 >> 3) * 512u; }
+__host__ __device__ constexpr uint32_t koff_kt(int k0) { return (k0 >> 3) * 1024u; }
+
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(umma::smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(umma::smem_u32(bar)) : "memory");
+}
+
+struct Bars {
+    uint64_t ld[NB];    // chunk data landed: 1 expect_tx arrive + 128 cp.async arrives
+    uint64_t ldG[2];    // G_m landed (index (m - 1) % 2)
+    uint64_t init;      // state warps: SH[0], SH[1] written (128 arrivals)
+    uint64_t yr;        // lower threads: Y_j in shared memory (128 arrivals)
+    uint64_t dr;        // lower threads: Dt_j in shared memory (128 arrivals)
+    uint64_t od[2];     // output threads: done with R_j, MMA_2(j) (128 arrivals, index j % 2)
+    uint64_t mR[2];     // R_j complete (index j % 2)
+    uint64_t m1a[2];    // MMA_1a(m) complete (index m % 2)
+    uint64_t m2[2];     // MMA_2(j) complete (index j % 2)
+    uint64_t m3;        // MMA_3(j) complete
+    uint64_t mSd;       // state warps: S_{j+1} formed, SH for MMA_1a(j + 2) written (128 arrivals)
+    uint64_t fin;       // drain of the issuer's MMAs at exit
+};
+
+// Chunk m's [K ; Q], [T ; P'] and gates (bulk copies by the loader) and its
+// v rows (cp.async by the 128 state-warp threads) into buffer m % 3.
+__device__ __forceinline__ void load_chunk(const PrefillParams& p, const unsigned char* ws, unsigned char* sm,
+                                           Bars& B, int buf, long long tc, int len, long long slot, int hq, int hv,
+                                           int v0, int sw, bool lead) {
+    if (lead) {
+        umma::mbar_arrive_expect_tx(&B.ld[buf], kTileKQ + kTileTP + kGateBytes);
+        const unsigned char* rec = ws + ((size_t)slot * p.HV + hv) * kSlotBytes;
+        const unsigned char* kq = ws_kq(p, ws) + ((size_t)slot * p.H + hq) * kTileKQ;
+        umma::bulk_g2s(umma::smem_u32(sm + OFF_KQ + buf * kTileKQ), kq, kTileKQ / 2, &B.ld[buf]);
+        umma::bulk_g2s(umma::smem_u32(sm + OFF_KQ + buf * kTileKQ + kTileKQ / 2), kq + kTileKQ / 2, kTileKQ / 2,
+                       &B.ld[buf]);
+        umma::bulk_g2s(umma::smem_u32(sm + OFF_TP + buf * kTileTP), rec, kTileTP, &B.ld[buf]);
+        umma::bulk_g2s(umma::smem_u32(sm + OFF_GB + buf * kGateBytes), rec + kTileTP, kGateBytes, &B.ld[buf]);
+    }
+    const uint32_t rv = umma::smem_u32(sm + OFF_RV) + buf * (C * VROW);
+#pragma unroll
+    for (int it = 0; it < C * (VT / 8) / kSW; ++it) {
+        const int idx = sw + it * kSW, r = idx / (VT / 8), c = idx % (VT / 8);
+        const bool ok = r < len;
+        const size_t off = ok ? ((size_t)(tc + r) * p.HV + hv) * kDim + v0 + c * 8 : 0;
+        cp_async16(rv + r * VROW + c * 16, p.v + off, ok);
+    }
+    cp_async_mbar_arrive_noinc(&B.ld[buf]);
+}
+
+__device__ __forceinline__ void load_g(const PrefillParams& p, const unsigned char* ws, unsigned char* sm, Bars& B,
+                                       int gb, long long slot, int hq) {
+    umma::mbar_arrive_expect_tx(&B.ldG[gb], kTileG);
+    umma::bulk_g2s(umma::smem_u32(sm + OFF_G + gb * kTileG), ws_g(p, ws) + ((size_t)slot * p.H + hq) * kTileG,
+                   kTileG, &B.ldG[gb]);
+}
+
+__device__ __forceinline__ bool wait_b(uint64_t* bar, uint32_t parity) {
+    return umma::mbar_wait(bar, parity, kWaitBudget);
+}
+__device__ __forceinline__ uint32_t ph(long long use) { return (uint32_t)(use & 1); }
+
+// f16 copy of scale * s (32 columns of lane `row`) into an SH tile.
+__device__ __forceinline__ void store_sh(unsigned char* sm, int which, int row, float scale, const float (&s)[32]) {
+#pragma unroll
+    for (int c8 = 0; c8 < 32; c8 += 8) {
+        float x[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = scale * s[c8 + e];
+        st_f16x8(sm + OFF_SH + which * SH_BYTES, b_off(c8, row), x);
+    }
+}
+
+__global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain2_kernel(const PrefillParams p,
+                                                                       const unsigned char* ws) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ Bars B;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ volatile int abort_flag;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quarter = warp & 3;
+    const int row = 32 * quarter + lane;  // TMEM lane of this thread
+    const bool lower = warp < 8 && quarter < 2;
+    const bool upper = warp < 8 && quarter >= 2;
+    const bool state = warp >= 8 && warp < 12;
+    const int sw = tid - 256;                          // state-warp thread index 0..127
+    const int cb = warp < 8 ? HALF * (warp >> 2) : 0;  // first column of this thread
+    const int vt = blockIdx.x % (kDim / VT);
+    const long long nh = blockIdx.x / (kDim / VT);
+    const int hv = (int)(nh % p.HV), n = (int)(nh / p.HV);
+    const int hq = hv / p.rep;
+    const int v0 = vt * VT;
+
+    long long t0, t1;
+    seq_bounds(p, n, t0, t1);
+    if (tid < VT) zero_uncovered_outputs(p, n, t0, t1, hv, v0 + tid, true);
+    const size_t state_off = ((size_t)nh * kDim + v0) * kDim;  // [n][hv][v0][0]
+    if (t1 == t0) {
+        for (int idx = tid; idx < VT * kDim / 4; idx += NT)
+            reinterpret_cast<float4*>(p.new_state + state_off)[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
+        return;
+    }
+    const long long slot0 = t0 / C + n;
+    const long long nchunks = (t1 - t0 + C - 1) / C;
+    auto chunk_len = [&](long long j) { const long long r = t1 - t0 - C * j; return (int)(r < C ? r : C); };
+    auto gates_of = [&](long long m) {
+        return reinterpret_cast<const float*>(sm + OFF_GB + (int)(m % NB) * kGateBytes);
+    };
+
+    if (warp == 0) {
+        umma::tmem_alloc(&tmem_base_sh, TM_COLS);
+        umma::tmem_relinquish();
+    }
+    if (tid == 0) {
+        for (int b = 0; b < NB; ++b) umma::mbar_init(&B.ld[b], 1 + kSW);
+        for (int b = 0; b < 2; ++b) {
+            umma::mbar_init(&B.ldG[b], 1);
+            umma::mbar_init(&B.od[b], 128);
+            umma::mbar_init(&B.mR[b], 1);
+            umma::mbar_init(&B.m1a[b], 1);
+            umma::mbar_init(&B.m2[b], 1);
+        }
+        umma::mbar_init(&B.init, kSW);
+        umma::mbar_init(&B.yr, 128);
+        umma::mbar_init(&B.dr, 128);
+        umma::mbar_init(&B.m3, 1);
+        umma::mbar_init(&B.mSd, kSW);
+        umma::mbar_init(&B.fin, 1);
+        umma::fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = tmem_base_sh;
+    const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);
+    const bool lead = tid == kLoader;
+    bool failed = false;
+    long long last_ld[NB] = {-1, -1, -1}, last_g[2] = {-1, -1};  // issued loads (loader's record)
+    auto fail = [&]() { failed = true; abort_flag = 1; };
+
+    if (tid == kMma) {
+        // ---- the MMA issuer: descriptors computed once, advanced by constant offsets ----
+        const uint64_t dKQ0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_KQ), 128, 0);
+        const uint64_t dKT0 = umma::desc_sw128(umma::smem_u32(sm + OFF_KQ), 16384u, 1024u);
+        const uint64_t dTP0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_TP), 128, 0);
+        const uint64_t dG0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_G), 128, 0);
+        const uint64_t dSH0 = umma::desc_mnmaj64(umma::smem_u32(sm + OFF_SH), 0);
+        const uint64_t dY = umma::desc_mnmaj64(umma::smem_u32(sm + OFF_Y), 0);
+        const uint64_t dDL = umma::desc_mnmaj64(umma::smem_u32(sm + OFF_DL), 0);
+        auto mma_1a = [&](long long m) {  // R_m = [K ; Q]_m SH[m % 2]
+            const uint64_t a = dadd(dKQ0, (uint32_t)(m % NB) * kTileKQ), bsh = dadd(dSH0, (uint32_t)(m % 2) * SH_BYTES);
+            const uint32_t d = tmem + TM_R + (uint32_t)(m % 2) * VT;
+#pragma unroll
+            for (int k0 = 0; k0 < kDim; k0 += 16)
+                umma::mma_f16(d, dadd(a, koff_kmaj128(k0)), dadd(bsh, koff_mn64(k0)), ID_S, k0 > 0);
+        };
+
+        bool ok = wait_b(&B.init, 0) && wait_b(&B.ld[0], 0);
+        if (ok) {
+            umma::fence_after_sync();
+            mma_1a(0);
+            umma::mma_commit(&B.m1a[0]);
+            umma::mma_commit(&B.mR[0]);
+        }
+        for (long long j = 0; j < nchunks && ok && !abort_flag; ++j) {
+            const int b = (int)(j % NB);
+            // MMA_2(j) = [T ; P']_j Y_j, once Y_j is written and TM_2[j % 2] has been read (outputs of j - 2)
+            ok = wait_b(&B.yr, ph(j));
+            if (ok && j >= 2) ok = wait_b(&B.od[j % 2], ph((j - 2) / 2));
+            if (!ok) break;
+            umma::fence_after_sync();
+            {
+                const uint32_t d2 = tmem + TM_2 + (uint32_t)(j % 2) * VT;
+#pragma unroll
+                for (int k0 = 0; k0 < C; k0 += 16)
+                    umma::mma_f16(d2, dadd(dTP0, b * kTileTP + koff_kmaj128(k0)), dadd(dY, koff_mn64(k0)), ID_S, k0 > 0);
+                umma::mma_commit(&B.m2[j % 2]);
+            }
+            // state after chunk j - 1 formed: TM_3 free, SH[(j + 1) % 2] written
+            if (j >= 1) ok = wait_b(&B.mSd, ph(j - 1));
+            // MMA_1a(j+1) = [K ; Q]_{j+1} (e^{gamma_C,j} S_j) into R[(j + 1) % 2], once R_{j-1} has been read
+            if (ok && j + 1 < nchunks) {
+                ok = wait_b(&B.ld[(j + 1) % NB], ph((j + 1) / NB));
+                if (ok && j >= 1) ok = wait_b(&B.od[(j + 1) % 2], ph((j - 1) / 2));
+                if (ok) {
+                    umma::fence_after_sync();
+                    mma_1a(j + 1);
+                    umma::mma_commit(&B.m1a[(j + 1) % 2]);
+                }
+            }
+            // Dt_j ready: MMA_1b(j+1) = G_{j+1} Dt_j onto R_{j+1}, then MMA_3(j) = K_j^T Dt_j
+            ok = ok && wait_b(&B.dr, ph(j));
+            if (ok && j + 1 < nchunks) {
+                ok = wait_b(&B.ldG[j % 2], ph(j / 2));
+                if (ok) {
+                    umma::fence_after_sync();
+                    const uint32_t d = tmem + TM_R + (uint32_t)((j + 1) % 2) * VT;
+#pragma unroll
+                    for (int k0 = 0; k0 < C; k0 += 16)
+                        umma::mma_f16(d, dadd(dG0, (uint32_t)(j % 2) * kTileG + koff_kmaj128(k0)),
+                                      dadd(dDL, koff_mn64(k0)), ID_S, true);
+                    umma::mma_commit(&B.mR[(j + 1) % 2]);
+                }
+            }
+            if (ok) {
+                umma::fence_after_sync();
+#pragma unroll
+                for (int k0 = 0; k0 < C; k0 += 16)
+                    umma::mma_f16(tmem + TM_3, dadd(dKT0, b * kTileKQ + koff_kt(k0)), dadd(dDL, koff_mn64(k0)), ID_D,
+                                  k0 > 0);
+                umma::mma_commit(&B.m3);
+            }
+        }
+        if (!ok) fail();
+        // drain: every MMA issued here completes before the CTA exits
+        umma::mma_commit(&B.fin);
+        if (!wait_b(&B.fin, 0)) fail();
+    } else if (state) {
+        // ---- state warps: S (fp32, registers) for TMEM lane `row`, 32 columns ----
+        for (long long m = 0; m < NB && m < nchunks; ++m) {
+            load_chunk(p, ws, sm, B, (int)m, t0 + C * m, chunk_len(m), slot0 + m, hq, hv, v0, sw, lead);
+            last_ld[m] = m;
+        }
+        if (lead) {
+            for (long long m = 1; m <= 2 && m < nchunks; ++m) {
+                load_g(p, ws, sm, B, (int)((m - 1) % 2), slot0 + m, hq);
+                last_g[(m - 1) % 2] = m;
+            }
+        }
+        float sv[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sv[e] = p.state ? p.state[state_off + (size_t)e * kDim + row] : 0.f;
+        if (!wait_b(&B.ld[0], 0)) fail();
+        if (!failed) {
+            store_sh(sm, 0, row, 1.f, sv);                                         // MMA_1a(0): S_0
+            if (nchunks > 1) store_sh(sm, 1, row, gates_of(0)[GR_DECAY], sv);    // MMA_1a(1): e^{gamma_C,0} S_0
+        }
+        umma::fence_proxy_async_smem();
+        mbar_arrive(&B.init);
+
+        for (long long j = 0; j < nchunks && !abort_flag; ++j) {
+            const int len = chunk_len(j);
+            const float* gr = gates_of(j);
+            const bool more = j + 2 < nchunks;  // MMA_1a(j + 2) will read SH[j % 2]
+            bool ok = wait_b(&B.ld[j % NB], ph(j / NB)) && wait_b(&B.m3, ph(j));
+            if (ok) {
+                umma::fence_after_sync();
+                float d[32];
+                umma::tmem_ld32(tl + TM_3, d);
+                const float decay = gr[GR_DECAY];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) sv[e] = fmaf(decay, sv[e], d[e]);
+            }
+            if (ok && more) {
+                ok = wait_b(&B.m1a[j % 2], ph(j / 2)) && wait_b(&B.ld[(j + 1) % NB], ph((j + 1) / NB));
+                if (ok) store_sh(sm, (int)(j % 2), row, gates_of(j + 1)[GR_DECAY], sv);
+            }
+            // the output threads are done with chunk j's buffer (read before
+            // their arrival) before the state may move on and refill it
+            ok = ok && wait_b(&B.od[j % 2], ph(j / 2));
+            if (!ok) { fail(); break; }
+            umma::fence_proxy_async_smem();
+            umma::fence_before_sync();
+            mbar_arrive(&B.mSd);
+            if (p.ckpt != nullptr && len == C && (C * (j + 1)) % p.ckpt_every == 0) {
+                float* cd = ckpt_dst(p, n, hv, C * (j + 1));
+                if (cd != nullptr) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) __stcs(cd + (size_t)(v0 + e) * kDim + row, sv[e]);
+                }
+            }
+            // chunk j's buffers are free: chunk j + 3's data; G_{j + 3} into the
+            // buffer of G_{j + 1}, consumed by MMA_1b(j + 1) before MMA_3(j)
+            if (j + NB < nchunks) {
+                load_chunk(p, ws, sm, B, (int)(j % NB), t0 + C * (j + NB), chunk_len(j + NB), slot0 + j + NB, hq, hv,
+                           v0, sw, lead);
+                last_ld[j % NB] = j + NB;
+            }
+            if (lead && j + 3 < nchunks) {
+                load_g(p, ws, sm, B, (int)((j + 2) % 2), slot0 + j + 3, hq);
+                last_g[(j + 2) % 2] = j + 3;
+            }
+            if (j + 1 == nchunks) {  // final state, fp32 k-last
+#pragma unroll
+                for (int e = 0; e < 32; ++e) __stcs(p.new_state + state_off + (size_t)e * kDim + row, sv[e]);
+            }
+        }
+    } else if (upper) {
+        // ---- output warps: O = scale e^gamma QS + P'Y for token row - 64 ----
+        for (long long j = 0; j < nchunks && !abort_flag; ++j) {
+            const int len = chunk_len(j);
+            const long long tc = t0 + C * j;
+            const float* gr = gates_of(j);
+            if (!(wait_b(&B.ld[j % NB], ph(j / NB)) && wait_b(&B.mR[j % 2], ph(j / 2)) &&
+                  wait_b(&B.m2[j % 2], ph(j / 2)))) { fail(); break; }
+            umma::fence_after_sync();
+            float qs[HALF], d[HALF];
+            umma::tmem_ld16x2(tl + TM_R + (uint32_t)(j % 2) * VT + cb, tl + TM_2 + (uint32_t)(j % 2) * VT + cb, qs, d);
+            const int i = row - 64;
+            const float fq = gr[GR_FQ + i];
+            umma::fence_before_sync();
+            mbar_arrive(&B.od[j % 2]);
+            if (i < len) {
+                __nv_bfloat16* op = p.out + ((size_t)(tc + i) * p.HV + hv) * kDim + v0 + cb;
+#pragma unroll
+                for (int c8 = 0; c8 < HALF; c8 += 8) {
+                    __nv_bfloat162 o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        o[e] = __floats2bfloat162_rn(fmaf(fq, qs[c8 + 2 * e], d[c8 + 2 * e]),
+                                                     fmaf(fq, qs[c8 + 2 * e + 1], d[c8 + 2 * e + 1]));
+                    *reinterpret_cast<uint4*>(op + c8) = *reinterpret_cast<uint4*>(o);
+                }
+            }
+        }
+    } else if (lower) {
+        // ---- lower warps: Y_j, Dt_j ----
+        for (long long j = 0; j < nchunks && !abort_flag; ++j) {
+            const int b = (int)(j % NB);
+            const int len = chunk_len(j);
+            const float* gr = gates_of(j);
+            if (!(wait_b(&B.ld[b], ph(j / NB)) && wait_b(&B.mR[j % 2], ph(j / 2)))) { fail(); break; }
+            umma::fence_after_sync();
+            {
+                float d[HALF];
+                umma::tmem_ld16(tl + TM_R + (uint32_t)(j % 2) * VT + cb, d);
+                const int i = row;
+                const bool live = i < len;
+                const float beg = gr[GR_BEG + i], b_i = gr[GR_BETA + i];
+                const unsigned char* vrow = sm + OFF_RV + b * (C * VROW) + i * VROW + cb * 2;
+#pragma unroll
+                for (int c8 = 0; c8 < HALF; c8 += 8) {
+                    float vv[8], y[8];
+                    unpack_bf16x8(*reinterpret_cast<const uint4*>(vrow + c8 * 2), vv);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) y[e] = live ? fmaf(-beg, d[c8 + e], b_i * vv[e]) : 0.f;
+                    st_f16x8(sm + OFF_Y, b_off(cb + c8, i), y);
+                }
+            }
+            umma::fence_proxy_async_smem();
+            umma::fence_before_sync();
+            mbar_arrive(&B.yr);
+            if (!wait_b(&B.m2[j % 2], ph(j / 2))) { fail(); break; }
+            umma::fence_after_sync();
+            {
+                float d[HALF];
+                umma::tmem_ld16(tl + TM_2 + (uint32_t)(j % 2) * VT + cb, d);
+                const float fk = gr[GR_FK + row];
+#pragma unroll
+                for (int e = 0; e < HALF; ++e) d[e] *= fk;
+#pragma unroll
+                for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_DL, b_off(cb + c8, row), d + c8);
+            }
+            umma::fence_proxy_async_smem();
+            umma::fence_before_sync();
+            mbar_arrive(&B.dr);
+        }
+    }
+
+    // ---- exit: copies in flight land first ----
+    cp_async_wait_all();
+    umma::fence_before_sync();
+    failed = __syncthreads_or(failed) || abort_flag;
+    if (failed && lead) {
+        atomicOr(&g_device_status, kDevStatTimeout);
+        for (int b = 0; b < NB; ++b)
+            if (last_ld[b] >= 0) wait_b(&B.ld[b], ph(last_ld[b] / NB));
+        for (int b = 0; b < 2; ++b)
+            if (last_g[b] >= 1) wait_b(&B.ldG[b], ph((last_g[b] - 1) / 2));
+    }
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, TM_COLS);
+}
+
+}  // namespace chain2
 }  // namespace chunk
 
 size_t prefill_workspace_bytes(int N, int T, int H, int HV) {
-    return (size_t)chunk::ws_slots(N, T) * ((size_t)HV * chunk::kSlotBytes + (size_t)H * chunk::kTileKQ);
+    return (size_t)chunk::ws_slots(N, T) *
+           ((size_t)HV * chunk::kSlotBytes + (size_t)H * (chunk::kTileKQ + chunk::kTileG));
 }
 
 void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st) {
@@ -760,8 +1274,8 @@ void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t 
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::prep::SMEM_BYTES);
         cudaFuncSetAttribute(chunk::chain::gdn_prefill_chunk_chain_kernel<64>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain::Cfg<64>::SMEM_BYTES);
-        cudaFuncSetAttribute(chunk::chain::gdn_prefill_chunk_chain_kernel<32>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain::Cfg<32>::SMEM_BYTES);
+        cudaFuncSetAttribute(chunk::chain2::gdn_prefill_chunk_chain2_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain2::SMEM_BYTES);
         int dev = 0, sms = 0;
         if (cudaGetDevice(&dev) == cudaSuccess &&
             cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0)
@@ -770,14 +1284,18 @@ void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t 
     }
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     const long long slots = chunk::ws_slots(p.N, p.T);
-    chunk::prep::gdn_prefill_chunk_prep_kernel<<<(unsigned)(slots * p.HV), chunk::prep::NT,
-                                                 chunk::prep::SMEM_BYTES, st>>>(p, ws);
-    // one chain per (sequence, v-head, V tile): split V into 32-wide tiles when
-    // 64-wide ones would not cover the SMs (e.g. a single long sequence)
+    // one chain per (sequence, v-head, V tile): 32-wide tiles on the split
+    // critical path when 64-wide ones would not cover the SMs (e.g. a single
+    // long sequence); that path needs the prep's cross-Gram tiles
     const long long chains64 = (long long)p.N * p.HV * (kDim / 64);
-    if (chains64 < num_sms) {
-        chunk::chain::gdn_prefill_chunk_chain_kernel<32><<<(unsigned)(chains64 * 2), chunk::chain::NT,
-                                                           chunk::chain::Cfg<32>::SMEM_BYTES, st>>>(p, ws);
+    const bool split = chains64 < num_sms;
+    PrefillParams q = p;
+    q.cross_gram = split ? 1 : 0;
+    chunk::prep::gdn_prefill_chunk_prep_kernel<<<(unsigned)(slots * p.HV), chunk::prep::NT,
+                                                 chunk::prep::SMEM_BYTES, st>>>(q, ws);
+    if (split) {
+        chunk::chain2::gdn_prefill_chunk_chain2_kernel<<<(unsigned)(chains64 * 2), chunk::chain2::NT,
+                                                         chunk::chain2::SMEM_BYTES, st>>>(q, ws);
     } else {
         chunk::chain::gdn_prefill_chunk_chain_kernel<64><<<(unsigned)chains64, chunk::chain::NT,
                                                            chunk::chain::Cfg<64>::SMEM_BYTES, st>>>(p, ws);

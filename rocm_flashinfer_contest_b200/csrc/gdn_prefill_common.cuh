@@ -27,6 +27,7 @@ struct PrefillParams {
     const long long* ckpt_cu;  // [N + 1]
     long long ckpt_total;
     int ckpt_every;            // > 0, a multiple of 64, when ckpt is set
+    int cross_gram;            // chunked path: the prep also publishes G tiles
 };
 
 // Destination of the checkpoint after `done` tokens of sequence n (done a

@@ -160,7 +160,7 @@ def test_prefill_checkpointed_rejects_bad_arguments(over, code):
 
 def test_prefill_workspace_size(monkeypatch):
     ws = _lib.lib().gdn_prefill_workspace_bytes
-    per_slot = lambda H, HV: HV * 17424 + H * 32768  # noqa: E731
+    per_slot = lambda H, HV: HV * 17424 + H * (32768 + 16384)  # noqa: E731
     monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "128")
     assert ws(1, 8192, 16, 32) == (8192 // 64 + 1) * per_slot(16, 32)
     assert ws(16, 5000, 4, 8) == (5000 // 64 + 16) * per_slot(4, 8)

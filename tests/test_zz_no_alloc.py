@@ -47,7 +47,7 @@ def test_noalloc_matches_workspace_entry_point(cuda_device, monkeypatch):
 
 def test_noalloc_refuses_problems_beyond_its_scratch(cuda_device, monkeypatch):
     monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "0")
-    T, HV = 4096, 32  # (4096 / 64 + 1) slots of 32 * 17,424 + 16 * 32,768 bytes > 16 MiB
+    T, HV = 4096, 32  # (4096 / 64 + 1) slots of 32 * 17,424 + 16 * 49,152 bytes > 16 MiB
     assert _lib.lib().gdn_prefill_workspace_bytes(1, T, 16, HV) > 16 << 20
     st = _lib.lib().gdn_prefill_fwd_noalloc(16, 16, 16, 0, 16, 16, 16, 16, 16, 1, 1, T, 0.0, 16, HV,
                                             128, 128, 16, 16, None)
