@@ -276,11 +276,12 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
         cp_async16(sKQ + umma::kmaj_off(r, c * 8, 128), p.k + row, ok);
         cp_async16(sKQ + umma::kmaj_off(64 + r, c * 8, 128), p.q + row, ok);
     }
-    // the first v-head of a q/k head publishes the chunk's [K ; Q] tile and,
-    // for every chunk after the first, the cross-Gram tile G (the previous
-    // chunk is a full one, so all its rows are valid)
+    // the first v-head of a q/k head publishes the chunk's [K ; Q] tile; for
+    // every chunk after the first the second v-head (the first when there is
+    // only one) publishes the cross-Gram tile G, so the extra work is split
+    // (the previous chunk is a full one, so all its rows are valid)
     const bool publish = hv % p.rep == 0;
-    const bool gram = publish && p.cross_gram && j > 0;
+    const bool gram = (p.rep > 1 ? hv % p.rep == 1 : true) && p.cross_gram && j > 0;
     if (gram) {
         const uint32_t sKP = umma::smem_u32(sm + OFF_KP);
 #pragma unroll
