@@ -177,60 +177,60 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
         for (int r = 0; r < 16; ++r) sT[(b0 + r) * LDA + b0 + lane] = x[r];
     }
     __syncthreads();
-    // off-diagonal blocks, level d = i - j: X_ij = sum_k A_ik T_kj, then
-    // T_ij = -T_ii X_ij.  Thread -> (rows r0, r0 + 1; column c) of a block.
-    const int c = tid & 15, r0 = (tid >> 4) * 2;
-    // outer loops stay rolled: the kernel is large and instruction fetch,
-    // not arithmetic, limits it
+    // Off-diagonal blocks, one column block at a time: for i > j,
+    //   X_ij = sum_{k=j}^{i-1} A_ik T_kj,   T_ij = -T_ii X_ij.
+    // Column blocks are independent once the diagonal inverses exist, so each
+    // warp walks down its own 8 columns of one (warps 0, 3: column block 0)
+    // or two (warps 1, 2: column blocks 1 and 2) column blocks; a lane holds
+    // 4 rows of one column.  Only the warp's own lanes exchange X and T
+    // values, so the walk needs no block-wide barrier.
+    const int half = (warp == 0 || warp == 1) ? 0 : 1;
+    const int cc = 8 * half + (lane & 7);  // column within the column block
+    const int rq = (lane >> 3) * 4;        // first of this lane's 4 rows
+    const int jfirst = (warp == 0 || warp == 3) ? 0 : 1;
+    const int jlast = (warp == 0 || warp == 3) ? 0 : 2;
 #pragma unroll 1
-    for (int d = 1; d < 4; ++d) {
+    for (int j = jfirst; j <= jlast; ++j) {
 #pragma unroll 1
-        for (int j = 0; j + d < 4; ++j) {
-            const int i = j + d;
-            // two partial sums per output row: four independent FMA chains
-            float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+        for (int i = j + 1; i < 4; ++i) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
             for (int k = j; k < i; ++k) {
-                const float* a0 = sA + (16 * i + r0) * LDA + 16 * k;
-                const float* tk = sT + (16 * k) * LDA + 16 * j + c;
+                const float* a = sA + (16 * i + rq) * LDA + 16 * k;
+                const float* t = sT + (16 * k) * LDA + 16 * j + cc;
 #pragma unroll
                 for (int s4 = 0; s4 < 16; s4 += 4) {
-                    const float4 x0 = *reinterpret_cast<const float4*>(a0 + s4);
-                    const float4 x1 = *reinterpret_cast<const float4*>(a0 + LDA + s4);
-                    const float2 tlo = make_float2(tk[(s4 + 0) * LDA], tk[(s4 + 1) * LDA]);
-                    const float2 thi = make_float2(tk[(s4 + 2) * LDA], tk[(s4 + 3) * LDA]);
-                    acc0 = __ffma2_rn(lo2(x0), tlo, acc0);
-                    acc1 = __ffma2_rn(lo2(x1), tlo, acc1);
-                    acc0 = __ffma2_rn(hi2(x0), thi, acc0);
-                    acc1 = __ffma2_rn(hi2(x1), thi, acc1);
+                    const float t0 = t[(s4 + 0) * LDA], t1 = t[(s4 + 1) * LDA];
+                    const float t2 = t[(s4 + 2) * LDA], t3 = t[(s4 + 3) * LDA];
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const float4 x = *reinterpret_cast<const float4*>(a + r * LDA + s4);
+                        acc[r] = fmaf(x.x, t0, fmaf(x.y, t1, fmaf(x.z, t2, fmaf(x.w, t3, acc[r]))));
+                    }
                 }
             }
-            sX[(16 * i + r0 - 16) * LDA + 16 * j + c] = acc0.x + acc0.y;
-            sX[(16 * i + r0 - 15) * LDA + 16 * j + c] = acc1.x + acc1.y;
-        }
-        __syncthreads();
-#pragma unroll 1
-        for (int j = 0; j + d < 4; ++j) {
-            const int i = j + d;
-            const float* t0r = sT + (16 * i + r0) * LDA + 16 * i;
-            const float* xc = sX + (16 * i - 16) * LDA + 16 * j + c;
-            float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) sX[(16 * i - 16 + rq + r) * LDA + 16 * j + cc] = acc[r];
+            __syncwarp();
+            const float* tii = sT + (16 * i + rq) * LDA + 16 * i;
+            const float* xc = sX + (16 * i - 16) * LDA + 16 * j + cc;
+            float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int s4 = 0; s4 < 16; s4 += 4) {
-                const float4 y0 = *reinterpret_cast<const float4*>(t0r + s4);
-                const float4 y1 = *reinterpret_cast<const float4*>(t0r + LDA + s4);
-                const float2 xlo = make_float2(xc[(s4 + 0) * LDA], xc[(s4 + 1) * LDA]);
-                const float2 xhi = make_float2(xc[(s4 + 2) * LDA], xc[(s4 + 3) * LDA]);
-                acc0 = __ffma2_rn(lo2(y0), xlo, acc0);
-                acc1 = __ffma2_rn(lo2(y1), xlo, acc1);
-                acc0 = __ffma2_rn(hi2(y0), xhi, acc0);
-                acc1 = __ffma2_rn(hi2(y1), xhi, acc1);
+                const float x0 = xc[(s4 + 0) * LDA], x1 = xc[(s4 + 1) * LDA];
+                const float x2 = xc[(s4 + 2) * LDA], x3 = xc[(s4 + 3) * LDA];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const float4 y = *reinterpret_cast<const float4*>(tii + r * LDA + s4);
+                    o[r] = fmaf(y.x, x0, fmaf(y.y, x1, fmaf(y.z, x2, fmaf(y.w, x3, o[r]))));
+                }
             }
-            sT[(16 * i + r0) * LDA + 16 * j + c] = -(acc0.x + acc0.y);
-            sT[(16 * i + r0 + 1) * LDA + 16 * j + c] = -(acc1.x + acc1.y);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) sT[(16 * i + rq + r) * LDA + 16 * j + cc] = -o[r];
+            __syncwarp();
         }
-        __syncthreads();
     }
+    __syncthreads();
 }
 
 __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const PrefillParams p, unsigned char* ws) {
