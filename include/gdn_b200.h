@@ -43,7 +43,7 @@ extern "C" {
 #define GDN_ERR_TOO_LARGE 6   /* needs more than gdn_prefill_fwd_noalloc's fixed scratch */
 
 /* Version of this ABI (bumped on any signature change or addition; 3 adds
- * gdn_mtp_fwd and gdn_prefill_fwd_checkpointed). */
+ * gdn_mtp_fwd and gdn_prefill_fwd_checkpointed, 4 gdn_decode_fwd_host). */
 int gdn_abi_version(void);
 
 /* Human-readable text for a status code. */
@@ -69,6 +69,37 @@ int gdn_decode_fwd(const void *q, const void *k, const void *v, const float *sta
                    const float *A_log, const void *a, const float *dt_bias, const void *b,
                    float scale, int B, int H, int HV, int K, int V, void *out,
                    float *new_state, void *stream);
+
+/*
+ * gdn_decode_fwd with every operand in HOST memory (q .. b, state, out and
+ * new_state host pointers; pinned memory for the copies to overlap): for a
+ * caller that keeps the recurrent states off the device between steps.  No
+ * counterpart in the reference, whose `run` takes device tensors
+ * (solutions/gdn_decode/main.py:117-135); the results are bit-identical to
+ * gdn_decode_fwd on device copies of the same inputs.
+ *
+ * The batch is cut into `chunks` slices (0: about 16 MiB of state each, at
+ * most 16).  Slice c is copied up and advanced on `stream` while slice c - 1
+ * is copied back on a stream this library creates per device (with two
+ * events, on the first call); `stream` is made to wait for the last copy
+ * back, so work queued on it afterwards (or a synchronisation of it) sees
+ * the results in `out` and `new_state`.  The state is advanced in place in
+ * `workspace` (device memory, 256-byte aligned, at least
+ * gdn_decode_host_workspace_bytes(B, H, HV) bytes; contents on entry do not
+ * matter), and each call first waits for the previous call's copies back on
+ * this device, so calls may reuse one workspace from any stream.  new_state
+ * may equal state.  Host enqueue is serialised per process by a mutex.  Not
+ * for use inside a stream capture.
+ */
+int gdn_decode_fwd_host(const void *q, const void *k, const void *v, const float *state,
+                        const float *A_log, const void *a, const float *dt_bias, const void *b,
+                        float scale, int B, int H, int HV, int K, int V, void *out,
+                        float *new_state, void *workspace, size_t workspace_bytes, int chunks,
+                        void *stream);
+
+/* Device workspace bytes gdn_decode_fwd_host needs for (B, H, HV) with
+ * K == V == 128: one copy of the state plus the step's inputs and outputs. */
+size_t gdn_decode_host_workspace_bytes(int B, int H, int HV);
 
 /*
  * Variable-length prefill over N sequences packed into T tokens.

@@ -28,6 +28,9 @@ SIGNATURES = {
     "gdn_device_status": (_i, [_i]),
     "gdn_decode_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f,
                             _i, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "gdn_decode_fwd_host": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _f,
+                                 _i, _i, _i, _i, _i, _vp, _vp, _vp, ctypes.c_size_t, _i, _vp]),
+    "gdn_decode_host_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i]),
     "gdn_prefill_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                              _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp, ctypes.c_size_t, _vp]),
     "gdn_prefill_fwd_checkpointed": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,

@@ -1,7 +1,7 @@
 // gdn_abi.cu — version and status-text entry points of the C ABI.
 #include "../../include/gdn_b200.h"
 
-extern "C" int gdn_abi_version(void) { return 3; }
+extern "C" int gdn_abi_version(void) { return 4; }
 
 extern "C" const char* gdn_strerror(int status) {
     switch (status) {

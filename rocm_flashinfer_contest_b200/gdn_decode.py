@@ -15,6 +15,13 @@ solution (solutions/gdn_decode/main.py:117-135) and the contest definition
 Inputs are never modified: ``new_state`` is a fresh tensor, as in the
 reference (main.py:104).
 
+``run_host_into(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)``
+is the same decode for a caller whose states live in (pinned) host memory,
+e.g. a serving loop that offloads recurrent states between steps: the batch
+is cut into chunks, chunk i + 1 is copied up while chunk i's results are
+copied back (PCIe moves data both ways at once), and each chunk runs the same
+kernel, so the results are identical to ``run`` on device copies.
+
 ``gated_delta_rule_decode_pretranspose(...)`` is flashinfer's serving decode
 API (flashinfer/gdn_decode.py:118-330): state fp32 or bf16 ([B, HV, V, K],
 updated in place) or a slot pool (``initial_state`` + ``initial_state_indices``,
@@ -127,3 +134,52 @@ def gated_delta_rule_decode_pretranspose(q, k, v, state, A_log, a, dt_bias, b, s
         target.copy_(out.view(target.shape))
         out = target
     return out, (initial_state if use_pool else state)
+
+
+def run_host_into(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state, *, device=None,
+                  chunks: int = 0):
+    """Decode with every tensor in pinned host memory (``gdn_decode_fwd_host``):
+    writes ``output`` [B,1,HV,V] bf16 and ``new_state`` [B,HV,V,K] fp32 (host,
+    pinned; ``new_state`` may be ``state``) and returns them.  The work is
+    queued on ``device`` (default: the current CUDA device) on its current
+    stream, which continues after the last copy back, so
+    ``torch.cuda.current_stream().synchronize()`` (or an event recorded on
+    it) marks the results as ready.  ``chunks`` batch slices pipeline the two
+    copy directions (0: about 16 MiB of state each).  The inputs must stay
+    unmodified and alive until then, as with any non-blocking copy."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    host = {"q": q, "k": k, "v": v, "a": a, "b": b, "A_log": A_log, "dt_bias": dt_bias,
+            "output": output, "new_state": new_state}
+    if state is not None:
+        host["state"] = state
+    for name, t in host.items():
+        if not isinstance(t, torch.Tensor) or t.device.type != "cpu" or not t.is_pinned() or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous pinned host tensor")
+    if q.dim() != 4 or q.shape[1] != 1:
+        raise ValueError(f"q must be [B, 1, H, K], got {tuple(q.shape)}")
+    B, _, H, K = q.shape
+    if v.dim() != 4:
+        raise ValueError(f"v must be [B, 1, HV, V], got {tuple(v.shape)}")
+    HV, V = v.shape[2], v.shape[3]
+    bf, f32 = torch.bfloat16, torch.float32
+    spec = {"q": (bf, (B, 1, H, K)), "k": (bf, (B, 1, H, K)), "v": (bf, (B, 1, HV, V)),
+            "a": (bf, (B, 1, HV)), "b": (bf, (B, 1, HV)), "A_log": (f32, (HV,)), "dt_bias": (f32, (HV,)),
+            "output": (bf, (B, 1, HV, V)), "new_state": (f32, (B, HV, V, K)), "state": (f32, (B, HV, V, K))}
+    for name, t in host.items():
+        dt, shp = spec[name]
+        if t.dtype != dt or tuple(t.shape) != shp:
+            raise ValueError(f"{name} must be {dt} {shp}, got {t.dtype} {tuple(t.shape)}")
+    if B == 0:
+        return output, new_state
+    L = lib()
+    # allocated on the stream the call joins at its end, so freeing it when
+    # this function returns is ordered after the last copy back
+    with torch.cuda.device(dev):
+        ws = torch.empty(L.gdn_decode_host_workspace_bytes(B, H, HV), dtype=torch.uint8, device=dev)
+        rc = L.gdn_decode_fwd_host(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), None if state is None else state.data_ptr(),
+            A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), C.normalize_scale(scale, K),
+            B, H, HV, K, V, output.data_ptr(), new_state.data_ptr(), ws.data_ptr(), ws.numel(), int(chunks),
+            C.stream_handle(dev))
+    check("gdn_decode_fwd_host", rc)
+    return output, new_state

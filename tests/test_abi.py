@@ -45,7 +45,7 @@ def test_python_signatures_cover_the_header():
 
 def test_version_and_strerror():
     lib = _lib.lib()
-    assert lib.gdn_abi_version() == 3
+    assert lib.gdn_abi_version() == 4
     for code in (0, 1, 2, 3, 4):
         assert lib.gdn_strerror(code)
     assert b"unknown" in lib.gdn_strerror(99)
@@ -80,6 +80,41 @@ def _prefill(**over):
 ])
 def test_decode_rejects_bad_arguments(over, code):
     assert _decode(**over) == code
+
+
+def _decode_host(**over):
+    B, H, HV = over.get("B", 2), over.get("H", 1), over.get("HV", 2)
+    need = _lib.lib().gdn_decode_host_workspace_bytes(max(B, 1), H, HV)
+    d = dict(q=16, k=16, v=16, state=16, A_log=16, a=16, dt_bias=16, b=16, scale=0.0,
+             B=B, H=H, HV=HV, K=128, V=128, out=16, new_state=16, ws=4096, ws_bytes=need,
+             chunks=0, stream=None)
+    d.update(over)
+    return _lib.lib().gdn_decode_fwd_host(*d.values())
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(K=64), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(H=3, HV=8), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(B=-1), _lib.GDN_ERR_INVALID),
+    (dict(chunks=-1), _lib.GDN_ERR_INVALID),
+    (dict(out=None), _lib.GDN_ERR_INVALID),
+    (dict(ws=None), _lib.GDN_ERR_INVALID),
+    (dict(ws_bytes=1024), _lib.GDN_ERR_INVALID),           # smaller than the workspace needs
+    (dict(ws=4096 + 128), _lib.GDN_ERR_ALIGN),             # workspace must be 256-byte aligned
+    (dict(B=0), _lib.GDN_OK),                              # nothing to do: no CUDA call
+])
+def test_decode_host_rejects_bad_arguments(over, code):
+    assert _decode_host(**over) == code
+
+
+def test_decode_host_workspace_bytes():
+    f = _lib.lib().gdn_decode_host_workspace_bytes
+    up = lambda x: (x + 255) // 256 * 256  # noqa: E731
+    B, H, HV = 64, 16, 32
+    want = (up(B * HV * 128 * 128 * 4) + 2 * up(B * H * 128 * 2) + 2 * up(B * HV * 128 * 2)
+            + 2 * up(B * HV * 2) + 2 * up(HV * 4))
+    assert f(B, H, HV) == want
+    assert f(0, H, HV) == 0 and f(B, 0, HV) == 0
 
 
 @pytest.mark.parametrize("over,code", [

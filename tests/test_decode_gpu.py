@@ -160,3 +160,57 @@ def test_decode_default_scale_value(cuda_device):
     args[8] = 1 / math.sqrt(128)
     o1, _ = gdn_decode.run(*args)
     assert torch.equal(o0, o1)
+
+
+@pytest.mark.parametrize("B,with_state,chunks", [(64, True, 8), (64, True, 0), (13, True, 4), (13, True, 3),
+                                                  (5, False, 8), (1, True, 0), (3, True, 1)])
+def test_decode_host_buffers_match_device_run(cuda_device, B, with_state, chunks):
+    """run_host_into (pinned host tensors, chunked copies both ways) gives
+    exactly the device run's results and leaves its inputs untouched."""
+    args = inputs.decode_inputs(B, 16, 32, seed=70 + B, with_state=with_state)
+    host = [x.pin_memory() if isinstance(x, torch.Tensor) else x for x in args]
+    before = [x.clone() if isinstance(x, torch.Tensor) else x for x in host]
+    out = torch.empty((B, 1, 32, 128), dtype=torch.bfloat16).pin_memory()
+    ns = torch.full((B, 32, 128, 128), float("nan")).pin_memory()
+    gdn_decode.run_host_into(*host, out, ns, device=cuda_device, chunks=chunks)
+    torch.cuda.current_stream(cuda_device).synchronize()
+    ro, rs = gdn_decode.run(*inputs.to_device(args, cuda_device))
+    torch.cuda.synchronize()
+    assert torch.equal(out, ro.cpu())
+    assert torch.equal(ns, rs.cpu())
+    for x, y in zip(host, before):
+        if isinstance(x, torch.Tensor):
+            assert torch.equal(x, y)
+
+
+def test_decode_host_buffers_reject_unpinned(cuda_device):
+    args = inputs.decode_inputs(2, 4, 8, seed=80)
+    out = torch.empty((2, 1, 8, 128), dtype=torch.bfloat16).pin_memory()
+    ns = torch.empty((2, 8, 128, 128)).pin_memory()
+    with pytest.raises(ValueError):
+        gdn_decode.run_host_into(*args, out, ns, device=cuda_device)
+
+
+def test_decode_host_buffers_in_place_and_back_to_back(cuda_device):
+    """Two calls queued without a synchronisation between them (the second
+    reuses the first one's workspace memory) and a host state advanced in
+    place give the device runs' results."""
+    B = 24
+    a1 = inputs.decode_inputs(B, 16, 32, seed=91)
+    a2 = inputs.decode_inputs(B, 16, 32, seed=92)
+    h1 = [x.pin_memory() if isinstance(x, torch.Tensor) else x for x in a1]
+    h2 = [x.pin_memory() if isinstance(x, torch.Tensor) else x for x in a2]
+    o1 = torch.empty((B, 1, 32, 128), dtype=torch.bfloat16).pin_memory()
+    o2 = torch.empty_like(o1).pin_memory()
+    s2 = h2[3]                                   # advanced in place
+    scratch = torch.empty_like(h1[3]).pin_memory()   # kept alive until the synchronisation
+    gdn_decode.run_host_into(*h1, o1, scratch, device=cuda_device, chunks=5)
+    ns1 = torch.empty_like(h1[3]).pin_memory()
+    gdn_decode.run_host_into(*h1, o1, ns1, device=cuda_device, chunks=2)
+    gdn_decode.run_host_into(*h2, o2, s2, device=cuda_device, chunks=7)
+    torch.cuda.current_stream(cuda_device).synchronize()
+    r1o, r1s = gdn_decode.run(*inputs.to_device(a1, cuda_device))
+    r2o, r2s = gdn_decode.run(*inputs.to_device(a2, cuda_device))
+    torch.cuda.synchronize()
+    assert torch.equal(o1, r1o.cpu()) and torch.equal(ns1, r1s.cpu())
+    assert torch.equal(o2, r2o.cpu()) and torch.equal(s2, r2s.cpu())
