@@ -42,8 +42,12 @@ extern "C" {
 #define GDN_ERR_DEVICE 5      /* a kernel reported an error (bounded wait timed out) */
 #define GDN_ERR_TOO_LARGE 6   /* needs more than gdn_prefill_fwd_noalloc's fixed scratch */
 
+/* flags of gdn_prefill_fwd_ex */
+#define GDN_PREFILL_QK_L2NORM 1 /* normalise q and k in the kernel: x * rsqrt(sum(x^2) + 1e-6) */
+
 /* Version of this ABI (bumped on any signature change or addition; 3 adds
- * gdn_mtp_fwd and gdn_prefill_fwd_checkpointed, 4 gdn_decode_fwd_host). */
+ * gdn_mtp_fwd and gdn_prefill_fwd_checkpointed, 4 gdn_decode_fwd_host and
+ * gdn_prefill_fwd_ex). */
 int gdn_abi_version(void);
 
 /* Human-readable text for a status code. */
@@ -146,6 +150,28 @@ int gdn_prefill_fwd_checkpointed(const void *q, const void *k, const void *v, co
                                  float *state_checkpoints, const int64_t *checkpoint_cu_starts,
                                  long long num_checkpoints, int checkpoint_every_n_tokens,
                                  void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * gdn_prefill_fwd with every option: checkpoints as in
+ * gdn_prefill_fwd_checkpointed when state_checkpoints is not NULL (then
+ * checkpoint_every_n_tokens > 0; NULL needs 0, as flashinfer requires,
+ * flashinfer/gdn_prefill.py:187-206), and `flags`:
+ *   GDN_PREFILL_QK_L2NORM  q and k head vectors are L2-normalised in the
+ *                          kernel, x * rsqrt(sum(x^2) + 1e-6): the option
+ *                          use_qk_l2norm_in_kernel of the AITER kernels the
+ *                          reference calls (solutions/gdn_prefill/main.py:72,79),
+ *                          FLA's rule (fla/modules/l2norm.py:42).  The chunked
+ *                          kernels keep the unit vectors in f16, the
+ *                          token-serial kernel in fp32.
+ * Unknown flag bits return GDN_ERR_INVALID.  Workspace as gdn_prefill_fwd.
+ */
+int gdn_prefill_fwd_ex(const void *q, const void *k, const void *v, const float *state,
+                       const float *A_log, const void *a, const float *dt_bias, const void *b,
+                       const void *cu_seqlens, int cu_seqlens_is_int64, int N, int T,
+                       float scale, int H, int HV, int K, int V, void *out, float *new_state,
+                       float *state_checkpoints, const int64_t *checkpoint_cu_starts,
+                       long long num_checkpoints, int checkpoint_every_n_tokens, int flags,
+                       void *workspace, size_t workspace_bytes, void *stream);
 
 /*
  * Workspace bytes gdn_prefill_fwd needs for (N, T, H, HV): 0 when the call

@@ -128,14 +128,27 @@ int gdn_oracle_decode(const float *q, const float *k, const float *v, const floa
     return 0;
 }
 
+/* q/k L2 normalisation, x / sqrt(sum(x^2) + 1e-6) (on == 0: a plain copy). */
+static void l2norm_copy(float *dst, const float *src, int K, int on) {
+    float ss = 0.0f;
+    for (int i = 0; i < K; ++i) ss += src[i] * src[i];
+    float inv = on ? 1.0f / sqrtf(ss + 1e-6f) : 1.0f;
+    for (int i = 0; i < K; ++i) dst[i] = src[i] * inv;
+}
+
 /* ckpt (optional): the state after tokens every, 2*every, ... of sequence n
  * is copied to ckpt[ckpt_cu[n] + i] (flashinfer's chunk_gated_delta_rule
- * checkpoints, flashinfer/gdn_prefill.py:161-174). */
+ * checkpoints, flashinfer/gdn_prefill.py:161-174).  qk_l2norm != 0 first
+ * normalises each q and k head vector (l2norm_copy): the option
+ * use_qk_l2norm_in_kernel of the AITER kernels the reference calls
+ * (solutions/gdn_prefill/main.py:72,79, there False), whose rule is FLA's
+ * l2norm, 1 / sqrt(sum(x^2) + eps) with eps = 1e-6 (fla/modules/l2norm.py:42,140). */
 int gdn_oracle_prefill(const float *q, const float *k, const float *v, const float *state,
                        const float *A_log, const float *a, const float *dt_bias,
                        const float *b, const int64_t *cu_seqlens, int N, int T, float scale,
                        int H, int HV, int K, int V, uint16_t *out_bf16, float *new_state,
-                       float *ckpt, const int64_t *ckpt_cu, int every, int nthreads) {
+                       float *ckpt, const int64_t *ckpt_cu, int every, int qk_l2norm,
+                       int nthreads) {
     if (ckpt && (every <= 0 || !ckpt_cu)) return 1;
     if (N < 0 || T < 0 || H <= 0 || HV <= 0 || K <= 0 || V <= 0 || HV % H) return 1;
     if (N > 0 && (cu_seqlens[0] < 0 || cu_seqlens[N] > T)) return 1;
@@ -159,11 +172,13 @@ int gdn_oracle_prefill(const float *q, const float *k, const float *v, const flo
         if (state) memcpy(S, state + (size_t)nh * V * K, sizeof(float) * (size_t)V * K);
         else memset(S, 0, sizeof(float) * (size_t)V * K);
         float *o = (float *)malloc(sizeof(float) * V);
+        float *qn = (float *)malloc(sizeof(float) * K), *kn = (float *)malloc(sizeof(float) * K);
         for (int64_t t = t0; t < t1; ++t) {
             float g, beta;
             gates(A_log[h], a[(size_t)t * HV + h], dt_bias[h], b[(size_t)t * HV + h], &g, &beta);
-            step_head(S, q + ((size_t)t * H + hq) * K, k + ((size_t)t * H + hq) * K,
-                      v + ((size_t)t * HV + h) * V, g, beta, scale, K, V, o);
+            l2norm_copy(qn, q + ((size_t)t * H + hq) * K, K, qk_l2norm);
+            l2norm_copy(kn, k + ((size_t)t * H + hq) * K, K, qk_l2norm);
+            step_head(S, qn, kn, v + ((size_t)t * HV + h) * V, g, beta, scale, K, V, o);
             for (int vi = 0; vi < V; ++vi)
                 out_bf16[((size_t)t * HV + h) * V + vi] = f32_to_bf16_rne(o[vi]);
             if (ckpt && (t - t0 + 1) % every == 0) {
@@ -172,6 +187,8 @@ int gdn_oracle_prefill(const float *q, const float *k, const float *v, const flo
             }
         }
         free(o);
+        free(qn);
+        free(kn);
     }
     return 0;
 }
@@ -195,13 +212,6 @@ int gdn_oracle_prefill(const float *q, const float *k, const float *v, const flo
  * output slot skips the write.  round_bf16 != 0 is the bf16-state form
  * (gdn_decode.py:206-260): pool_in holds bf16 values (widened), the state is
  * advanced in fp32 and rounded to bf16 (nearest even) once, when stored. */
-static void l2norm_copy(float *dst, const float *src, int K, int on) {
-    float ss = 0.0f;
-    for (int i = 0; i < K; ++i) ss += src[i] * src[i];
-    float inv = on ? 1.0f / sqrtf(ss + 1e-6f) : 1.0f;
-    for (int i = 0; i < K; ++i) dst[i] = src[i] * inv;
-}
-
 static float round_bf16(float f) {
     uint32_t u = (uint32_t)f32_to_bf16_rne(f) << 16;
     float r;

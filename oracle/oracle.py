@@ -60,7 +60,7 @@ def _load():
         _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i64p,
         ctypes.c_int, ctypes.c_int, ctypes.c_float,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-        _u16p, _f32p, _f32p, _i64p, ctypes.c_int, ctypes.c_int,
+        _u16p, _f32p, _f32p, _i64p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
     ]
     lib.gdn_oracle_mtp.restype = ctypes.c_int
     lib.gdn_oracle_mtp.argtypes = [
@@ -118,9 +118,11 @@ def checkpoint_cu_starts(cu_seqlens, every: int) -> torch.Tensor:
 
 
 def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: int = 0,
-            checkpoint_every_n_tokens: int = 0):
+            checkpoint_every_n_tokens: int = 0, qk_l2norm: bool = False):
     """Returns (output, new_state), plus the checkpoints [total, HV, V, K] when
-    checkpoint_every_n_tokens > 0."""
+    checkpoint_every_n_tokens > 0.  qk_l2norm normalises every q and k head
+    vector as x / sqrt(sum(x^2) + 1e-6) first (AITER's / FLA's
+    use_qk_l2norm_in_kernel, fla/modules/l2norm.py:42)."""
     lib = _load()
     T, H, K = q.shape
     HV, V = v.shape[1], v.shape[2]
@@ -141,7 +143,7 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: in
         _ptr(Af, _f32p), _ptr(af, _f32p), _ptr(dtf, _f32p), _ptr(bf, _f32p), _ptr(cu, _i64p),
         N, T, _scale(scale, K), H, HV, K, V,
         _ptr(out, _u16p), _ptr(new_state, _f32p), _ptr(ckpt, _f32p), _ptr(ckpt_cu, _i64p), every,
-        int(threads))
+        int(bool(qk_l2norm)), int(threads))
     if rc != 0:
         raise ValueError(f"gdn_oracle_prefill rejected its arguments (rc={rc})")
     if every > 0:

@@ -33,9 +33,10 @@ static int prefill_impl(const void* q, const void* k, const void* v, const float
                         const float* A_log, const void* a, const float* dt_bias, const void* b,
                         const void* cu_seqlens, int cu_seqlens_is_int64, int N, int T, float scale,
                         int H, int HV, int K, int V, void* out, float* new_state, float* ckpt,
-                        const int64_t* ckpt_cu, long long ckpt_total, int ckpt_every, void* workspace,
-                        size_t workspace_bytes, void* stream) {
+                        const int64_t* ckpt_cu, long long ckpt_total, int ckpt_every, int flags,
+                        void* workspace, size_t workspace_bytes, void* stream) {
     if (N < 0 || T < 0 || H <= 0 || HV <= 0) return GDN_ERR_INVALID;
+    if (flags & ~GDN_PREFILL_QK_L2NORM) return GDN_ERR_INVALID;
     if (ckpt != nullptr && (ckpt_every <= 0 || ckpt_every % 64 != 0 || !ckpt_cu || ckpt_total < 0))
         return GDN_ERR_INVALID;
     if (ckpt != nullptr && (!gdn_aligned(ckpt, 16) || !gdn_aligned(ckpt_cu, 8))) return GDN_ERR_ALIGN;
@@ -76,6 +77,7 @@ static int prefill_impl(const void* q, const void* k, const void* v, const float
     p.ckpt_total = ckpt_total;
     p.ckpt_every = ckpt != nullptr ? ckpt_every : 0;
     p.cross_gram = 0;
+    p.qk_l2norm = (flags & GDN_PREFILL_QK_L2NORM) != 0;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (N == 0) {
         // no sequence: every token is uncovered, its output is zero
@@ -100,7 +102,8 @@ extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, cons
                                float* new_state, void* workspace, size_t workspace_bytes,
                                void* stream) {
     return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64, N, T, scale,
-                        H, HV, K, V, out, new_state, nullptr, nullptr, 0, 0, workspace, workspace_bytes, stream);
+                        H, HV, K, V, out, new_state, nullptr, nullptr, 0, 0, 0, workspace, workspace_bytes,
+                        stream);
 }
 
 extern "C" int gdn_prefill_fwd_checkpointed(const void* q, const void* k, const void* v, const float* state,
@@ -114,5 +117,19 @@ extern "C" int gdn_prefill_fwd_checkpointed(const void* q, const void* k, const 
     if (!state_checkpoints) return GDN_ERR_INVALID;
     return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64, N, T, scale,
                         H, HV, K, V, out, new_state, state_checkpoints, checkpoint_cu_starts, num_checkpoints,
-                        checkpoint_every_n_tokens, workspace, workspace_bytes, stream);
+                        checkpoint_every_n_tokens, 0, workspace, workspace_bytes, stream);
+}
+
+extern "C" int gdn_prefill_fwd_ex(const void* q, const void* k, const void* v, const float* state,
+                                  const float* A_log, const void* a, const float* dt_bias, const void* b,
+                                  const void* cu_seqlens, int cu_seqlens_is_int64, int N, int T, float scale,
+                                  int H, int HV, int K, int V, void* out, float* new_state,
+                                  float* state_checkpoints, const int64_t* checkpoint_cu_starts,
+                                  long long num_checkpoints, int checkpoint_every_n_tokens, int flags,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+    // checkpoints: all of them or none (flashinfer/gdn_prefill.py:187-206)
+    if ((state_checkpoints == nullptr) != (checkpoint_every_n_tokens == 0)) return GDN_ERR_INVALID;
+    return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64, N, T, scale,
+                        H, HV, K, V, out, new_state, state_checkpoints, checkpoint_cu_starts, num_checkpoints,
+                        checkpoint_every_n_tokens, flags, workspace, workspace_bytes, stream);
 }

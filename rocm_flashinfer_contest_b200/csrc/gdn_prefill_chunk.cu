@@ -101,6 +101,32 @@ __device__ __forceinline__ void unpack_bf16x8(const uint4& raw, float* x) {
     }
 }
 
+// L2-normalises row `row` of a bf16 K-major tile (`rows` rows, 128 columns)
+// in place and stores it as f16: x * rsqrt(sum(x^2) + 1e-6) in fp32 (the
+// rule of FLA's l2norm behind AITER's use_qk_l2norm_in_kernel,
+// fla/modules/l2norm.py:42).  f16 keeps 3 more mantissa bits of the unit
+// vector than bf16; every later use of the tile reads it as f16.
+__device__ __forceinline__ void l2norm_row_to_f16(unsigned char* tile, uint32_t row, uint32_t rows) {
+    float ss = 0.f;
+#pragma unroll 4
+    for (uint32_t c = 0; c < kDim; c += 8) {
+        float x[8];
+        unpack_bf16x8(*reinterpret_cast<const uint4*>(tile + umma::kmaj_off(row, c, rows)), x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(x[e], x[e], ss);
+    }
+    const float inv = rsqrtf(ss + 1e-6f);
+#pragma unroll 4
+    for (uint32_t c = 0; c < kDim; c += 8) {
+        const uint32_t off = umma::kmaj_off(row, c, rows);
+        float x[8];
+        unpack_bf16x8(*reinterpret_cast<const uint4*>(tile + off), x);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] *= inv;
+        st_f16x8(tile, off, x);
+    }
+}
+
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
     // src-size 0 zero-fills the 16 bytes without reading memory
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
@@ -320,13 +346,20 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
     __syncthreads();
     if (warp == 1) sG[tid] = lg + sG[31];
     cp_async_wait_all();
+    if (p.qk_l2norm) {
+        // thread r normalises row r of [K ; Q] (and of K_{j-1}); rows past
+        // the sequence are zero and stay zero
+        __syncthreads();
+        l2norm_row_to_f16(sm + OFF_KQ, tid, 128);
+        if (gram && tid < C) l2norm_row_to_f16(sm + OFF_KP, tid, 64);
+    }
     sync_for_mma();
     const uint32_t tmem = tmem_base_sh;
     const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
 
-    // MMA_A: [K ; Q] K^T in bf16; MMA_G: [K ; Q] K_{j-1}^T
+    // MMA_A: [K ; Q] K^T (bf16, or f16 once normalised); MMA_G: [K ; Q] K_{j-1}^T
     if (tid == 0) {
-        constexpr uint32_t ID = umma::idesc_f16(128, 64, 1, 1, 0, 0);
+        const uint32_t ID = p.qk_l2norm ? umma::idesc_f16(128, 64, 0, 0, 0, 0) : umma::idesc_f16(128, 64, 1, 1, 0, 0);
 #pragma unroll
         for (int k0 = 0; k0 < kDim; k0 += 16)
             umma::mma_f16(tmem, umma::desc_kmaj(sKQ, 128, k0), umma::desc_kmaj(sKQ, 128, k0), ID, k0 > 0);
@@ -362,6 +395,11 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
     // tile for the chain kernel: the same swizzled layout, converted to f16
     if (publish) {
         uint4* dst = reinterpret_cast<uint4*>(ws_kq(p, ws) + ((size_t)s * p.H + hq) * kTileKQ);
+        if (p.qk_l2norm) {  // already f16
+#pragma unroll 4
+            for (int idx = tid; idx < (int)(kTileKQ / 16); idx += NT)
+                dst[idx] = reinterpret_cast<const uint4*>(sm + OFF_KQ)[idx];
+        } else
 #pragma unroll 4
         for (int idx = tid; idx < (int)(kTileKQ / 16); idx += NT) {
             float x[8];

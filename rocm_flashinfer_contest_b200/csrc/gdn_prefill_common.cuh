@@ -28,6 +28,7 @@ struct PrefillParams {
     long long ckpt_total;
     int ckpt_every;            // > 0, a multiple of 64, when ckpt is set
     int cross_gram;            // chunked path: the prep also publishes G tiles
+    int qk_l2norm;             // normalise q and k rows in the kernel: x * rsqrt(sum(x^2) + 1e-6)
 };
 
 // Destination of the checkpoint after `done` tokens of sequence n (done a

@@ -9,7 +9,8 @@
 // kernel), so a head is split over 8 CTAs and nothing but the inputs and the
 // outputs moves through memory.  The next token's q/k/v/gates are loaded
 // while the current token is processed.  With checkpoints enabled the rows
-// are also stored after every `ckpt_every` tokens.
+// are also stored after every `ckpt_every` tokens.  With qk_l2norm the q and
+// k head vectors are normalised in registers, in fp32, before they are used.
 #include "gdn_common.cuh"
 #include "gdn_prefill_common.cuh"
 
@@ -92,6 +93,26 @@ __global__ void __launch_bounds__(128) gdn_prefill_recurrent_kernel(const Prefil
         }
         const float g = expf(log_gate(A_log, bf16_to_f32(cur.a), dt_bias));
         const float beta = sigmoidf_(bf16_to_f32(cur.b));
+        if (p.qk_l2norm) {
+            // the 8 lanes of a row hold a whole q and k head vector
+            float qq = 0.f, kk = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                qq += dot4r(qf[j], qf[j]);
+                kk += dot4r(kf[j], kf[j]);
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) {
+                qq += __shfl_xor_sync(0xffffffffu, qq, o);
+                kk += __shfl_xor_sync(0xffffffffu, kk, o);
+            }
+            const float iq = rsqrtf(qq + 1e-6f), ik = rsqrtf(kk + 1e-6f);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                qf[j] = make_float4(qf[j].x * iq, qf[j].y * iq, qf[j].z * iq, qf[j].w * iq);
+                kf[j] = make_float4(kf[j].x * ik, kf[j].y * ik, kf[j].z * ik, kf[j].w * ik);
+            }
+        }
         float kq = dot4r(kf[0], qf[0]) + dot4r(kf[1], qf[1]) + dot4r(kf[2], qf[2]) + dot4r(kf[3], qf[3]);
         float2 sk2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);
 #pragma unroll

@@ -22,6 +22,9 @@ chunk_gated_delta_rule, flashinfer/gdn_prefill.py:113-115,161-214):
 ``checkpoint_cu_starts_for``) and ``checkpoint_every_n_tokens`` (a positive
 multiple of 64, 0 = off): the state after tokens every, 2*every, ... of each
 sequence is written to its slots.
+``use_qk_l2norm_in_kernel=True`` (keyword-only, the option of the AITER
+kernels the reference calls, solutions/gdn_prefill/main.py:72,79) normalises
+every q and k head vector in the kernel as x * rsqrt(sum(x^2) + 1e-6).
 Inputs are never modified; ``run_into`` is the destination-passing form and
 accepts ``new_state is state``.  The chunked kernels' workspace
 (gdn_prefill_workspace_bytes) comes from torch's caching allocator, so a
@@ -34,6 +37,7 @@ import torch
 from . import _common as C
 from ._lib import check, lib
 
+GDN_PREFILL_QK_L2NORM = 1  # gdn_prefill_fwd_ex flag (include/gdn_b200.h)
 
 def _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens):
     dev = C.cuda_device_of(q)
@@ -106,7 +110,8 @@ def _validate_checkpoints(state_checkpoints, checkpoint_cu_starts, every, N, HV,
 
 
 def run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, *,
-             state_checkpoints=None, checkpoint_cu_starts=None, checkpoint_every_n_tokens: int = 0):
+             state_checkpoints=None, checkpoint_cu_starts=None, checkpoint_every_n_tokens: int = 0,
+             use_qk_l2norm_in_kernel: bool = False):
     """Destination-passing prefill into ``output`` [T,HV,V] bf16 and
     ``new_state`` [N,HV,V,K] fp32 (``new_state`` may be ``state``)."""
     dev, args, (T, N, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
@@ -122,29 +127,32 @@ def run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, ne
     scale = C.normalize_scale(scale, K)
     ws_bytes = lib().gdn_prefill_workspace_bytes(N, T, H, HV)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
-    if ck is None:
+    if ck is None and not use_qk_l2norm_in_kernel:
         st = lib().gdn_prefill_fwd(
             C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(state), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias),
             C.ptr(b), C.ptr(cu), 1 if cu.dtype == torch.int64 else 0, N, T, scale, H, HV, K, V,
             C.ptr(output), C.ptr(new_state), C.ptr(ws), ws_bytes, C.stream_handle(dev))
         check("gdn_prefill_fwd", st)
     else:
-        ckpt, ckpt_cu, every = ck
-        st = lib().gdn_prefill_fwd_checkpointed(
+        ckpt, ckpt_cu, every = ck if ck is not None else (None, None, 0)
+        st = lib().gdn_prefill_fwd_ex(
             C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(state), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias),
             C.ptr(b), C.ptr(cu), 1 if cu.dtype == torch.int64 else 0, N, T, scale, H, HV, K, V,
-            C.ptr(output), C.ptr(new_state), C.ptr(ckpt), C.ptr(ckpt_cu), ckpt.shape[0], every,
+            C.ptr(output), C.ptr(new_state), C.ptr(ckpt), C.ptr(ckpt_cu),
+            0 if ckpt is None else ckpt.shape[0], every, GDN_PREFILL_QK_L2NORM if use_qk_l2norm_in_kernel else 0,
             C.ptr(ws), ws_bytes, C.stream_handle(dev))
-        check("gdn_prefill_fwd_checkpointed", st)
+        check("gdn_prefill_fwd_ex", st)
     return output, new_state
 
 
 def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *,
-        state_checkpoints=None, checkpoint_cu_starts=None, checkpoint_every_n_tokens: int = 0):
+        state_checkpoints=None, checkpoint_cu_starts=None, checkpoint_every_n_tokens: int = 0,
+        use_qk_l2norm_in_kernel: bool = False):
     """Contest entry point; see the module docstring."""
     dev, _, (T, N, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
     output = torch.empty((T, HV, V), dtype=torch.bfloat16, device=dev)
     new_state = torch.empty((N, HV, V, K), dtype=torch.float32, device=dev)
     return run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
                     state_checkpoints=state_checkpoints, checkpoint_cu_starts=checkpoint_cu_starts,
-                    checkpoint_every_n_tokens=checkpoint_every_n_tokens)
+                    checkpoint_every_n_tokens=checkpoint_every_n_tokens,
+                    use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)

@@ -46,6 +46,15 @@ PREFILL_CASES = [
     ("pre_gva4_extreme", [9, 3], 1, 4, 16, True, 1.0, 14, torch.int64),
 ]
 
+# (name, seqlens, H, HV, K, seed): raw (unnormalised) q/k, normalised the way
+# AITER's / FLA's use_qk_l2norm_in_kernel does (x / sqrt(sum(x^2) + 1e-6),
+# fla/modules/l2norm.py:42) before the template runs; the fixture keeps the
+# raw q/k and a qk_l2norm flag
+PREFILL_L2_CASES = [
+    ("pre_l2norm", [45, 0, 70], 2, 4, 32, 17),
+    ("pre_l2norm_k128", [33, 64], 1, 2, 128, 18),
+]
+
 # (name, seqlens, checkpoint_every_n_tokens, seed); H = 1, HV = 2, K = V = 16
 CKPT_CASES = [
     ("ckpt_every64", [130, 0, 200, 64], 64, 15),
@@ -121,6 +130,24 @@ def main():
             if t is not None:
                 out[f"{name}/{kname}"] = _np(t)
         out[f"{name}/scale"] = np.float32(scale)
+        out[f"{name}/out"] = _np(o)
+        out[f"{name}/new_state"] = _np(s)
+    for name, lens, H, HV, K, seed in PREFILL_L2_CASES:
+        args = prefill_inputs(lens, H, HV, K, K, seed=seed, with_state=True, cu_dtype=torch.int64)
+        args[9] = 0.0
+        run_args = list(args[:10])
+        g = torch.Generator().manual_seed(seed + 100)
+        for i in (0, 1):
+            raw = (torch.randn(args[i].shape, generator=g) * 3.0).to(torch.bfloat16)
+            args[i] = raw
+            xf = raw.float()
+            run_args[i] = xf / torch.sqrt((xf * xf).sum(-1, keepdim=True) + 1e-6)
+        o, s = _gdn_prefill_reference(*run_args)
+        keys = ["q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens"]
+        for kname, t in zip(keys, args[:9]):
+            out[f"{name}/{kname}"] = _np(t)
+        out[f"{name}/qk_l2norm"] = np.int32(1)
+        out[f"{name}/scale"] = np.float32(0.0)
         out[f"{name}/out"] = _np(o)
         out[f"{name}/new_state"] = _np(s)
     # state checkpoints (flashinfer's chunk_gated_delta_rule, gdn_prefill.py:161-174):

@@ -193,6 +193,29 @@ def test_prefill_checkpointed_rejects_bad_arguments(over, code):
     assert _prefill_ckpt(**over) == code
 
 
+def _prefill_ex(**over):
+    d = dict(q=16, k=16, v=16, state=16, A_log=16, a=16, dt_bias=16, b=16, cu=16, cu64=1,
+             N=1, T=4, scale=0.0, H=1, HV=2, K=128, V=128, out=16, new_state=16,
+             ckpt=None, ckpt_cu=None, total=0, every=0, flags=0, ws=None, ws_bytes=0, stream=None)
+    d.update(over)
+    return _lib.lib().gdn_prefill_fwd_ex(*d.values())
+
+
+@pytest.mark.parametrize("over,code", [
+    (dict(flags=2), _lib.GDN_ERR_INVALID),                 # unknown flag bit
+    (dict(flags=-1), _lib.GDN_ERR_INVALID),
+    (dict(every=64), _lib.GDN_ERR_INVALID),                # every > 0 without checkpoints
+    (dict(ckpt=16, ckpt_cu=16, total=1), _lib.GDN_ERR_INVALID),  # checkpoints with every == 0
+    (dict(ckpt=16, ckpt_cu=16, total=1, every=96), _lib.GDN_ERR_INVALID),
+    (dict(ckpt=24, ckpt_cu=16, total=1, every=64), _lib.GDN_ERR_ALIGN),
+    (dict(flags=1, K=64), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(flags=1, N=0, T=0), _lib.GDN_OK),
+    (dict(flags=1, N=0, T=0, ckpt=16, ckpt_cu=16, total=0, every=64), _lib.GDN_OK),
+])
+def test_prefill_ex_rejects_bad_arguments(over, code):
+    assert _prefill_ex(**over) == code
+
+
 def test_prefill_workspace_size(monkeypatch):
     ws = _lib.lib().gdn_prefill_workspace_bytes
     per_slot = lambda H, HV: HV * 17424 + H * (32768 + 16384)  # noqa: E731

@@ -71,6 +71,7 @@ def test_golden_file_present():
     assert len([c for c in CASES if c.startswith("pre_")]) >= 4
     assert len([c for c in CASES if c.startswith("mtp_")]) >= 4
     assert len([c for c in CASES if c.startswith("ckpt_")]) >= 2
+    assert len([c for c in CASES if c.startswith("pre_l2norm")]) >= 2
 
 
 @pytest.mark.parametrize("name", sorted(c for c in CASES if c.startswith("dec_")))
@@ -85,8 +86,18 @@ def test_oracle_decode_matches_reference(name):
 def test_oracle_prefill_matches_reference(name):
     c = CASES[name]
     args = [_t(c, f) for f in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens")]
-    o, s = oracle.prefill(*args, float(c["scale"]))
+    l2 = bool(int(c["qk_l2norm"])) if "qk_l2norm" in c else False
+    o, s = oracle.prefill(*args, float(c["scale"]), qk_l2norm=l2)
     _check(o, s, c)
+
+
+def test_oracle_prefill_l2norm_is_not_a_no_op():
+    """The l2norm cases feed raw q/k: without the flag the oracle misses."""
+    c = CASES["pre_l2norm"]
+    args = [_t(c, f) for f in ("q", "k", "v", "state", "A_log", "a", "dt_bias", "b", "cu_seqlens")]
+    o, s = oracle.prefill(*args, float(c["scale"]), qk_l2norm=False)
+    # (raw vectors of norm ~17 make the recurrence diverge; NaN compares unequal)
+    assert not torch.allclose(s, _t(c, "new_state"), rtol=1e-2, atol=1e-2)
 
 
 MTP_FIELDS = ("q", "k", "v", "initial_state", "initial_state_indices", "A_log", "a", "dt_bias", "b")

@@ -4,7 +4,8 @@ Cases: the benchmark configurations (one 8192-token sequence with a zero
 state; 16 sequences of seeded lengths in [1, 1024] with non-zero states), the
 contest shape, zero-length sequences, lengths around the 64-token chunk
 (1, 63, 64, 65, 127, 129), int32 / int64 cu_seqlens, H == HV, many short
-sequences, tokens outside every sequence, in-place update and non-mutation.
+sequences, tokens outside every sequence, in-place update and non-mutation,
+state checkpoints, and in-kernel q/k L2 normalisation on raw q/k.
 """
 import pytest
 import torch
@@ -177,3 +178,52 @@ def test_prefill_checkpoint_arguments(cuda_device):
         gdn_prefill.run(*args, state_checkpoints=ck, checkpoint_every_n_tokens=64)
     with pytest.raises(ValueError):
         gdn_prefill.run(*args, state_checkpoints=ck, checkpoint_cu_starts=starts)
+
+
+# ---- in-kernel q/k L2 normalisation (use_qk_l2norm_in_kernel) ----
+
+def _raw_qk(args, seed):
+    """Replace the (unit-norm) q and k by raw bf16 vectors of norm ~34."""
+    g = torch.Generator().manual_seed(seed)
+    for i in (0, 1):
+        args[i] = (torch.randn(args[i].shape, generator=g) * 3.0).to(torch.bfloat16)
+    return args
+
+
+@pytest.mark.parametrize("lens,H,HV,with_state", [
+    ([200, 0, 64, 129], 4, 8, True),     # chunk tails, an empty sequence, cross-chunk Gram tiles
+    ([1, 63, 65], 16, 32, True),          # benchmark heads, lengths around one chunk
+    ([300], 2, 2, False),                 # H == HV, zero initial state
+])
+def test_prefill_qk_l2norm_matches_oracle(cuda_device, path, lens, H, HV, with_state):
+    args = _raw_qk(inputs.prefill_inputs(lens, H, HV, seed=400 + sum(lens), with_state=with_state,
+                                         cu_dtype=torch.int64), 500 + sum(lens))
+    o, s = gdn_prefill.run(*inputs.to_device(args, cuda_device), use_qk_l2norm_in_kernel=True)
+    torch.cuda.synchronize()
+    ro, rs = oracle.prefill(*inputs.to_cpu(args), qk_l2norm=True)
+    print("parity", assert_output_close(o.cpu(), ro), assert_state_close(s.cpu(), rs))
+
+
+def test_prefill_qk_l2norm_on_unit_vectors_is_the_plain_run(cuda_device, path):
+    """Inputs that are already unit vectors: the flag changes (almost) nothing."""
+    args = inputs.to_device(inputs.prefill_inputs([190, 70], 4, 8, seed=41), cuda_device)
+    o0, s0 = gdn_prefill.run(*args)
+    o1, s1 = gdn_prefill.run(*args, use_qk_l2norm_in_kernel=True)
+    torch.cuda.synchronize()
+    assert_output_close(o1.cpu(), o0.cpu())
+    assert_state_close(s1.cpu(), s0.cpu())
+
+
+def test_prefill_qk_l2norm_with_checkpoints(cuda_device, path):
+    lens, every = [260, 64, 0, 131], 64
+    args = _raw_qk(inputs.prefill_inputs(lens, 4, 8, seed=43, with_state=True, cu_dtype=torch.int64), 44)
+    dargs = inputs.to_device(args, cuda_device)
+    starts = gdn_prefill.checkpoint_cu_starts_for(dargs[8], every)
+    ck = torch.full((int(starts[-1]), 8, 128, 128), 7.0, device=cuda_device)
+    o, s = gdn_prefill.run(*dargs, state_checkpoints=ck, checkpoint_cu_starts=starts,
+                           checkpoint_every_n_tokens=every, use_qk_l2norm_in_kernel=True)
+    torch.cuda.synchronize()
+    ro, rs, rck = oracle.prefill(*inputs.to_cpu(args), checkpoint_every_n_tokens=every, qk_l2norm=True)
+    assert_output_close(o.cpu(), ro)
+    assert_state_close(s.cpu(), rs)
+    assert_state_close(ck.cpu(), rck, what="checkpoints")
