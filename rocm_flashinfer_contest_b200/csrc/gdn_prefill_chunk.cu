@@ -875,18 +875,24 @@ done:
 //   warps 8-11      all lanes, 32 columns each: the state, held in registers
 //                   for the whole sequence, and its f16 operand copies;
 //                   thread 256 also issues the bulk copies;
-//   warp 12         one thread issues every MMA, in one order per chunk:
-//                   MMA_2(j), MMA_1a(j+1), MMA_1b(j+1), MMA_3(j).  MMAs that
-//                   feed one accumulator are never issued from two threads.
-// Producers hand operands to the issuer through mbarriers they arrive on.
+//   warp 12         one thread (issuer X) issues MMA_2(j) and MMA_3(j);
+//   warp 13         one thread (issuer Y) issues MMA_1a(j+1) and MMA_1b(j+1).
+//                   MMAs that feed one accumulator always come from the same
+//                   thread, so they reach the tensor pipe in issue order; two
+//                   issuers halve the serial issue work on the critical path
+//                   (about 60 cycles per M128 N32 MMA plus each wait and commit).
+//                   A commit covers only its own thread's MMAs, so every
+//                   reader waits on the commit of the issuer that wrote it.
+// Producers hand operands to the issuers through mbarriers they arrive on.
 // Every wait is bounded; a timeout raises a shared abort flag that every loop
 // checks, so no thread is left waiting on a barrier that will not complete.
 namespace chain2 {
 
 constexpr int VT = 32, HALF = 16;
-constexpr int NT = 416;                  // 13 warps
+constexpr int NT = 448;                  // 14 warps
 constexpr int kLoader = 256;             // bulk-copy issuer (state warps)
-constexpr int kMma = 384;                // MMA issuer
+constexpr int kMma = 384;                // MMA issuer X: MMA_2 and MMA_3 (accumulators TM_2, TM_3)
+constexpr int kMmaR = 416;               // MMA issuer Y: MMA_1a and MMA_1b (accumulator R)
 constexpr int kSW = 128;                 // state-warp threads
 constexpr int NB = 3;                    // chunk m's data in buffer m % 3
 constexpr uint32_t TM_R = 0;             // R[2]: columns 0-31 / 32-63
@@ -941,7 +947,7 @@ struct Bars {
     uint64_t m2[2];     // MMA_2(j) complete (index j % 2)
     uint64_t m3;        // MMA_3(j) complete
     uint64_t mSd;       // state warps: S_{j+1} formed, SH for MMA_1a(j + 2) written (128 arrivals)
-    uint64_t fin;       // drain of the issuer's MMAs at exit
+    uint64_t fin[2];    // drain of each issuer's MMAs at exit
 };
 
 // Chunk m's [K ; Q], [T ; P'] and gates (bulk copies by the loader) and its
@@ -1050,7 +1056,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain2_kernel(const P
         umma::mbar_init(&B.dr, 128);
         umma::mbar_init(&B.m3, 1);
         umma::mbar_init(&B.mSd, kSW);
-        umma::mbar_init(&B.fin, 1);
+        umma::mbar_init(&B.fin[0], 1);
+        umma::mbar_init(&B.fin[1], 1);
         umma::fence_mbar_init();
         abort_flag = 0;
     }
@@ -1063,8 +1070,11 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain2_kernel(const P
     long long last_ld[NB] = {-1, -1, -1}, last_g[2] = {-1, -1};  // issued loads (loader's record)
     auto fail = [&]() { failed = true; abort_flag = 1; };
 
-    if (tid == kMma) {
-        // ---- the MMA issuer: descriptors computed once, advanced by constant offsets ----
+    if (tid == kMma || tid == kMmaR) {
+        // ---- two MMA issuers, one per accumulator group: descriptors computed
+        // once, advanced by constant offsets.  tcgen05.commit covers only the
+        // issuing thread's MMAs; every reader waits on the commit of the
+        // issuer that wrote what it reads. ----
         const uint64_t dKQ0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_KQ), 128, 0);
         const uint64_t dKT0 = umma::desc_sw128(umma::smem_u32(sm + OFF_KQ), 16384u, 1024u);
         const uint64_t dTP0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_TP), 128, 0);
@@ -1072,62 +1082,64 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain2_kernel(const P
         const uint64_t dSH0 = umma::desc_mnmaj64(umma::smem_u32(sm + OFF_SH), 0);
         const uint64_t dY = umma::desc_mnmaj64(umma::smem_u32(sm + OFF_Y), 0);
         const uint64_t dDL = umma::desc_mnmaj64(umma::smem_u32(sm + OFF_DL), 0);
-        auto mma_1a = [&](long long m) {  // R_m = [K ; Q]_m SH[m % 2]
-            const uint64_t a = dadd(dKQ0, (uint32_t)(m % NB) * kTileKQ), bsh = dadd(dSH0, (uint32_t)(m % 2) * SH_BYTES);
-            const uint32_t d = tmem + TM_R + (uint32_t)(m % 2) * VT;
+        const int me = tid == kMma ? 0 : 1;
+        bool ok = true;
+        if (me == 1) {
+            auto mma_1a = [&](long long m) {  // R_m = [K ; Q]_m SH[m % 2]
+                const uint64_t a = dadd(dKQ0, (uint32_t)(m % NB) * kTileKQ), bsh = dadd(dSH0, (uint32_t)(m % 2) * SH_BYTES);
+                const uint32_t d = tmem + TM_R + (uint32_t)(m % 2) * VT;
 #pragma unroll
-            for (int k0 = 0; k0 < kDim; k0 += 16)
-                umma::mma_f16(d, dadd(a, koff_kmaj128(k0)), dadd(bsh, koff_mn64(k0)), ID_S, k0 > 0);
-        };
-
-        bool ok = wait_b(&B.init, 0) && wait_b(&B.ld[0], 0);
-        if (ok) {
-            umma::fence_after_sync();
-            mma_1a(0);
-            umma::mma_commit(&B.m1a[0]);
-            umma::mma_commit(&B.mR[0]);
-        }
-        for (long long j = 0; j < nchunks && ok && !abort_flag; ++j) {
-            const int b = (int)(j % NB);
-            // MMA_2(j) = [T ; P']_j Y_j, once Y_j is written and TM_2[j % 2] has been read (outputs of j - 2)
-            ok = wait_b(&B.yr, ph(j));
-            if (ok && j >= 2) ok = wait_b(&B.od[j % 2], ph((j - 2) / 2));
-            if (!ok) break;
-            umma::fence_after_sync();
-            {
-                const uint32_t d2 = tmem + TM_2 + (uint32_t)(j % 2) * VT;
+                for (int k0 = 0; k0 < kDim; k0 += 16)
+                    umma::mma_f16(d, dadd(a, koff_kmaj128(k0)), dadd(bsh, koff_mn64(k0)), ID_S, k0 > 0);
+            };
+            ok = wait_b(&B.init, 0) && wait_b(&B.ld[0], 0);
+            if (ok) {
+                umma::fence_after_sync();
+                mma_1a(0);
+                umma::mma_commit(&B.m1a[0]);
+                umma::mma_commit(&B.mR[0]);
+            }
+            for (long long j = 0; j + 1 < nchunks && ok && !abort_flag; ++j) {
+                // MMA_1a(j+1) = [K ; Q]_{j+1} (e^{gamma_C,j} S_j): S_j formed (SH written), chunk j+1
+                // landed, R[(j+1) % 2] read (chunk j - 1)
+                if (j >= 1) ok = wait_b(&B.mSd, ph(j - 1));
+                ok = ok && wait_b(&B.ld[(j + 1) % NB], ph((j + 1) / NB));
+                if (ok && j >= 1) ok = wait_b(&B.od[(j + 1) % 2], ph((j - 1) / 2));
+                if (!ok) break;
+                umma::fence_after_sync();
+                mma_1a(j + 1);
+                umma::mma_commit(&B.m1a[(j + 1) % 2]);
+                // Dt_j ready: MMA_1b(j+1) = G_{j+1} Dt_j onto R_{j+1}
+                ok = wait_b(&B.dr, ph(j)) && wait_b(&B.ldG[j % 2], ph(j / 2));
+                if (!ok) break;
+                umma::fence_after_sync();
+                const uint32_t d = tmem + TM_R + (uint32_t)((j + 1) % 2) * VT;
 #pragma unroll
                 for (int k0 = 0; k0 < C; k0 += 16)
-                    umma::mma_f16(d2, dadd(dTP0, b * kTileTP + koff_kmaj128(k0)), dadd(dY, koff_mn64(k0)), ID_S, k0 > 0);
-                umma::mma_commit(&B.m2[j % 2]);
+                    umma::mma_f16(d, dadd(dG0, (uint32_t)(j % 2) * kTileG + koff_kmaj128(k0)),
+                                  dadd(dDL, koff_mn64(k0)), ID_S, true);
+                umma::mma_commit(&B.mR[(j + 1) % 2]);
             }
-            // state after chunk j - 1 formed: TM_3 free, SH[(j + 1) % 2] written
-            if (j >= 1) ok = wait_b(&B.mSd, ph(j - 1));
-            // MMA_1a(j+1) = [K ; Q]_{j+1} (e^{gamma_C,j} S_j) into R[(j + 1) % 2], once R_{j-1} has been read
-            if (ok && j + 1 < nchunks) {
-                ok = wait_b(&B.ld[(j + 1) % NB], ph((j + 1) / NB));
-                if (ok && j >= 1) ok = wait_b(&B.od[(j + 1) % 2], ph((j - 1) / 2));
-                if (ok) {
-                    umma::fence_after_sync();
-                    mma_1a(j + 1);
-                    umma::mma_commit(&B.m1a[(j + 1) % 2]);
-                }
-            }
-            // Dt_j ready: MMA_1b(j+1) = G_{j+1} Dt_j onto R_{j+1}, then MMA_3(j) = K_j^T Dt_j
-            ok = ok && wait_b(&B.dr, ph(j));
-            if (ok && j + 1 < nchunks) {
-                ok = wait_b(&B.ldG[j % 2], ph(j / 2));
-                if (ok) {
-                    umma::fence_after_sync();
-                    const uint32_t d = tmem + TM_R + (uint32_t)((j + 1) % 2) * VT;
+        } else {
+            for (long long j = 0; j < nchunks && ok && !abort_flag; ++j) {
+                const int b = (int)(j % NB);
+                // MMA_2(j) = [T ; P']_j Y_j, once Y_j is written and TM_2[j % 2] has been read (outputs of j - 2)
+                ok = wait_b(&B.yr, ph(j));
+                if (ok && j >= 2) ok = wait_b(&B.od[j % 2], ph((j - 2) / 2));
+                if (!ok) break;
+                umma::fence_after_sync();
+                {
+                    const uint32_t d2 = tmem + TM_2 + (uint32_t)(j % 2) * VT;
 #pragma unroll
                     for (int k0 = 0; k0 < C; k0 += 16)
-                        umma::mma_f16(d, dadd(dG0, (uint32_t)(j % 2) * kTileG + koff_kmaj128(k0)),
-                                      dadd(dDL, koff_mn64(k0)), ID_S, true);
-                    umma::mma_commit(&B.mR[(j + 1) % 2]);
+                        umma::mma_f16(d2, dadd(dTP0, b * kTileTP + koff_kmaj128(k0)), dadd(dY, koff_mn64(k0)), ID_S,
+                                      k0 > 0);
+                    umma::mma_commit(&B.m2[j % 2]);
                 }
-            }
-            if (ok) {
+                // MMA_3(j) = K_j^T Dt_j, once Dt_j is written and TM_3 has been read (state of chunk j - 1)
+                ok = wait_b(&B.dr, ph(j));
+                if (ok && j >= 1) ok = wait_b(&B.mSd, ph(j - 1));
+                if (!ok) break;
                 umma::fence_after_sync();
 #pragma unroll
                 for (int k0 = 0; k0 < C; k0 += 16)
@@ -1138,8 +1150,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain2_kernel(const P
         }
         if (!ok) fail();
         // drain: every MMA issued here completes before the CTA exits
-        umma::mma_commit(&B.fin);
-        if (!wait_b(&B.fin, 0)) fail();
+        umma::mma_commit(&B.fin[me]);
+        if (!wait_b(&B.fin[me], 0)) fail();
     } else if (state) {
         // ---- state warps: S (fp32, registers) for TMEM lane `row`, 32 columns ----
         for (long long m = 0; m < NB && m < nchunks; ++m) {
@@ -1202,8 +1214,13 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain2_kernel(const P
                 last_ld[j % NB] = j + NB;
             }
             if (lead && j + 3 < nchunks) {
-                load_g(p, ws, sm, B, (int)((j + 2) % 2), slot0 + j + 3, hq);
-                last_g[(j + 2) % 2] = j + 3;
+                // G_{j+1} (same buffer) is read by MMA_1b(j+1), which issuer Y commits to mR
+                if (wait_b(&B.mR[(j + 1) % 2], ph((j + 1) / 2))) {
+                    load_g(p, ws, sm, B, (int)((j + 2) % 2), slot0 + j + 3, hq);
+                    last_g[(j + 2) % 2] = j + 3;
+                } else {
+                    fail();
+                }
             }
             if (j + 1 == nchunks) {  // final state, fp32 k-last
 #pragma unroll
