@@ -44,6 +44,7 @@ sys.path.insert(0, ROOT)
 D = 128
 H, HV = 16, 32
 DECODE_B = 64
+DECODE_B_STRONG = 1024  # config 4: one B = 1024 batch split across the ranks
 PREFILL_T = 8192
 FLUSH_BYTES = 256 << 20
 
@@ -269,6 +270,24 @@ def bench_ours(args, rank, world, local):
         torch.cuda.synchronize()
         barrier(world)
 
+        # ---- decode: this rank's shard of one B = 1024 batch (strong scaling) ----
+        s1k = partition.plan_decode(DECODE_B_STRONG, H, HV, world)[rank]
+        b1k = len(s1k.seqs)
+        kargs = inputs.decode_inputs(b1k, H, HV, seed=5000 + rank, device=dev)
+        kout = torch.empty((b1k, 1, HV, D), dtype=torch.bfloat16, device=dev)
+
+        def b1k_step():
+            gdn_decode.run_into(*kargs[:3], kargs[3], *kargs[4:], output=kout, new_state=kargs[3])
+
+        for _ in range(3):
+            b1k_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        b1k_ms = timed_steps(b1k_step, args.steps, flush, stream)
+        del kargs, kout
+        torch.cuda.synchronize()
+        barrier(world)
+
         # ---- prefill: one 8192-token sequence per rank, zero initial state ----
         pargs = inputs.prefill_inputs([PREFILL_T], H, HV, seed=2000 + rank, device=dev,
                                       with_state=False)
@@ -321,6 +340,7 @@ def bench_ours(args, rank, world, local):
     bf16_step_ms = max_over_ranks(statistics.mean(bf16_ms), world, dev)
 
     dec_step_ms = max_over_ranks(statistics.mean(dec_ms), world, dev)
+    b1k_step_ms = max_over_ranks(statistics.mean(b1k_ms), world, dev)
     pre_step_ms = max_over_ranks(statistics.mean(pre_ms), world, dev)
 
     # ---- e2e through the public run() with host buffers ----
@@ -414,12 +434,20 @@ def bench_ours(args, rank, world, local):
                         "copy directions overlapped"},
         # one kernel per decode / prefill call, one per batch slice of the
         # host-buffer decode; counted over every timed region
-        "gpu_launches": 5 * args.steps + e2e_steps * host_slices + pe2e_steps,
-        "gpu_launches_by_region": {"decode": args.steps, "decode_clean_l2": args.steps, "prefill": args.steps,
+        "gpu_launches": 6 * args.steps + e2e_steps * host_slices + pe2e_steps,
+        "gpu_launches_by_region": {"decode": args.steps, "decode_clean_l2": args.steps,
+                                   "decode_b1024": args.steps, "prefill": args.steps,
                                    "mtp": args.steps,
                                    "decode_bf16_state": args.steps,
                                    "decode_e2e": e2e_steps * host_slices, "prefill_e2e": pe2e_steps},
         "clocks": clocks,
+        "decode_b1024": {
+            "metric": f"gdn_decode state GB/s, one B={DECODE_B_STRONG} batch split across the ranks",
+            "value": round(decode_state_bytes(DECODE_B_STRONG) / (b1k_step_ms * 1e-3) / 1e9, 1), "unit": UNIT,
+            "us_per_step": round(b1k_step_ms * 1e3, 2), "step_ms_stats": _stats(b1k_ms),
+            "B_per_gpu": len(partition.plan_decode(DECODE_B_STRONG, H, HV, world)[0].seqs),
+            "scaling": "strong",
+        },
         "prefill": {
             "metric": "gdn_prefill tokens/s at T=8192 (1 sequence, zero state)",
             "value": round(PREFILL_T * world / (pre_step_ms * 1e-3), 1), "unit": "tokens/s",

@@ -360,14 +360,18 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
     // MMA_A: [K ; Q] K^T (bf16, or f16 once normalised); MMA_G: [K ; Q] K_{j-1}^T
     if (tid == 0) {
         const uint32_t ID = p.qk_l2norm ? umma::idesc_f16(128, 64, 0, 0, 0, 0) : umma::idesc_f16(128, 64, 1, 1, 0, 0);
+        const uint64_t dKQ = umma::desc_kmaj(sKQ, 128, 0);
 #pragma unroll
-        for (int k0 = 0; k0 < kDim; k0 += 16)
-            umma::mma_f16(tmem, umma::desc_kmaj(sKQ, 128, k0), umma::desc_kmaj(sKQ, 128, k0), ID, k0 > 0);
+        for (int k0 = 0; k0 < kDim; k0 += 16) {
+            const uint64_t a = umma::desc_add(dKQ, umma::koff_kmaj(128, k0));
+            umma::mma_f16(tmem, a, a, ID, k0 > 0);
+        }
         if (gram) {
-            const uint32_t sKP = umma::smem_u32(sm + OFF_KP);
+            const uint64_t dKP = umma::desc_kmaj(umma::smem_u32(sm + OFF_KP), 64, 0);
 #pragma unroll
             for (int k0 = 0; k0 < kDim; k0 += 16)
-                umma::mma_f16(tmem + 64, umma::desc_kmaj(sKQ, 128, k0), umma::desc_kmaj(sKP, 64, k0), ID, k0 > 0);
+                umma::mma_f16(tmem + 64, umma::desc_add(dKQ, umma::koff_kmaj(128, k0)),
+                              umma::desc_add(dKP, umma::koff_kmaj(64, k0)), ID, k0 > 0);
         }
         umma::mma_commit(&mbar[0]);
     }
@@ -487,10 +491,12 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
     // MMA_P: [T ; P] T -> rows 64-127 = P' = P T
     if (tid == 0) {
         constexpr uint32_t ID = umma::idesc_f16(128, 64, 0, 0, 0, 1);
-        const uint32_t sTP = umma::smem_u32(sm + OFF_TP), sTB = umma::smem_u32(sm + OFF_TB);
+        const uint64_t dTP = umma::desc_kmaj(umma::smem_u32(sm + OFF_TP), 128, 0);
+        const uint64_t dTB = umma::desc_mnmaj(umma::smem_u32(sm + OFF_TB), C, 0);
 #pragma unroll
         for (int k0 = 0; k0 < C; k0 += 16)
-            umma::mma_f16(tmem, umma::desc_kmaj(sTP, 128, k0), umma::desc_mnmaj(sTB, C, k0), ID, k0 > 0);
+            umma::mma_f16(tmem, umma::desc_add(dTP, umma::koff_kmaj(128, k0)), umma::desc_add(dTB, umma::koff_mnmaj(k0)),
+                          ID, k0 > 0);
         umma::mma_commit(&mbar[1]);
     }
     if (!wait_mma(&mbar[1], 0)) goto done;
@@ -572,6 +578,10 @@ struct Cfg {
     static __device__ __forceinline__ uint64_t b_desc(uint32_t tile, uint32_t kext, uint32_t k0) {
         if constexpr (VT == 32) return umma::desc_mnmaj64(tile, k0);
         else return umma::desc_mnmaj(tile, kext, k0);
+    }
+    // byte offset of the K step at k0 from the descriptor b_desc(tile, kext, 0)
+    static __host__ __device__ constexpr uint32_t b_koff(uint32_t k0) {
+        return VT == 32 ? umma::koff_mnmaj64(k0) : umma::koff_mnmaj(k0);
     }
     static __device__ __forceinline__ void ld(uint32_t taddr, float (&v)[HALF]) {
         if constexpr (HALF == 16) umma::tmem_ld16(taddr, v);
@@ -705,6 +715,10 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
     constexpr uint32_t ID_S = umma::idesc_f16(128, VT, 0, 0, 0, 1);  // [K;Q] x S (MN-major B)
     constexpr uint32_t ID_Y = umma::idesc_f16(128, VT, 0, 0, 0, 1);  // [T;P'] x Y (MN-major B)
     constexpr uint32_t ID_D = umma::idesc_f16(128, VT, 0, 0, 1, 1);  // K^T x Delta~ (both MN-major)
+    // operand descriptors, built once; every K step and buffer is a constant offset
+    const uint64_t dKQ0 = umma::desc_kmaj(sKQ0, 128, 0), dKT0 = umma::desc_sw128(sKQ0, 16384u, 1024u);
+    const uint64_t dTP0 = umma::desc_kmaj(sTP0, 128, 0);
+    const uint64_t dSH = G::b_desc(sSH, kDim, 0), dY = G::b_desc(sY, C, 0), dDL = G::b_desc(sDL, C, 0);
 
     for (long long j = 0; j < nchunks; ++j) {
         const int b = (int)(j % NBUF);
@@ -713,15 +727,14 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
         const int len = chunk_len(j);
         wait_local(&ldbar[b], lpar, failed);
         const float* gr = reinterpret_cast<const float*>(sm + OFF_GB + b * kGateBytes);
-        const uint32_t sKQ = sKQ0 + b * kTileKQ;
 
         // ---- MMA_1: [K ; Q] S ----
         if (tid == 0) {
             umma::fence_after_sync();
 #pragma unroll
             for (int k0 = 0; k0 < kDim; k0 += 16)
-                umma::mma_f16(tmem + TM_1, umma::desc_kmaj(sKQ, 128, k0), G::b_desc(sSH, kDim, k0), ID_S,
-                              k0 > 0);
+                umma::mma_f16(tmem + TM_1, umma::desc_add(dKQ0, b * kTileKQ + umma::koff_kmaj(128, k0)),
+                              umma::desc_add(dSH, G::b_koff(k0)), ID_S, k0 > 0);
             umma::mma_commit(&mbar[0]);
         }
         // while MMA_1 runs: stream in chunk j + 2 (its buffer was chunk j - 1's)
@@ -754,11 +767,10 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
                 lower_sync();
                 if (tid == 0) {
                     umma::fence_after_sync();
-                    const uint32_t sTP = sTP0 + b * kTileTP;
 #pragma unroll
                     for (int k0 = 0; k0 < C; k0 += 16)
-                        umma::mma_f16(tmem + TM_2, umma::desc_kmaj(sTP, 128, k0), G::b_desc(sY, C, k0), ID_Y,
-                                      k0 > 0);
+                        umma::mma_f16(tmem + TM_2, umma::desc_add(dTP0, b * kTileTP + umma::koff_kmaj(128, k0)),
+                                      umma::desc_add(dY, G::b_koff(k0)), ID_Y, k0 > 0);
                     umma::mma_commit(&mbar[1]);
                 }
             } else {
@@ -788,8 +800,8 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const Pr
                     umma::fence_after_sync();
 #pragma unroll
                     for (int k0 = 0; k0 < C; k0 += 16)
-                        umma::mma_f16(tmem + TM_3, umma::desc_sw128(sKQ + (k0 >> 3) * 1024u, 16384u, 1024u),
-                                      G::b_desc(sDL, C, k0), ID_D, k0 > 0);
+                        umma::mma_f16(tmem + TM_3, umma::desc_add(dKT0, b * kTileKQ + umma::koff_mnmaj(k0)),
+                                      umma::desc_add(dDL, G::b_koff(k0)), ID_D, k0 > 0);
                     umma::mma_commit(&mbar[2]);
                 }
             } else {

@@ -96,6 +96,23 @@ __device__ __forceinline__ uint64_t desc_mnmaj(uint32_t tile_saddr, uint32_t kex
     return desc_sw128(tile_saddr + (k0 >> 3) * 1024u, kext * 128u, 1024u);
 }
 
+// A descriptor advanced by `bytes` (a multiple of 16): the start-address
+// field is bits 0-13 in 16-byte units and no shared-memory address carries
+// out of it, so the advance is one 64-bit add.  Kernels build each operand's
+// descriptor once and step through K (and ring buffers) by constant offsets:
+// rebuilt per instruction from a run-time address, a descriptor costs more
+// issue time than the MMA it feeds (measured: ~200-300 against ~42 cycles
+// per M128 N32 K16 MMA).
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
+// Byte offset of the K step at element k0 for desc_kmaj (a tile of `rows` rows) ...
+__host__ __device__ constexpr uint32_t koff_kmaj(uint32_t rows, uint32_t k0) {
+    return (k0 >> 6) * rows * 128u + (k0 & 63u) * 2u;
+}
+// ... for desc_mnmaj (and K^T read MN-major from a K-major tile) ...
+__host__ __device__ constexpr uint32_t koff_mnmaj(uint32_t k0) { return (k0 >> 3) * 1024u; }
+// ... and for desc_mnmaj64.
+__host__ __device__ constexpr uint32_t koff_mnmaj64(uint32_t k0) { return (k0 >> 3) * 512u; }
+
 // Instruction descriptor, kind::f16 with fp32 accumulation.
 // fmt: 0 = f16, 1 = bf16.  major: 0 = K-major, 1 = MN-major.
 __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int a_fmt, int b_fmt, int a_major, int b_major) {
