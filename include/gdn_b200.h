@@ -42,12 +42,16 @@ extern "C" {
 #define GDN_ERR_DEVICE 5      /* a kernel reported an error (bounded wait timed out) */
 #define GDN_ERR_TOO_LARGE 6   /* needs more than gdn_prefill_fwd_noalloc's fixed scratch */
 
+/* flags of gdn_mtp_fwd */
+#define GDN_MTP_QK_L2NORM 1          /* normalise q and k in the kernel */
+#define GDN_MTP_SNAPSHOTS_BY_ENTRY 2 /* intermediate states indexed by batch entry, not pool slot */
+
 /* flags of gdn_prefill_fwd_ex */
 #define GDN_PREFILL_QK_L2NORM 1 /* normalise q and k in the kernel: x * rsqrt(sum(x^2) + 1e-6) */
 
 /* Version of this ABI (bumped on any signature change or addition; 3 adds
- * gdn_mtp_fwd and gdn_prefill_fwd_checkpointed, 4 gdn_decode_fwd_host and
- * gdn_prefill_fwd_ex). */
+ * gdn_mtp_fwd and gdn_prefill_fwd_checkpointed, 4 gdn_decode_fwd_host,
+ * gdn_prefill_fwd_ex and gdn_mtp_fwd's flags word). */
 int gdn_abi_version(void);
 
 /* Human-readable text for a status code. */
@@ -246,19 +250,31 @@ int gdn_prefill_fwd_noalloc(const void *q, const void *k, const void *v, const f
  * An index outside [0, pool_size) in `indices` marks padding (flashinfer's
  * -1): its output rows are written as zeros and no state is read or written.
  * No slot may be written by one entry and read or written by another.  When
- * `intermediate` is not NULL (fp32 pools only) the state after token t of the
- * entry read from slot s is written to intermediate[s, t] for s < inter_slots
- * (cache_steps >= T).  qk_l2norm == 1 normalises every q and k head vector in
- * the kernel as x * rsqrt(sum(x^2) + 1e-6) (`use_qk_l2norm`); 0 takes them as
- * given (the contest definition).  Alignment as decode: q, k 8 bytes; pools
- * and intermediate 16 bytes; indices their own size.  B == 0 or T == 0
- * launches no kernel (only the pool copy).
+ * `intermediate` ([inter_slots, cache_steps, HV, V, K] fp32, cache_steps >=
+ * T; fp32 pools only) is not NULL, the state after token t of batch entry i
+ * (read from slot s) is written
+ *   - without GDN_MTP_SNAPSHOTS_BY_ENTRY: to intermediate[s, t], for
+ *     s < inter_slots (the contest definition, gdn.py:457-460);
+ *   - with it: to state row i * T + t of the buffer seen as
+ *     [inter_slots * cache_steps] rows, if entry i's T rows fit (the rows
+ *     flashinfer's gated_delta_rule_mtp kernel writes,
+ *     gdn_kernels/gdn_decode_mtp.py:645; = intermediate[i, t] when
+ *     cache_steps == T).
+ * Padding entries write no snapshot.  `flags`:
+ *   GDN_MTP_QK_L2NORM           normalise every q and k head vector in the
+ *                               kernel as x * rsqrt(sum(x^2) + 1e-6)
+ *                               (`use_qk_l2norm`); without it they are taken
+ *                               as given (the contest definition);
+ *   GDN_MTP_SNAPSHOTS_BY_ENTRY  snapshot rows by batch entry, as above.
+ * Unknown flag bits return GDN_ERR_INVALID.  Alignment as decode: q, k 8
+ * bytes; pools and intermediate 16 bytes; indices their own size.  B == 0 or
+ * T == 0 launches no kernel (only the pool copy).
  */
 int gdn_mtp_fwd(const void *q, const void *k, const void *v, const void *pool_in,
                 void *pool_out, int state_bf16, const void *indices, const void *out_indices,
                 int indices_int64, const float *A_log, const void *a, const float *dt_bias,
                 const void *b, float scale, int B, int T, int H, int HV, int K, int V,
-                int pool_size, int qk_l2norm, void *out, float *intermediate, int inter_slots,
+                int pool_size, int flags, void *out, float *intermediate, int inter_slots,
                 int cache_steps, void *stream);
 
 #ifdef __cplusplus

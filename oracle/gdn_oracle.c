@@ -223,9 +223,10 @@ int gdn_oracle_mtp(const float *q, const float *k, const float *v, const float *
                    float *pool_out, const int64_t *idx, const int64_t *out_idx, const float *A_log,
                    const float *a, const float *dt_bias, const float *b, float scale, int B, int T,
                    int H, int HV, int K, int V, int pool_size, int round_bf16_state, int qk_l2norm,
-                   uint16_t *out_bf16, float *inter, int cache_steps, int nthreads) {
+                   uint16_t *out_bf16, float *inter, int cache_steps, long long inter_rows,
+                   int snap_by_entry, int nthreads) {
     if (B < 0 || T < 0 || H <= 0 || HV <= 0 || K <= 0 || V <= 0 || HV % H || pool_size < 0) return 1;
-    if (inter && cache_steps < T) return 1;
+    if (inter && (cache_steps < T || inter_rows < 0)) return 1;
     if (scale == 0.0f) scale = 1.0f / sqrtf((float)K);
     const int rep = HV / H;
     const size_t head = (size_t)V * K;
@@ -237,6 +238,15 @@ int gdn_oracle_mtp(const float *q, const float *k, const float *v, const float *
         int bi = (int)(bh / HV), h = (int)(bh % HV), hq = h / rep;
         int64_t slot = idx[bi];
         if (slot < 0 || slot >= pool_size) continue;
+        /* first snapshot row of this entry, or -1: an entry's T rows are
+         * written whole or not at all (by pool slot: inter[slot, t]; by entry:
+         * row bi * T + t, flashinfer's CuTe kernel, gdn_decode_mtp.py:645) */
+        long long row0 = -1;
+        if (inter) {
+            long long r = snap_by_entry ? (long long)bi * T : (long long)slot * cache_steps;
+            long long need = snap_by_entry ? (long long)T : (long long)cache_steps;
+            if (r + need <= inter_rows) row0 = r;
+        }
         float *S = (float *)malloc(sizeof(float) * head);
         memcpy(S, pool_in + ((size_t)slot * HV + h) * head, sizeof(float) * head);
         float *o = (float *)malloc(sizeof(float) * (V + 2 * K));
@@ -249,8 +259,8 @@ int gdn_oracle_mtp(const float *q, const float *k, const float *v, const float *
             l2norm_copy(kn, k + (bt * H + hq) * K, K, qk_l2norm);
             step_head(S, qn, kn, v + (bt * HV + h) * V, g, beta, scale, K, V, o);
             for (int vi = 0; vi < V; ++vi) out_bf16[(bt * HV + h) * V + vi] = f32_to_bf16_rne(o[vi]);
-            if (inter)
-                memcpy(inter + (((size_t)slot * cache_steps + t) * HV + h) * head, S, sizeof(float) * head);
+            if (row0 >= 0)
+                memcpy(inter + (((size_t)row0 + t) * HV + h) * head, S, sizeof(float) * head);
         }
         int64_t oslot = out_idx ? out_idx[bi] : slot;
         if (oslot >= 0 && oslot < pool_size) {

@@ -66,7 +66,8 @@ def _load():
     lib.gdn_oracle_mtp.argtypes = [
         _f32p, _f32p, _f32p, _f32p, _f32p, _i64p, _i64p, _f32p, _f32p, _f32p, _f32p, ctypes.c_float,
         ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-        ctypes.c_int, ctypes.c_int, ctypes.c_int, _u16p, _f32p, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, ctypes.c_int, _u16p, _f32p, ctypes.c_int, ctypes.c_longlong,
+        ctypes.c_int, ctypes.c_int,
     ]
     _lib = lib
     return lib
@@ -153,11 +154,14 @@ def prefill(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, threads: in
 
 def mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale,
         intermediate_states_buffer=None, qk_l2norm: bool = False, output_state_indices=None,
-        threads: int = 0):
+        threads: int = 0, snapshots_by_entry: bool = False):
     """Returns (output [B,T,HV,V] bf16, final_state [pool,HV,V,K]) and fills
-    intermediate_states_buffer ([pool,cache_steps>=T,HV,V,K] fp32) in place
-    when given.  A bf16 initial_state selects the bf16-state form and gives a
-    bf16 final_state."""
+    intermediate_states_buffer ([slots,cache_steps>=T,HV,V,K] fp32) in place
+    when given: the state after token t of the entry reading slot s goes to
+    buffer[s, t], or with snapshots_by_entry to row i * T + t of the buffer
+    seen as [slots * cache_steps] rows for batch entry i; an entry whose rows
+    do not fit is skipped.  A bf16 initial_state selects the bf16-state form
+    and gives a bf16 final_state."""
     lib = _load()
     B, T, H, K = q.shape
     HV, V = v.shape[2], v.shape[3]
@@ -172,15 +176,17 @@ def mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, sca
     Af, af, dtf, bf = _f32(A_log), _f32(a), _f32(dt_bias), _f32(b)
     out = torch.empty((B, T, HV, V), dtype=torch.int16)
     pout = torch.empty_like(pin)
-    inter, steps = None, T
+    inter, steps, rows = None, T, 0
     if intermediate_states_buffer is not None:
         inter = _f32(intermediate_states_buffer).clone()
         steps = inter.shape[1]
+        rows = inter.shape[0] * steps
     rc = lib.gdn_oracle_mtp(
         _ptr(qf, _f32p), _ptr(kf, _f32p), _ptr(vf, _f32p), _ptr(pin, _f32p), _ptr(pout, _f32p),
         _ptr(idx, _i64p), _ptr(oidx, _i64p), _ptr(Af, _f32p), _ptr(af, _f32p), _ptr(dtf, _f32p),
         _ptr(bf, _f32p), _scale(scale, K), B, T, H, HV, K, V, pool, int(bf16_state),
-        int(bool(qk_l2norm)), _ptr(out, _u16p), _ptr(inter, _f32p), steps, int(threads))
+        int(bool(qk_l2norm)), _ptr(out, _u16p), _ptr(inter, _f32p), steps, rows,
+        int(bool(snapshots_by_entry)), int(threads))
     if rc != 0:
         raise ValueError(f"gdn_oracle_mtp rejected its arguments (rc={rc})")
     if inter is not None:

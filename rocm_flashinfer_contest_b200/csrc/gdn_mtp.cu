@@ -8,7 +8,10 @@
 //   * an index outside [0, pool_size) is padding (the -1 convention of
 //     gdn_decode.py:182-193): zero output, no state read or written;
 //   * optional per-token state snapshots into inter[slot, t] (gdn.py:457-460),
-//     `cache_steps` >= T token slots per pool slot (gdn_decode.py:686-692);
+//     `cache_steps` >= T token slots per pool slot (gdn_decode.py:686-692),
+//     or, with snap_entry, into row i * T + t of the buffer for batch entry i
+//     (the row flashinfer's CuTe MTP kernel writes, gdn_kernels/
+//     gdn_decode_mtp.py:645: batch-scoped, packed with stride T);
 //   * optional in-kernel q/k L2 normalisation, x * rsqrt(sum(x^2) + 1e-6)
 //     (`use_qk_l2norm`, gdn_decode.py:571);
 //   * the pool in fp32 or in bf16 (the bf16-state decode of
@@ -46,6 +49,7 @@ struct MtpParams {
     float* inter;            // nullable: [inter_slots, cache_steps, HV, 128, 128]
     float scale;
     int T, H, HV, rep, pool_size, inter_slots, cache_steps, idx64, l2norm;
+    int snap_entry;          // snapshots indexed by batch entry (row bi * T + t), not by pool slot
 };
 
 __device__ __forceinline__ float mtp_dot4(float4 x, float4 y) {
@@ -56,6 +60,18 @@ __device__ __forceinline__ float mtp_dot4(float4 x, float4 y) {
 // group j at columns 4*sub + 32*j (one 16-byte access per group).  bf16 state:
 // groups 2p, 2p+1 at columns 8*sub + 64*p (+4), so one 16-byte access moves
 // two groups and a row needs two accesses per lane.
+// First snapshot row (in units of one head's V x K state times HV) of batch
+// entry bi reading pool slot `slot`, or -1 when its snapshots do not fit in
+// the buffer (an entry is written whole or not at all).
+__device__ __forceinline__ long long mtp_snap_row(const MtpParams& p, int bi, long long slot) {
+    if (p.inter == nullptr) return -1;
+    if (p.snap_entry) {
+        const long long r = (long long)bi * p.T;
+        return r + p.T <= (long long)p.inter_slots * p.cache_steps ? r : -1;
+    }
+    return slot < p.inter_slots ? slot * p.cache_steps : -1;
+}
+
 template <typename StateT>
 __device__ __forceinline__ int mtp_col(int sub, int j) {
     return sizeof(StateT) == 4 ? 4 * sub + 32 * j : 8 * sub + 64 * (j >> 1) + 4 * (j & 1);
@@ -174,7 +190,8 @@ __global__ void __launch_bounds__(128) gdn_mtp_kernel(const MtpParams p) {
 #pragma unroll
     for (int ps = 0; ps < kPasses; ++ps) mtp_load_row(pin, sbase + (size_t)ps * 4 * kDim, sub, s[ps]);
 
-    const bool snap = p.inter != nullptr && slot < p.inter_slots;
+    const long long snap_row = mtp_snap_row(p, bi, slot);
+    const bool snap = snap_row >= 0;
     const bool upper = (sub & 4) != 0;
     MtpToken<kPasses> cur, nxt;
     mtp_load_token<StateT>(cur, p, (size_t)bi * T, hq, hv, sub, row_base);
@@ -211,8 +228,7 @@ __global__ void __launch_bounds__(128) gdn_mtp_kernel(const MtpParams p) {
         kq = row8_sum(kq);
 
         const size_t ob = (bt * p.HV + hv) * kDim + row_base;
-        float* snap_dst = snap ? p.inter + (((size_t)slot * p.cache_steps + t) * p.HV + hv) * kDim * kDim + row_off
-                               : nullptr;
+        float* snap_dst = snap ? p.inter + (((size_t)snap_row + t) * p.HV + hv) * kDim * kDim + row_off : nullptr;
 #pragma unroll
         for (int ps = 0; ps < kPasses; ++ps) {
             float2 sk2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);
@@ -354,9 +370,8 @@ __global__ void __launch_bounds__(128) gdn_pool_decode_kernel(const MtpParams p)
     StateT* pout = (p.pool_out != nullptr && oslot >= 0 && oslot < p.pool_size) ? static_cast<StateT*>(p.pool_out)
                                                                                 : nullptr;
     const size_t obase = ((size_t)oslot * p.HV + hv) * kDim * kDim + row_off;
-    float* snap_dst = (p.inter != nullptr && slot < p.inter_slots)
-                          ? p.inter + ((size_t)slot * p.cache_steps * p.HV + hv) * kDim * kDim + row_off
-                          : nullptr;
+    const long long snap_row = mtp_snap_row(p, bi, slot);
+    float* snap_dst = snap_row >= 0 ? p.inter + ((size_t)snap_row * p.HV + hv) * kDim * kDim + row_off : nullptr;
     const bool upper = (sub & 4) != 0;
 #pragma unroll
     for (int ps = 0; ps < kPasses; ++ps) {
@@ -392,10 +407,10 @@ extern "C" int gdn_mtp_fwd(const void* q, const void* k, const void* v, const vo
                            void* pool_out, int state_bf16, const void* indices, const void* out_indices,
                            int indices_int64, const float* A_log, const void* a, const float* dt_bias,
                            const void* b, float scale, int B, int T, int H, int HV, int K, int V,
-                           int pool_size, int qk_l2norm, void* out, float* intermediate, int inter_slots,
+                           int pool_size, int flags, void* out, float* intermediate, int inter_slots,
                            int cache_steps, void* stream) {
     if (B < 0 || T < 0 || H <= 0 || HV <= 0 || pool_size < 0) return GDN_ERR_INVALID;
-    if ((indices_int64 != 0 && indices_int64 != 1) || (qk_l2norm != 0 && qk_l2norm != 1) ||
+    if ((indices_int64 != 0 && indices_int64 != 1) || (flags & ~(GDN_MTP_QK_L2NORM | GDN_MTP_SNAPSHOTS_BY_ENTRY)) ||
         (state_bf16 != 0 && state_bf16 != 1))
         return GDN_ERR_INVALID;
     if (K != gdn::kDim || V != gdn::kDim || HV % H != 0) return GDN_ERR_UNSUPPORTED;
@@ -454,7 +469,8 @@ extern "C" int gdn_mtp_fwd(const void* q, const void* k, const void* v, const vo
     p.pool_size = pool_size;
     p.inter_slots = intermediate ? inter_slots : 0;
     p.cache_steps = cache_steps;
-    p.l2norm = qk_l2norm;
+    p.l2norm = (flags & GDN_MTP_QK_L2NORM) != 0;
+    p.snap_entry = (flags & GDN_MTP_SNAPSHOTS_BY_ENTRY) != 0;
     const long long heads = (long long)B * HV;
     const bool small = heads * (gdn::kDim / 32) < 4 * 148;
     if (T == 1) {

@@ -15,7 +15,12 @@ disable_state_update=None, use_qk_l2norm=True) -> (output, initial_state)``
     flashinfer's serving API (flashinfer/gdn_decode.py:557-745): the pool is
     updated in place unless ``disable_state_update``; q and k are
     L2-normalised in the kernel when ``use_qk_l2norm``.  As there,
-    ``disable_state_update=None`` means True with a one-time warning.
+    ``disable_state_update=None`` means True with a one-time warning, and the
+    snapshots go where flashinfer's kernel puts them: batch entry i's state
+    after token t to row i * T + t of the buffer seen as
+    [slots * cache_steps] rows (gdn_kernels/gdn_decode_mtp.py:645; that is
+    buffer[i, t] when cache_steps == T), where ``run`` follows the contest
+    definition's buffer[slot, t].
 
 Shapes: q, k [B, T, H, 128] bf16; v [B, T, HV, 128] bf16; a, b [B, T, HV]
 bf16; A_log, dt_bias [HV] fp32; initial_state [pool, HV, 128, 128] fp32 or
@@ -94,15 +99,20 @@ def _out_indices(out_idx, idx, B, dev):
     return out_idx.to(idx.dtype).contiguous()
 
 
+GDN_MTP_QK_L2NORM = 1           # gdn_mtp_fwd flags (include/gdn_b200.h)
+GDN_MTP_SNAPSHOTS_BY_ENTRY = 2
+
+
 def _launch(dev, tensors, dims, pool_in, pool_out, scale, output, buf, slots, steps, l2norm,
-            out_idx=None):
+            out_idx=None, snapshots_by_entry=False):
     q, k, v, idx, A_log, a, dt_bias, b = tensors
     B, T, H, HV, K, V = dims
+    flags = (GDN_MTP_QK_L2NORM if l2norm else 0) | (GDN_MTP_SNAPSHOTS_BY_ENTRY if snapshots_by_entry else 0)
     st = lib().gdn_mtp_fwd(
         C.ptr(q), C.ptr(k), C.ptr(v), C.ptr(pool_in), C.ptr(pool_out),
         int(pool_in.dtype == torch.bfloat16), C.ptr(idx), C.ptr(out_idx),
         int(idx.dtype == torch.int64), C.ptr(A_log), C.ptr(a), C.ptr(dt_bias), C.ptr(b),
-        C.normalize_scale(scale, K), B, T, H, HV, K, V, pool_in.shape[0], int(bool(l2norm)),
+        C.normalize_scale(scale, K), B, T, H, HV, K, V, pool_in.shape[0], flags,
         C.ptr(output), C.ptr(buf), slots, steps, C.stream_handle(dev))
     check("gdn_mtp_fwd", st)
 
@@ -169,7 +179,7 @@ def gated_delta_rule_mtp(q, k, v, initial_state, initial_state_indices, A_log, a
     _check_output(output, B, T, HV, V, dev)
     pool = initial_state if initial_state.is_contiguous() else initial_state.contiguous()
     _launch(dev, tensors, dims, pool, None if disable_state_update else pool, scale, output,
-            intermediate_states_buffer, slots, steps, use_qk_l2norm)
+            intermediate_states_buffer, slots, steps, use_qk_l2norm, snapshots_by_entry=True)
     if not disable_state_update and pool is not initial_state:
         initial_state.copy_(pool)
     if target is not None:

@@ -139,7 +139,7 @@ def test_prefill_rejects_bad_arguments(over, code):
 def _mtp(**over):
     d = dict(q=16, k=16, v=16, pool_in=4096, pool_out=4096, bf16=0, idx=16, out_idx=None, idx64=0,
              A_log=16, a=16, dt_bias=16, b=16, scale=0.0, B=2, T=3, H=1, HV=2, K=128, V=128, pool=4,
-             l2=0, out=16, inter=None, inter_slots=0, steps=0, stream=None)
+             l2=0, out=16, inter=None, inter_slots=0, steps=0, stream=None)  # l2 = the flags word
     d.update(over)
     return _lib.lib().gdn_mtp_fwd(*d.values())
 
@@ -151,7 +151,9 @@ def _mtp(**over):
     (dict(T=-1), _lib.GDN_ERR_INVALID),
     (dict(pool=-1), _lib.GDN_ERR_INVALID),
     (dict(idx64=2), _lib.GDN_ERR_INVALID),
-    (dict(l2=3), _lib.GDN_ERR_INVALID),
+    (dict(l2=4), _lib.GDN_ERR_INVALID),                                 # unknown flag bit
+    (dict(l2=-1), _lib.GDN_ERR_INVALID),
+    (dict(l2=3, B=0), _lib.GDN_OK),                                     # l2norm | snapshots by entry
     (dict(idx=None), _lib.GDN_ERR_INVALID),
     (dict(out=None), _lib.GDN_ERR_INVALID),
     (dict(inter=4096, inter_slots=4, steps=2), _lib.GDN_ERR_INVALID),   # cache_steps < T

@@ -272,3 +272,31 @@ def test_decode_pretranspose_pool_mode(cuda_device):
     assert_output_close(out.cpu(), ro)
     assert not out[1].float().any()
     _bf16_tol(pool_dev, rs)
+
+
+@pytest.mark.parametrize("T,steps,rows_entries", [(4, 4, 6), (3, 5, 4), (2, 2, 3), (1, 1, 6)])
+def test_mtp_serving_api_snapshots_by_entry(cuda_device, T, steps, rows_entries):
+    """gated_delta_rule_mtp puts snapshots where flashinfer's kernel does: batch
+    entry i, token t at row i * T + t of the buffer seen as [slots * steps]
+    rows (buffer[i, t] when steps == T); padding entries and entries whose T
+    rows do not fit write nothing."""
+    B, pool, H, HV = 6, 10, 4, 8
+    idx = [7, -1, 2, 9, 0, 4]
+    args = inputs.mtp_inputs(B, T, pool, H, HV, seed=60 + T, indices=idx)
+    slots = max(1, rows_entries * T // steps)
+    buf = torch.full((slots, steps, HV, 128, 128), -3.0)
+    _, _ = oracle.mtp(*args[:10], intermediate_states_buffer=buf, snapshots_by_entry=True)
+    ro, rs = oracle.mtp(*args[:10])
+    dargs = inputs.to_device(args, cuda_device)
+    dbuf = torch.full((slots, steps, HV, 128, 128), -3.0, device=cuda_device)
+    pool_dev = dargs[3].clone()
+    o, _ = gdn_mtp.gated_delta_rule_mtp(*dargs[:3], pool_dev, *dargs[4:10], intermediate_states_buffer=dbuf,
+                                        disable_state_update=False, use_qk_l2norm=False)
+    torch.cuda.synchronize()
+    assert_output_close(o.cpu(), ro)
+    assert_state_close(pool_dev.cpu(), rs)
+    got, want = dbuf.cpu().view(-1, HV, 128, 128), buf.view(-1, HV, 128, 128)
+    untouched = want == -3.0
+    assert torch.equal(untouched, got == -3.0)   # the same rows written
+    assert_state_close(got[~untouched.all(-1).all(-1).all(-1)], want[~untouched.all(-1).all(-1).all(-1)],
+                       what="snapshots")

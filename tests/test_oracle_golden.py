@@ -185,3 +185,43 @@ def test_oracle_plants_are_caught():
     o, s = oracle.decode(*bad, float(c["scale"]))
     with pytest.raises(AssertionError):
         _check(o, s, c)
+
+
+def test_oracle_mtp_snapshots_by_entry_are_a_reindexing():
+    """Snapshots by batch entry (flashinfer's kernel, row i * T + t) hold the
+    same states as the golden-pinned by-slot snapshots (the contest
+    definition), moved from slot idx[i] to entry i; padding entries and
+    entries whose rows do not fit write nothing."""
+    B, T, pool, H, HV, K = 4, 3, 6, 1, 2, 16
+    g = torch.Generator().manual_seed(7)
+    q = torch.nn.functional.normalize(torch.randn(B, T, H, K, generator=g), dim=-1).to(torch.bfloat16)
+    k = torch.nn.functional.normalize(torch.randn(B, T, H, K, generator=g), dim=-1).to(torch.bfloat16)
+    v = torch.randn(B, T, HV, K, generator=g).to(torch.bfloat16)
+    st = torch.randn(pool, HV, K, K, generator=g) * 0.1
+    A_log = torch.rand(HV, generator=g)
+    a = torch.randn(B, T, HV, generator=g).to(torch.bfloat16)
+    dt = torch.rand(HV, generator=g) - 0.5
+    b = torch.randn(B, T, HV, generator=g).to(torch.bfloat16)
+    idx = torch.tensor([4, -1, 0, 5])
+    by_slot = torch.zeros(pool, T, HV, K, K)
+    oracle.mtp(q, k, v, st, idx, A_log, a, dt, b, 0.0, intermediate_states_buffer=by_slot)
+    by_entry = torch.full((B, T, HV, K, K), 7.0)
+    oracle.mtp(q, k, v, st, idx, A_log, a, dt, b, 0.0, intermediate_states_buffer=by_entry,
+               snapshots_by_entry=True)
+    for i, s in enumerate(idx.tolist()):
+        if s < 0:
+            assert torch.all(by_entry[i] == 7.0)
+        else:
+            assert torch.equal(by_entry[i], by_slot[s])
+    # a buffer of 3 entries' rows with cache_steps = T + 1: rows i * T + t, entry 3 does not fit
+    packed = torch.full((3, T + 1, HV, K, K), 7.0)
+    oracle.mtp(q, k, v, st, idx, A_log, a, dt, b, 0.0, intermediate_states_buffer=packed,
+               snapshots_by_entry=True)
+    rows = packed.view(-1, HV, K, K)
+    for i, s in enumerate(idx.tolist()):
+        for t in range(T):
+            r = i * T + t
+            if s >= 0 and (i + 1) * T <= rows.shape[0]:
+                assert torch.equal(rows[r], by_slot[s, t])
+            elif r < rows.shape[0]:
+                assert torch.all(rows[r] == 7.0)
