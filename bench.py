@@ -375,11 +375,14 @@ def bench_ours(args, rank, world, local):
     p_hs = torch.empty((1, HV, D, D), dtype=torch.float32).pin_memory()
     p_d2h = p_ho.numel() * 2 + p_hs.numel() * 4
 
+    # gdn_prefill_fwd_host's launches per call: the int32 cu_seqlens widened
+    # once, then a cu kernel, the prep and the chain per 2048-token segment
+    host_pre_launches = (0 if phost[8].dtype == torch.int64 else 1) + 3 * ((PREFILL_T + 2047) // 2048)
+
     def pre_e2e_step():
-        dv = [x.to(dev, non_blocking=True) if isinstance(x, torch.Tensor) else x for x in phost]
-        o, s = gdn_prefill.run(*dv)
-        p_ho.copy_(o, non_blocking=True)
-        p_hs.copy_(s, non_blocking=True)
+        # the host-buffer entry point (gdn_prefill_fwd_host): 2048-token segments
+        # copied up, prefilled and copied back on overlapping streams
+        gdn_prefill.run_host_into(*phost, p_ho, p_hs, device=dev)
 
     for _ in range(2):
         pre_e2e_step()
@@ -432,14 +435,17 @@ def bench_ours(args, rank, world, local):
                 "path": "gdn_decode.run_host_into -> C-ABI gdn_decode_fwd_host: pinned host inputs -> "
                         "device -> pinned host outputs, batch slices of ~16 MiB of state with the two "
                         "copy directions overlapped"},
-        # one kernel per decode / prefill call, one per batch slice of the
-        # host-buffer decode; counted over every timed region
-        "gpu_launches": 6 * args.steps + e2e_steps * host_slices + pe2e_steps,
+        # one kernel per decode / MTP call, two per prefill call (prep + chain),
+        # one per batch slice of the host-buffer decode, and per host-buffer
+        # prefill step a cu_seqlens widening plus (cu, prep, chain) per segment;
+        # counted over every timed region
+        "gpu_launches": 7 * args.steps + e2e_steps * host_slices + pe2e_steps * host_pre_launches,
         "gpu_launches_by_region": {"decode": args.steps, "decode_clean_l2": args.steps,
-                                   "decode_b1024": args.steps, "prefill": args.steps,
+                                   "decode_b1024": args.steps, "prefill": 2 * args.steps,
                                    "mtp": args.steps,
                                    "decode_bf16_state": args.steps,
-                                   "decode_e2e": e2e_steps * host_slices, "prefill_e2e": pe2e_steps},
+                                   "decode_e2e": e2e_steps * host_slices,
+                                   "prefill_e2e": pe2e_steps * host_pre_launches},
         "clocks": clocks,
         "decode_b1024": {
             "metric": f"gdn_decode state GB/s, one B={DECODE_B_STRONG} batch split across the ranks",
@@ -459,7 +465,9 @@ def bench_ours(args, rank, world, local):
                          "traffic": profile_traffic("gdn_prefill_T8192_ncu.txt"),
                          "alg_flops_per_launch": pre_flops, "peak_src": peaks["src"]},
             "e2e": {"value": round(PREFILL_T * world / (pe2e_step_ms * 1e-3), 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h},
+                    "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h,
+                    "path": "gdn_prefill.run_host_into -> C-ABI gdn_prefill_fwd_host: pinned host inputs, "
+                            "2048-token segments uploaded / prefilled / downloaded on overlapping streams"},
         },
         "mtp": {
             "metric": f"gdn_mtp GB/s at B={MTP_B}, T={MTP_T} (pool 128 slots, snapshots, in place)",

@@ -51,7 +51,7 @@ extern "C" {
 
 /* Version of this ABI (bumped on any signature change or addition; 3 adds
  * gdn_mtp_fwd and gdn_prefill_fwd_checkpointed, 4 gdn_decode_fwd_host,
- * gdn_prefill_fwd_ex and gdn_mtp_fwd's flags word). */
+ * gdn_prefill_fwd_host, gdn_prefill_fwd_ex and gdn_mtp_fwd's flags word). */
 int gdn_abi_version(void);
 
 /* Human-readable text for a status code. */
@@ -176,6 +176,38 @@ int gdn_prefill_fwd_ex(const void *q, const void *k, const void *v, const float 
                        float *state_checkpoints, const int64_t *checkpoint_cu_starts,
                        long long num_checkpoints, int checkpoint_every_n_tokens, int flags,
                        void *workspace, size_t workspace_bytes, void *stream);
+
+/*
+ * gdn_prefill_fwd with every operand in HOST memory (q .. b, state, the
+ * [N + 1] cu_seqlens, out and new_state host pointers; pinned memory for the
+ * copies to overlap): for a caller that keeps tokens and states off the
+ * device.  No counterpart in the reference, whose `run` takes device tensors
+ * (solutions/gdn_prefill/main.py:31-84).
+ *
+ * The tokens are cut into segments of `segment_tokens` (0: 2048; rounded up
+ * to a multiple of 64).  Segment s + 1 is copied up on a stream this library
+ * creates per device while segment s is prefilled on `stream` and segment
+ * s - 1's output is copied back on a second library stream; every sequence's
+ * running state stays in `workspace` between segments, so a sequence cut by a
+ * segment boundary continues from its state (the results equal one
+ * gdn_prefill_fwd call to rounding: a cut moves the boundary between two of
+ * its tensor-core chunks only when the sequence does not start on a multiple
+ * of 64 tokens).  cu_seqlens is read and validated on the host (non-decreasing,
+ * within [0, T]: else GDN_ERR_INVALID).  `stream` waits for the last copy
+ * back; each call first waits for the previous call's on this device, so one
+ * workspace (device memory, 256-byte aligned, at least
+ * gdn_prefill_host_workspace_bytes(N, T, H, HV, segment_tokens) bytes) may be
+ * reused from any stream.  Not for use inside a stream capture.
+ */
+int gdn_prefill_fwd_host(const void *q, const void *k, const void *v, const float *state,
+                         const float *A_log, const void *a, const float *dt_bias, const void *b,
+                         const void *cu_seqlens, int cu_seqlens_is_int64, int N, int T, float scale,
+                         int H, int HV, int K, int V, void *out, float *new_state, void *workspace,
+                         size_t workspace_bytes, int segment_tokens, void *stream);
+
+/* Device workspace bytes gdn_prefill_fwd_host needs: every sequence's state,
+ * two segments of inputs and outputs, and one segment's chunk workspace. */
+size_t gdn_prefill_host_workspace_bytes(int N, int T, int H, int HV, int segment_tokens);
 
 /*
  * Workspace bytes gdn_prefill_fwd needs for (N, T, H, HV): 0 when the call

@@ -39,6 +39,9 @@ SIGNATURES = {
     "gdn_prefill_fwd_ex": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                                 _i, _i, _f, _i, _i, _i, _i, _vp, _vp,
                                 _vp, _vp, ctypes.c_longlong, _i, _i, _vp, ctypes.c_size_t, _vp]),
+    "gdn_prefill_fwd_host": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
+                                  _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp, ctypes.c_size_t, _i, _vp]),
+    "gdn_prefill_host_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i, _i]),
     "gdn_prefill_workspace_bytes": (ctypes.c_size_t, [_i, _i, _i, _i]),
     "gdn_prefill_fwd_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                                      _i, _i, _f, _i, _i, _i, _i, _vp, _vp, _vp]),

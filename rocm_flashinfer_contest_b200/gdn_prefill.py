@@ -25,6 +25,9 @@ sequence is written to its slots.
 ``use_qk_l2norm_in_kernel=True`` (keyword-only, the option of the AITER
 kernels the reference calls, solutions/gdn_prefill/main.py:72,79) normalises
 every q and k head vector in the kernel as x * rsqrt(sum(x^2) + 1e-6).
+``run_host_into(...)`` is the same prefill for tensors in pinned host memory
+(``gdn_prefill_fwd_host``): token segments are copied up, prefilled and
+copied back on overlapping streams.
 Inputs are never modified; ``run_into`` is the destination-passing form and
 accepts ``new_state is state``.  The chunked kernels' workspace
 (gdn_prefill_workspace_bytes) comes from torch's caching allocator, so a
@@ -156,3 +159,58 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *,
                     state_checkpoints=state_checkpoints, checkpoint_cu_starts=checkpoint_cu_starts,
                     checkpoint_every_n_tokens=checkpoint_every_n_tokens,
                     use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+
+
+def run_host_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, *,
+                  device=None, segment_tokens: int = 0):
+    """Prefill with every tensor in pinned host memory (``gdn_prefill_fwd_host``):
+    writes ``output`` [T,HV,V] bf16 and ``new_state`` [N,HV,V,K] fp32 (host,
+    pinned) and returns them.  ``cu_seqlens`` is a host int32/int64 tensor.
+    The work is queued on ``device`` (default: the current CUDA device) on its
+    current stream, which continues after the last copy back, so a
+    synchronisation of that stream (or an event recorded on it) marks the
+    results as ready.  Tokens go up, through the kernels and back in segments
+    of ``segment_tokens`` (0: 2048) on overlapping streams; the results equal
+    ``run`` on device copies to rounding.  The inputs must stay unmodified and
+    alive until then, as with any non-blocking copy."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    host = {"q": q, "k": k, "v": v, "a": a, "b": b, "A_log": A_log, "dt_bias": dt_bias,
+            "cu_seqlens": cu_seqlens, "output": output, "new_state": new_state}
+    if state is not None:
+        host["state"] = state
+    for name, t in host.items():
+        if not isinstance(t, torch.Tensor) or t.device.type != "cpu" or not t.is_contiguous() \
+                or (t.numel() > 0 and not t.is_pinned()):
+            raise ValueError(f"{name} must be a contiguous pinned host tensor")
+    if q.dim() != 3:
+        raise ValueError(f"q must be [T, H, K], got {tuple(q.shape)}")
+    T, H, K = q.shape
+    if v.dim() != 3:
+        raise ValueError(f"v must be [T, HV, V], got {tuple(v.shape)}")
+    HV, V = v.shape[1], v.shape[2]
+    if cu_seqlens.dim() != 1 or cu_seqlens.dtype not in (torch.int32, torch.int64):
+        raise ValueError("cu_seqlens must be a 1-D int32 or int64 tensor")
+    N = cu_seqlens.numel() - 1
+    bf, f32 = torch.bfloat16, torch.float32
+    spec = {"q": (bf, (T, H, K)), "k": (bf, (T, H, K)), "v": (bf, (T, HV, V)), "a": (bf, (T, HV)),
+            "b": (bf, (T, HV)), "A_log": (f32, (HV,)), "dt_bias": (f32, (HV,)), "output": (bf, (T, HV, V)),
+            "new_state": (f32, (N, HV, V, K)), "state": (f32, (N, HV, V, K))}
+    for name, t in host.items():
+        if name in spec and (t.dtype != spec[name][0] or tuple(t.shape) != spec[name][1]):
+            raise ValueError(f"{name} must be {spec[name][0]} {spec[name][1]}, got {t.dtype} {tuple(t.shape)}")
+    L = lib()
+    nbytes = L.gdn_prefill_host_workspace_bytes(N, T, H, HV, int(segment_tokens))
+    if nbytes == 0:
+        return output, new_state
+    with torch.cuda.device(dev):
+        # allocated on the stream the call joins at its end: freeing it when this
+        # function returns is ordered after the last copy back
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        st = L.gdn_prefill_fwd_host(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), None if state is None else state.data_ptr(),
+            A_log.data_ptr(), a.data_ptr(), dt_bias.data_ptr(), b.data_ptr(), cu_seqlens.data_ptr(),
+            int(cu_seqlens.dtype == torch.int64), N, T, C.normalize_scale(scale, K), H, HV, K, V,
+            output.data_ptr(), new_state.data_ptr(), ws.data_ptr(), ws.numel(), int(segment_tokens),
+            C.stream_handle(dev))
+    check("gdn_prefill_fwd_host", st)
+    return output, new_state

@@ -218,6 +218,46 @@ def test_prefill_ex_rejects_bad_arguments(over, code):
     assert _prefill_ex(**over) == code
 
 
+def _prefill_host(cu, **over):
+    import numpy as np
+    cu_arr = np.asarray(cu, dtype=np.int64)
+    N, T = len(cu) - 1, over.pop("T", 8)
+    need = _lib.lib().gdn_prefill_host_workspace_bytes(N, T, 1, 2, 0)
+    d = dict(q=16, k=16, v=16, state=16, A_log=16, a=16, dt_bias=16, b=16, cu=cu_arr.ctypes.data, cu64=1,
+             N=N, T=T, scale=0.0, H=1, HV=2, K=128, V=128, out=16, new_state=16, ws=4096, ws_bytes=need,
+             seg=0, stream=None)
+    d.update(over)
+    return _lib.lib().gdn_prefill_fwd_host(*d.values())
+
+
+@pytest.mark.parametrize("cu,over,code", [
+    ([0, 5, 3], {}, _lib.GDN_ERR_INVALID),                 # cu_seqlens decreasing (read on the host)
+    ([0, 9], {}, _lib.GDN_ERR_INVALID),                    # cu_seqlens[N] > T
+    ([-1, 4], {}, _lib.GDN_ERR_INVALID),
+    ([0, 8], dict(ws_bytes=1024), _lib.GDN_ERR_INVALID),   # workspace too small
+    ([0, 8], dict(ws=4096 + 64), _lib.GDN_ERR_ALIGN),
+    ([0, 8], dict(seg=-1), _lib.GDN_ERR_INVALID),
+    ([0, 8], dict(cu64=2), _lib.GDN_ERR_INVALID),
+    ([0, 8], dict(K=64), _lib.GDN_ERR_UNSUPPORTED),
+    ([0, 8], dict(out=None), _lib.GDN_ERR_INVALID),
+    ([0], dict(T=0), _lib.GDN_OK),                          # nothing to do: no CUDA call
+])
+def test_prefill_host_rejects_bad_arguments(cu, over, code):
+    assert _prefill_host(cu, **over) == code
+
+
+def test_prefill_host_workspace_bytes():
+    f = _lib.lib().gdn_prefill_host_workspace_bytes
+    assert f(0, 0, 16, 32, 0) == 0 and f(-1, 8, 16, 32, 0) == 0 and f(1, 8, 16, 32, -1) == 0
+    # one sequence of 8192 tokens in 2048-token segments: its state, two segments of
+    # q, k, v, a, b and output, and one segment's chunk workspace
+    seg_io = 2048 * (2 * 16 * 128 * 2 + 2 * 32 * 128 * 2 + 2 * 32 * 2)
+    assert f(1, 8192, 16, 32, 0) >= 32 * 128 * 128 * 4 + 2 * seg_io
+    assert f(1, 8192, 16, 32, 0) == f(1, 8192, 16, 32, 2048)
+    assert f(1, 8192, 16, 32, 1024) < f(1, 8192, 16, 32, 2048)
+    assert f(4, 100, 16, 32, 0) > 0 and f(0, 100, 16, 32, 0) > 0   # T < 2048: one 128-token segment
+
+
 def test_prefill_workspace_size(monkeypatch):
     ws = _lib.lib().gdn_prefill_workspace_bytes
     per_slot = lambda H, HV: HV * 17424 + H * (32768 + 16384)  # noqa: E731
