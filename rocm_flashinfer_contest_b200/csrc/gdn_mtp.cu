@@ -154,8 +154,25 @@ __device__ __forceinline__ void mtp_load_token(MtpToken<kPasses>& tk, const MtpP
 
 // ROWS_PER_CTA rows of one (batch entry, v-head) per CTA of 4 warps; the pool
 // holds StateT (float or __nv_bfloat16).
+// Resident CTAs per SM each instantiation is compiled for (register cap
+// 65536 / (128 * n)).  The fp32 32-row kernels stream the pool at B = 64 and
+// gain from one more resident CTA (more state bytes in flight): the T > 1
+// kernel 149.5 -> 141.3 us at T = 4 with 96 instead of 123 registers, the
+// T = 1 kernel 47.1 -> 46.1 us with 80 instead of 92, both without spills
+// of note; the other instantiations keep the occupancy their register
+// counts give them (a tighter cap made the bf16 64-row decode spill and
+// run slower).
+template <int ROWS, typename StateT>
+constexpr int mtp_min_blocks() {
+    return sizeof(StateT) == 4 ? 5 : (ROWS == 64 ? 3 : ROWS == 32 ? 4 : 5);
+}
+template <int ROWS, typename StateT>
+constexpr int pool_decode_min_blocks() {
+    return sizeof(StateT) == 4 ? (ROWS == 32 ? 6 : 8) : (ROWS == 64 ? 5 : 8);
+}
+
 template <int ROWS_PER_CTA, typename StateT>
-__global__ void __launch_bounds__(128) gdn_mtp_kernel(const MtpParams p) {
+__global__ void __launch_bounds__(128, mtp_min_blocks<ROWS_PER_CTA, StateT>()) gdn_mtp_kernel(const MtpParams p) {
     constexpr int kRowsPerWarp = ROWS_PER_CTA / 4;
     constexpr int kPasses = kRowsPerWarp / 4;
     constexpr int kBlocksPerHead = kDim / ROWS_PER_CTA;
@@ -305,7 +322,8 @@ __device__ __forceinline__ void pack_widen(const RowPack<__nv_bfloat16>& r, floa
 }
 
 template <int ROWS_PER_CTA, typename StateT>
-__global__ void __launch_bounds__(128) gdn_pool_decode_kernel(const MtpParams p) {
+__global__ void __launch_bounds__(128, pool_decode_min_blocks<ROWS_PER_CTA, StateT>())
+    gdn_pool_decode_kernel(const MtpParams p) {
     constexpr int kRowsPerWarp = ROWS_PER_CTA / 4;
     constexpr int kPasses = kRowsPerWarp / 4;
     constexpr int kBlocksPerHead = kDim / ROWS_PER_CTA;
