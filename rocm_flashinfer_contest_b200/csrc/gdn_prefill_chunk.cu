@@ -510,29 +510,32 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
             st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), d);
             st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), d + 8);
         }
+    } else {
+        // meanwhile the chunk's gate record, in the T operand region that
+        // MMA_P (complete) no longer reads: gamma <= 0, so every factor is
+        // in (0, 1] (times scale)
+        float* gr = reinterpret_cast<float*>(sm + OFF_TB);
+        const float eg = expf(sG[tid]);
+        gr[GR_BEG + tid] = sBeta[tid] * eg;
+        gr[GR_BETA + tid] = sBeta[tid];
+        gr[GR_FK + tid] = expf(fminf(sG[C - 1] - sG[tid], 0.f));
+        gr[GR_FQ + tid] = p.scale * eg;
+        if (tid < 4) gr[GR_DECAY + tid] = expf(sG[C - 1]);
     }
+    umma::fence_proxy_async_smem();  // the tile's rows and the gate record -> the bulk copies below
     __syncthreads();
 
-    // slot <- [T ; P'] tile as laid out in shared memory, gamma, beta
+    // slot <- [T ; P'] tile as laid out in shared memory and the gate record (two bulk copies)
     {
         unsigned char* slot = ws + ((size_t)s * p.HV + hv) * kSlotBytes;
-#pragma unroll
-        for (int it = 0; it < (int)(kTileTP / 16 / NT); ++it) {
-            const int idx = tid + it * NT;
-            reinterpret_cast<uint4*>(slot)[idx] = reinterpret_cast<const uint4*>(sm + OFF_TP)[idx];
+        if (tid == 0) {
+            umma::bulk_s2g(slot, umma::smem_u32(sm + OFF_TP), kTileTP);
+            umma::bulk_s2g(slot + kTileTP, umma::smem_u32(sm + OFF_TB), kGateBytes);
         }
-        float* gr = reinterpret_cast<float*>(slot + kTileTP);
-        if (tid < 64) {  // gamma <= 0: every factor is in (0, 1] (times scale)
-            const float eg = expf(sG[tid]);
-            gr[GR_BEG + tid] = sBeta[tid] * eg;
-            gr[GR_BETA + tid] = sBeta[tid];
-            gr[GR_FK + tid] = expf(fminf(sG[C - 1] - sG[tid], 0.f));
-            gr[GR_FQ + tid] = p.scale * eg;
-        }
-        if (tid < 4) gr[GR_DECAY + tid] = expf(sG[C - 1]);
     }
 
 done:
+    if (tid == 0) umma::bulk_wait_read0();  // the tile and gates stay in shared memory until copied out
     umma::fence_before_sync();
     __syncthreads();
     if (warp == 0) umma::tmem_dealloc(tmem, TM_COLS);

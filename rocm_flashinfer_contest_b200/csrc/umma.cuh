@@ -211,6 +211,19 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst_smem, const void* src, uin
         :: "r"(dst_smem), "l"(src), "r"(bytes), "r"(smem_u32(mbar)) : "memory");
 }
 
+// Shared -> global bulk copy (TMA engine, no multicast), in a bulk group of
+// the issuing thread: both addresses 16-byte aligned, bytes a multiple of 16;
+// the source must be fenced (fence_proxy_async_smem) after the threads that
+// wrote it and before the issue.  bulk_wait_read0 returns once every such
+// copy of the thread has read its source, after which it may be reused (or
+// the CTA exit); the global writes are complete when the kernel is.
+__device__ __forceinline__ void bulk_s2g(void* dst, uint32_t src_smem, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" :: "l"(dst), "r"(src_smem), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // ---- TMEM -> registers (32 lanes x 32 bit, one lane per thread) ----
 
 // 16 consecutive fp32 columns starting at `taddr` for this warp's 32 lanes
