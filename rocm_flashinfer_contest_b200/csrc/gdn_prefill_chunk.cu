@@ -164,27 +164,36 @@ namespace prep {
 
 constexpr int NT = 128;
 constexpr uint32_t OFF_KQ = 0;                     // [K ; Q] bf16 K-major 128 x 128   32 KiB
-// A and the level scratch X only live after MMA_A has consumed [K ; Q], so
-// they share its 32 KiB; three CTAs fit on an SM.
+// A and T only live after MMA_A has consumed [K ; Q], so they take its
+// 32 KiB and 2 KiB more; with the [T ; P] tile, the gate record and the gates
+// a CTA holds ~52 KiB and four CTAs (and their 4 x 128 TMEM columns) fit on
+// an SM.
 constexpr uint32_t OFF_A = 0;                      // A fp32 [64][LDA]                 17 KiB
-constexpr uint32_t OFF_X = OFF_A + 64 * LDA * 4;   // solve scratch, rows 16-63        12.75 KiB
-constexpr uint32_t OFF_TP = 32768;                 // [T ; P] f16 K-major 128 x 64     16 KiB
-constexpr uint32_t OFF_TB = OFF_TP + kTileTP;      // T as MN-major B (m x j) f16        8 KiB
-constexpr uint32_t OFF_T = OFF_TB + 8192;          // T fp32 [64][LDA]                 17 KiB
-constexpr uint32_t OFF_G = OFF_T + 64 * LDA * 4;   // gamma[64]
+constexpr uint32_t OFF_T = 64 * LDA * 4;           // T fp32 [64][LDA]                 17 KiB
+constexpr uint32_t OFF_TP = 2 * 64 * LDA * 4;      // [T ; P] f16 K-major 128 x 64     16 KiB
+constexpr uint32_t OFF_GR = OFF_TP + kTileTP;      // gate record (kGateBytes)
+constexpr uint32_t OFF_G = OFF_GR + 1056;          // gamma[64]
 constexpr uint32_t OFF_BETA = OFF_G + 256;         // beta[64]
 constexpr uint32_t SMEM_BYTES = OFF_BETA + 256 + 1024;  // + alignment slack
-static_assert(OFF_X + 48 * LDA * 4 <= OFF_TP, "A and X fit in the [K ; Q] tile");
+static_assert(OFF_TP % 1024 == 0 && OFF_TP >= kTileKQ, "[T ; P] tile after [K ; Q], 1 KiB aligned");
+static_assert(kGateBytes <= OFF_G - OFF_GR, "gate record fits");
+static_assert(4 * (SMEM_BYTES + 1024) <= 233472, "four CTAs per SM");
 // The previous chunk's K rows (bf16, K-major 64 x 128) for the cross-Gram
 // G_j = [K ; Q]_j K_{j-1}^T borrow the [T ; P] region, which is only written
 // after G has been computed.
 constexpr uint32_t OFF_KP = OFF_TP;
 constexpr uint32_t TM_COLS = 128;  // columns 0-63: [K ; Q] K^T, then P'; 64-127: G
 
-// Blocked T = (I + A)^-1 for the 64 x 64 strictly lower A in sA (fp32, row
-// stride LDA); writes T into sT, whose upper blocks must already be zero.
-// sX holds rows 16-63 of the level scratch X.
-__device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, int tid) {
+// Element (r, c) of a 64 x 64 fp32 solve matrix: rows padded to LDA floats,
+// so eight consecutive rows put one float4 column on all 32 banks (the masks'
+// row-per-thread stores), and so do rows r, r + 4, r + 8, r + 12 (the solve's
+// four-row float4 loads); offsets stay compile-time immediates.
+__device__ __forceinline__ int sw(int r, int c) { return r * LDA + c; }
+
+// Blocked T = (I + A)^-1 for the 64 x 64 strictly lower A in sA; writes the
+// diagonal and lower 16 x 16 blocks of T into sT (the upper blocks are never
+// read).  Every matrix access goes through sw().
+__device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
     // diagonal blocks: warp b inverts I + A_bb by right-looking substitution,
     // lane l < 16 owning column l
@@ -197,10 +206,10 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
         for (int j = 0; j < 16; ++j) {
             const float xj = x[j];
 #pragma unroll
-            for (int r = j + 1; r < 16; ++r) x[r] -= sA[(b0 + r) * LDA + b0 + j] * xj;
+            for (int r = j + 1; r < 16; ++r) x[r] -= sA[sw(b0 + r, b0 + j)] * xj;
         }
 #pragma unroll
-        for (int r = 0; r < 16; ++r) sT[(b0 + r) * LDA + b0 + lane] = x[r];
+        for (int r = 0; r < 16; ++r) sT[sw(b0 + r, b0 + lane)] = x[r];
     }
     __syncthreads();
     // Off-diagonal blocks, one column block at a time: for i > j,
@@ -208,8 +217,9 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
     // Column blocks are independent once the diagonal inverses exist, so each
     // warp walks down its own 8 columns of one (warps 0, 3: column block 0)
     // or two (warps 1, 2: column blocks 1 and 2) column blocks; a lane holds
-    // 4 rows of one column.  Only the warp's own lanes exchange X and T
-    // values, so the walk needs no block-wide barrier.
+    // 4 rows of one column.  X_ij passes through the T_ij block itself (only
+    // this warp touches these columns), so the walk needs no block-wide
+    // barrier and no scratch matrix.
     const int half = (warp == 0 || warp == 1) ? 0 : 1;
     const int cc = 8 * half + (lane & 7);  // column within the column block
     const int rq = (lane >> 3) * 4;        // first of this lane's 4 rows
@@ -217,49 +227,57 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, float* sX, i
     const int jlast = (warp == 0 || warp == 3) ? 0 : 2;
 #pragma unroll 1
     for (int j = jfirst; j <= jlast; ++j) {
+        const int col = 16 * j + cc;
 #pragma unroll 1
         for (int i = j + 1; i < 4; ++i) {
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
             for (int k = j; k < i; ++k) {
-                const float* a = sA + (16 * i + rq) * LDA + 16 * k;
-                const float* t = sT + (16 * k) * LDA + 16 * j + cc;
 #pragma unroll
                 for (int s4 = 0; s4 < 16; s4 += 4) {
-                    const float t0 = t[(s4 + 0) * LDA], t1 = t[(s4 + 1) * LDA];
-                    const float t2 = t[(s4 + 2) * LDA], t3 = t[(s4 + 3) * LDA];
+                    const float t0 = sT[sw(16 * k + s4 + 0, col)], t1 = sT[sw(16 * k + s4 + 1, col)];
+                    const float t2 = sT[sw(16 * k + s4 + 2, col)], t3 = sT[sw(16 * k + s4 + 3, col)];
 #pragma unroll
                     for (int r = 0; r < 4; ++r) {
-                        const float4 x = *reinterpret_cast<const float4*>(a + r * LDA + s4);
+                        const float4 x = *reinterpret_cast<const float4*>(sA + sw(16 * i + rq + r, 16 * k + s4));
                         acc[r] = fmaf(x.x, t0, fmaf(x.y, t1, fmaf(x.z, t2, fmaf(x.w, t3, acc[r]))));
                     }
                 }
             }
 #pragma unroll
-            for (int r = 0; r < 4; ++r) sX[(16 * i - 16 + rq + r) * LDA + 16 * j + cc] = acc[r];
+            for (int r = 0; r < 4; ++r) sT[sw(16 * i + rq + r, col)] = acc[r];
             __syncwarp();
-            const float* tii = sT + (16 * i + rq) * LDA + 16 * i;
-            const float* xc = sX + (16 * i - 16) * LDA + 16 * j + cc;
+            float xc[16];
+#pragma unroll
+            for (int s = 0; s < 16; ++s) xc[s] = sT[sw(16 * i + s, col)];
+            __syncwarp();  // every lane holds its X column before T_ij replaces it
             float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int s4 = 0; s4 < 16; s4 += 4) {
-                const float x0 = xc[(s4 + 0) * LDA], x1 = xc[(s4 + 1) * LDA];
-                const float x2 = xc[(s4 + 2) * LDA], x3 = xc[(s4 + 3) * LDA];
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    const float4 y = *reinterpret_cast<const float4*>(tii + r * LDA + s4);
-                    o[r] = fmaf(y.x, x0, fmaf(y.y, x1, fmaf(y.z, x2, fmaf(y.w, x3, o[r]))));
+                    const float4 y = *reinterpret_cast<const float4*>(sT + sw(16 * i + rq + r, 16 * i + s4));
+                    o[r] = fmaf(y.x, xc[s4], fmaf(y.y, xc[s4 + 1], fmaf(y.z, xc[s4 + 2], fmaf(y.w, xc[s4 + 3], o[r]))));
                 }
             }
 #pragma unroll
-            for (int r = 0; r < 4; ++r) sT[(16 * i + rq + r) * LDA + 16 * j + cc] = -o[r];
+            for (int r = 0; r < 4; ++r) sT[sw(16 * i + rq + r, col)] = -o[r];
             __syncwarp();
         }
     }
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const PrefillParams p, unsigned char* ws) {
+// MMA_P reads rows 0-63 of the K-major [T ; P] tile as an MN-major operand.
+constexpr bool t_rows_are_mn_major() {
+    for (uint32_t i = 0; i < 64; ++i)
+        for (uint32_t j = 0; j < 64; ++j)
+            if (umma::kmaj_off(i, j, 128) != umma::mnmaj_off(j, i, 64)) return false;
+    return true;
+}
+static_assert(t_rows_are_mn_major(), "T rows of the [T ; P] tile double as the MN-major B operand");
+
+__global__ void __launch_bounds__(NT, 4) gdn_prefill_chunk_prep_kernel(const PrefillParams p, unsigned char* ws) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -288,7 +306,6 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
 
     float* sA = reinterpret_cast<float*>(sm + OFF_A);
     float* sT = reinterpret_cast<float*>(sm + OFF_T);
-    float* sX = reinterpret_cast<float*>(sm + OFF_X);
     float* sG = reinterpret_cast<float*>(sm + OFF_G);
     float* sBeta = reinterpret_cast<float*>(sm + OFF_BETA);
 
@@ -439,7 +456,7 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
                 if (tid < 64) {
 #pragma unroll
                     for (int e = 0; e < 16; e += 4)
-                        *reinterpret_cast<float4*>(sA + i * LDA + c16 + e) = make_float4(0.f, 0.f, 0.f, 0.f);
+                        *reinterpret_cast<float4*>(sA + sw(i, c16 + e)) = make_float4(0.f, 0.f, 0.f, 0.f);
                 } else {
                     st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), r);
                     st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), r + 8);
@@ -452,7 +469,7 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
                 }
 #pragma unroll
                 for (int e = 0; e < 16; e += 4)
-                    *reinterpret_cast<float4*>(sA + i * LDA + c16 + e) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
+                    *reinterpret_cast<float4*>(sA + sw(i, c16 + e)) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
             } else {
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
@@ -467,32 +484,33 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
     }
     __syncthreads();
 
-    // T = (I + A)^-1; f16 copies: rows 0-63 of [T ; P] and T as MN-major B
-    solve_T(sA, sT, sX, tid);
+    // T = (I + A)^-1; f16 copy: rows 0-63 of [T ; P]
+    solve_T(sA, sT, tid);
     {
         const int i = tid >> 1, h = (tid & 1) * 32;  // row i, columns h..h+31
-        const float* tr = sT + i * LDA + h;
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
             // blocks above the diagonal are zero and are never stored in sT
             float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             if (((h + c) >> 4) <= (i >> 4)) {
-                const float4 a = *reinterpret_cast<const float4*>(tr + c);
-                const float4 b = *reinterpret_cast<const float4*>(tr + c + 4);
+                const float4 a = *reinterpret_cast<const float4*>(sT + sw(i, h + c));
+                const float4 b = *reinterpret_cast<const float4*>(sT + sw(i, h + c + 4));
                 x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
                 x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
             }
-            st_f16x8(sm + OFF_TP, umma::kmaj_off(i, h + c, 128), x);  // A rows: T[i][j]
-            st_f16x8(sm + OFF_TB, umma::mnmaj_off(h + c, i, C), x);   // B: (n = m, k = j) = T[j][m]
+            st_f16x8(sm + OFF_TP, umma::kmaj_off(i, h + c, 128), x);  // T[i][j]
         }
     }
     sync_for_mma();
 
-    // MMA_P: [T ; P] T -> rows 64-127 = P' = P T
+    // MMA_P: [T ; P] T -> rows 64-127 = P' = P T.  The B operand is T read
+    // MN-major from rows 0-63 of the same tile: for a row i < 64 the K-major
+    // byte offset of (i, j) equals the MN-major offset of (mn = j, k = i)
+    // with a K extent of 64, so those 8 KiB are T as a (k = i, n = j) operand.
     if (tid == 0) {
         constexpr uint32_t ID = umma::idesc_f16(128, 64, 0, 0, 0, 1);
         const uint64_t dTP = umma::desc_kmaj(umma::smem_u32(sm + OFF_TP), 128, 0);
-        const uint64_t dTB = umma::desc_mnmaj(umma::smem_u32(sm + OFF_TB), C, 0);
+        const uint64_t dTB = umma::desc_mnmaj(umma::smem_u32(sm + OFF_TP), C, 0);
 #pragma unroll
         for (int k0 = 0; k0 < C; k0 += 16)
             umma::mma_f16(tmem, umma::desc_add(dTP, umma::koff_kmaj(128, k0)), umma::desc_add(dTB, umma::koff_mnmaj(k0)),
@@ -511,10 +529,9 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
             st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), d + 8);
         }
     } else {
-        // meanwhile the chunk's gate record, in the T operand region that
-        // MMA_P (complete) no longer reads: gamma <= 0, so every factor is
+        // meanwhile the chunk's gate record: gamma <= 0, so every factor is
         // in (0, 1] (times scale)
-        float* gr = reinterpret_cast<float*>(sm + OFF_TB);
+        float* gr = reinterpret_cast<float*>(sm + OFF_GR);
         const float eg = expf(sG[tid]);
         gr[GR_BEG + tid] = sBeta[tid] * eg;
         gr[GR_BETA + tid] = sBeta[tid];
@@ -530,7 +547,7 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_chunk_prep_kernel(const Pre
         unsigned char* slot = ws + ((size_t)s * p.HV + hv) * kSlotBytes;
         if (tid == 0) {
             umma::bulk_s2g(slot, umma::smem_u32(sm + OFF_TP), kTileTP);
-            umma::bulk_s2g(slot + kTileTP, umma::smem_u32(sm + OFF_TB), kGateBytes);
+            umma::bulk_s2g(slot + kTileTP, umma::smem_u32(sm + OFF_GR), kGateBytes);
         }
     }
 
