@@ -433,52 +433,40 @@ __global__ void __launch_bounds__(NT, 4) gdn_prefill_chunk_prep_kernel(const Pre
     }
     __syncthreads();  // [K ; Q] is overwritten by A and X from here on
 
-    // masks: rows 0-63 -> A (fp32), rows 64-127 -> P (f16, rows 64-127 of [T ; P])
+    // masks: rows 0-63 -> A (fp32), rows 64-127 -> P (f16, rows 64-127 of [T ; P]).
+    // Both use e^{gamma_i - gamma_j}: A = beta_i e^{..} k_i.k_j for j < i,
+    // P = scale e^{..} q_i.k_j for j <= i; one code path with a per-thread
+    // coefficient and column bound keeps the kernel's instruction footprint
+    // small (four CTAs of this kernel run different phases on one SM).
     {
         const int i = tid & 63;
+        const bool arow = tid < 64;
         const float gi = sG[i];
-        const float bi = sBeta[i];
+        const float coef = arow ? sBeta[i] : p.scale;
+        const int lim = arow ? i : i + 1;  // columns jj < lim are kept
 #pragma unroll 1
-        for (int c32 = 0; c32 < C; c32 += 32) {
-            float d2[2][16];
-            umma::tmem_ld16x2(tmem + lane_base + c32, tmem + lane_base + c32 + 16, d2[0], d2[1]);
-#pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-            const int c16 = c32 + 16 * hh;
-            const float (&d)[16] = d2[hh];
-            float r[16];
-            // the warp's rows are 32 * (warp % 2) .. + 31: a block of columns
-            // past them is all zero (warp-uniform)
-            const bool zero_block = c16 > 32 * (warp & 1) + 31;
-            if (zero_block) {
+        for (int c16 = 0; c16 < C; c16 += 16) {
+            float d[16], r[16];
+            umma::tmem_ld16(tmem + lane_base + c16, d);
+            // the warp's rows are 32 * (warp % 2) .. + 31: a block of
+            // columns past them is all zero (warp-uniform)
+            if (c16 > 32 * (warp & 1) + 31) {
 #pragma unroll
                 for (int e = 0; e < 16; ++e) r[e] = 0.f;
-                if (tid < 64) {
-#pragma unroll
-                    for (int e = 0; e < 16; e += 4)
-                        *reinterpret_cast<float4*>(sA + sw(i, c16 + e)) = make_float4(0.f, 0.f, 0.f, 0.f);
-                } else {
-                    st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), r);
-                    st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), r + 8);
-                }
-            } else if (tid < 64) {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int jj = c16 + e;
-                    r[e] = (jj < i) ? bi * __expf(fminf(gi - sG[jj], 0.f)) * d[e] : 0.f;
-                }
-#pragma unroll
-                for (int e = 0; e < 16; e += 4)
-                    *reinterpret_cast<float4*>(sA + sw(i, c16 + e)) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
             } else {
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     const int jj = c16 + e;
-                    r[e] = (jj <= i) ? p.scale * __expf(fminf(gi - sG[jj], 0.f)) * d[e] : 0.f;
+                    r[e] = (jj < lim) ? coef * __expf(fminf(gi - sG[jj], 0.f)) * d[e] : 0.f;
                 }
+            }
+            if (arow) {
+#pragma unroll
+                for (int e = 0; e < 16; e += 4)
+                    *reinterpret_cast<float4*>(sA + sw(i, c16 + e)) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
+            } else {
                 st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), r);
                 st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), r + 8);
-            }
             }
         }
     }
