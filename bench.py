@@ -376,11 +376,19 @@ def bench_ours(args, rank, world, local):
     p_d2h = p_ho.numel() * 2 + p_hs.numel() * 4
 
     # gdn_prefill_fwd_host's launches per call: the int32 cu_seqlens widened
-    # once, then a cu kernel, the prep and the chain per 2048-token segment
-    host_pre_launches = (0 if phost[8].dtype == torch.int64 else 1) + 3 * ((PREFILL_T + 2047) // 2048)
+    # once, then a cu kernel, the prep and the chain per segment (segments of
+    # 2048 tokens, the last 2048 halved down to 256: the library's
+    # segment_starts schedule)
+    n_seg, s0 = 0, 0
+    while PREFILL_T - s0 > 2048:
+        n_seg, s0 = n_seg + 1, s0 + 2048
+    while PREFILL_T - s0 > 256:
+        n_seg, s0 = n_seg + 1, s0 + ((PREFILL_T - s0) // 2 + 63) // 64 * 64
+    n_seg += 1 if PREFILL_T > s0 else 0
+    host_pre_launches = (0 if phost[8].dtype == torch.int64 else 1) + 3 * n_seg
 
     def pre_e2e_step():
-        # the host-buffer entry point (gdn_prefill_fwd_host): 2048-token segments
+        # the host-buffer entry point (gdn_prefill_fwd_host): token segments
         # copied up, prefilled and copied back on overlapping streams
         gdn_prefill.run_host_into(*phost, p_ho, p_hs, device=dev)
 
@@ -467,7 +475,7 @@ def bench_ours(args, rank, world, local):
             "e2e": {"value": round(PREFILL_T * world / (pe2e_step_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h,
                     "path": "gdn_prefill.run_host_into -> C-ABI gdn_prefill_fwd_host: pinned host inputs, "
-                            "2048-token segments uploaded / prefilled / downloaded on overlapping streams"},
+                            "2048-token segments (the last 2048 tokens as 1024 + 512 + 256 + 256) uploaded / prefilled / downloaded on overlapping streams"},
         },
         "mtp": {
             "metric": f"gdn_mtp GB/s at B={MTP_B}, T={MTP_T} (pool 128 slots, snapshots, in place)",

@@ -185,7 +185,9 @@ int gdn_prefill_fwd_ex(const void *q, const void *k, const void *v, const float 
  * (solutions/gdn_prefill/main.py:31-84).
  *
  * The tokens are cut into segments of `segment_tokens` (0: 2048; rounded up
- * to a multiple of 64).  Segment s + 1 is copied up on a stream this library
+ * to a multiple of 64), the last `segment_tokens` or fewer halved down to
+ * 256-token pieces (2048 -> 1024, 512, 256, 256) so that little work is left
+ * once the last upload has landed.  Segment s + 1 is copied up on a stream this library
  * creates per device while segment s is prefilled on `stream` and segment
  * s - 1's output is copied back on a second library stream; every sequence's
  * running state stays in `workspace` between segments, so a sequence cut by a

@@ -4,7 +4,8 @@
 // PCIe-bound: q, k, v go up and the output comes back (8192 tokens at
 // H = 16, HV = 32: 135 MB up, 67 MB down) while the kernels take a fraction
 // of that.  The tokens are cut into segments (64-token aligned, so chunk
-// boundaries stay where one call would put them) and pipelined over three
+// boundaries stay where one call would put them; the last ones shrink, see
+// segment_starts) and pipelined over three
 // streams: segment s + 1 is copied up (library stream `up`) while segment s
 // is prefilled (the caller's stream) and segment s - 1's output is copied
 // back (library stream `down`).  The running state of every sequence stays
@@ -103,6 +104,29 @@ int effective_segment(int segment_tokens) {
 
 }  // namespace
 
+// Segment starts (and T at the end): segments of `seg` tokens, except that
+// the last `seg` or fewer tokens are cut in halves down to kTailTokens
+// (2048 -> 1024, 512, 256, 256), all 64-aligned.  Once the last upload has
+// landed only the last segment's prefill and copy back are left, so a short
+// last segment keeps that tail short while the long ones keep the per-copy
+// overheads low.
+constexpr long long kTailTokens = 256;
+std::vector<long long> segment_starts(long long T, long long seg) {
+    std::vector<long long> s;
+    long long s0 = 0;
+    while (T - s0 > seg) {
+        s.push_back(s0);
+        s0 += seg;
+    }
+    while (T - s0 > kTailTokens) {
+        s.push_back(s0);
+        s0 += ((T - s0) / 2 + 63) / 64 * 64;
+    }
+    if (T > s0) s.push_back(s0);
+    s.push_back(T);
+    return s;
+}
+
 extern "C" size_t gdn_prefill_host_workspace_bytes(int N, int T, int H, int HV, int segment_tokens) {
     if (N < 0 || T < 0 || H <= 0 || HV <= 0 || segment_tokens < 0 || (N == 0 && T == 0)) return 0;
     const int seg = T > 0 ? std::min(effective_segment(segment_tokens), (T + 63) / 64 * 64) : 64;
@@ -179,11 +203,12 @@ extern "C" int gdn_prefill_fwd_host(const void* q, const void* k, const void* v,
     ok(cudaEventRecord(pp.h2d[1], cs));
     ok(cudaStreamWaitEvent(pp.up, pp.h2d[1], 0));
 
-    const int nseg = T > 0 ? (T + seg - 1) / seg : 0;
+    const std::vector<long long> starts = segment_starts(T, seg);
+    const int nseg = (int)starts.size() - 1;
     for (int si = 0; si < nseg && status == GDN_OK; ++si) {
         const int r = si & 1;
         char* slot = ws + L.ring + (size_t)r * L.ring_stride;
-        const long long s0 = (long long)si * seg, s1 = std::min<long long>((long long)T, s0 + seg);
+        const long long s0 = starts[si], s1 = starts[si + 1];
         const long long nt = s1 - s0;
         // 1. upload the segment (after the prefill of segment si - 2 is done with this slot)
         ok(cudaStreamWaitEvent(pp.up, pp.comp[r], 0));

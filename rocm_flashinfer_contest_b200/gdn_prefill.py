@@ -170,7 +170,8 @@ def run_host_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, outpu
     current stream, which continues after the last copy back, so a
     synchronisation of that stream (or an event recorded on it) marks the
     results as ready.  Tokens go up, through the kernels and back in segments
-    of ``segment_tokens`` (0: 2048) on overlapping streams; the results equal
+    of ``segment_tokens`` (0: 2048; the last ones halved down to 256) on
+    overlapping streams; the results equal
     ``run`` on device copies to rounding.  The inputs must stay unmodified and
     alive until then, as with any non-blocking copy."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
