@@ -188,11 +188,11 @@ constexpr uint32_t TM_COLS = 128;  // columns 0-63: [K ; Q] K^T, then P'; 64-127
 // so eight consecutive rows put one float4 column on all 32 banks (the masks'
 // row-per-thread stores), and so do rows r, r + 4, r + 8, r + 12 (the solve's
 // four-row float4 loads); offsets stay compile-time immediates.
-__device__ __forceinline__ int sw(int r, int c) { return r * LDA + c; }
+__device__ __forceinline__ int ix(int r, int c) { return r * LDA + c; }
 
 // Blocked T = (I + A)^-1 for the 64 x 64 strictly lower A in sA; writes the
 // diagonal and lower 16 x 16 blocks of T into sT (the upper blocks are never
-// read).  Every matrix access goes through sw().
+// read).  Every matrix access goes through ix().
 __device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
     // diagonal blocks: warp b inverts I + A_bb by right-looking substitution,
@@ -206,10 +206,10 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
         for (int j = 0; j < 16; ++j) {
             const float xj = x[j];
 #pragma unroll
-            for (int r = j + 1; r < 16; ++r) x[r] -= sA[sw(b0 + r, b0 + j)] * xj;
+            for (int r = j + 1; r < 16; ++r) x[r] -= sA[ix(b0 + r, b0 + j)] * xj;
         }
 #pragma unroll
-        for (int r = 0; r < 16; ++r) sT[sw(b0 + r, b0 + lane)] = x[r];
+        for (int r = 0; r < 16; ++r) sT[ix(b0 + r, b0 + lane)] = x[r];
     }
     __syncthreads();
     // Off-diagonal blocks, one column block at a time: for i > j,
@@ -235,33 +235,33 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
             for (int k = j; k < i; ++k) {
 #pragma unroll
                 for (int s4 = 0; s4 < 16; s4 += 4) {
-                    const float t0 = sT[sw(16 * k + s4 + 0, col)], t1 = sT[sw(16 * k + s4 + 1, col)];
-                    const float t2 = sT[sw(16 * k + s4 + 2, col)], t3 = sT[sw(16 * k + s4 + 3, col)];
+                    const float t0 = sT[ix(16 * k + s4 + 0, col)], t1 = sT[ix(16 * k + s4 + 1, col)];
+                    const float t2 = sT[ix(16 * k + s4 + 2, col)], t3 = sT[ix(16 * k + s4 + 3, col)];
 #pragma unroll
                     for (int r = 0; r < 4; ++r) {
-                        const float4 x = *reinterpret_cast<const float4*>(sA + sw(16 * i + rq + r, 16 * k + s4));
+                        const float4 x = *reinterpret_cast<const float4*>(sA + ix(16 * i + rq + r, 16 * k + s4));
                         acc[r] = fmaf(x.x, t0, fmaf(x.y, t1, fmaf(x.z, t2, fmaf(x.w, t3, acc[r]))));
                     }
                 }
             }
 #pragma unroll
-            for (int r = 0; r < 4; ++r) sT[sw(16 * i + rq + r, col)] = acc[r];
+            for (int r = 0; r < 4; ++r) sT[ix(16 * i + rq + r, col)] = acc[r];
             __syncwarp();
             float xc[16];
 #pragma unroll
-            for (int s = 0; s < 16; ++s) xc[s] = sT[sw(16 * i + s, col)];
+            for (int s = 0; s < 16; ++s) xc[s] = sT[ix(16 * i + s, col)];
             __syncwarp();  // every lane holds its X column before T_ij replaces it
             float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int s4 = 0; s4 < 16; s4 += 4) {
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    const float4 y = *reinterpret_cast<const float4*>(sT + sw(16 * i + rq + r, 16 * i + s4));
+                    const float4 y = *reinterpret_cast<const float4*>(sT + ix(16 * i + rq + r, 16 * i + s4));
                     o[r] = fmaf(y.x, xc[s4], fmaf(y.y, xc[s4 + 1], fmaf(y.z, xc[s4 + 2], fmaf(y.w, xc[s4 + 3], o[r]))));
                 }
             }
 #pragma unroll
-            for (int r = 0; r < 4; ++r) sT[sw(16 * i + rq + r, col)] = -o[r];
+            for (int r = 0; r < 4; ++r) sT[ix(16 * i + rq + r, col)] = -o[r];
             __syncwarp();
         }
     }
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(NT, 4) gdn_prefill_chunk_prep_kernel(const Pre
             if (arow) {
 #pragma unroll
                 for (int e = 0; e < 16; e += 4)
-                    *reinterpret_cast<float4*>(sA + sw(i, c16 + e)) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
+                    *reinterpret_cast<float4*>(sA + ix(i, c16 + e)) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
             } else {
                 st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), r);
                 st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), r + 8);
@@ -481,8 +481,8 @@ __global__ void __launch_bounds__(NT, 4) gdn_prefill_chunk_prep_kernel(const Pre
             // blocks above the diagonal are zero and are never stored in sT
             float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             if (((h + c) >> 4) <= (i >> 4)) {
-                const float4 a = *reinterpret_cast<const float4*>(sT + sw(i, h + c));
-                const float4 b = *reinterpret_cast<const float4*>(sT + sw(i, h + c + 4));
+                const float4 a = *reinterpret_cast<const float4*>(sT + ix(i, h + c));
+                const float4 b = *reinterpret_cast<const float4*>(sT + ix(i, h + c + 4));
                 x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
                 x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
             }
