@@ -60,6 +60,18 @@ def test_host_prefill_edges(cuda_device, lens, seg, cu_dtype):
     _check(inputs.prefill_inputs(lens, 4, 8, seed=sum(lens) + seg, cu_dtype=cu_dtype), seg, cuda_device)
 
 
+@pytest.mark.parametrize("lens", [
+    [1000],            # segments 512 + 256 + 232: the last one ends mid-chunk
+    [2500],            # 2048 + 256 + 196
+    [700, 1300, 333],  # sequences cut by the shrinking tail segments
+])
+def test_host_prefill_tail_segments(cuda_device, lens):
+    """Default segments: the last 2048 tokens (or fewer) are halved down to
+    256-token pieces, so sequence boundaries and segment cuts fall at
+    uneven places; the results still equal the device-buffer call."""
+    _check(inputs.prefill_inputs(lens, seed=sum(lens)), 0, cuda_device)
+
+
 def test_host_prefill_tokens_outside_sequences(cuda_device):
     args = inputs.prefill_inputs([100, 50], 4, 8, seed=9)
     T = args[0].shape[0]
