@@ -37,6 +37,26 @@ def test_prefill_resume_equals_one_call(cuda_device, split):
     assert_state_close(s2.cpu(), s.cpu())
 
 
+def test_prefill_resume_past_32_bit_offsets(cuda_device):
+    """One sequence of 525,288 tokens: the output holds more than 2^31
+    elements (4.3 GB), the workspace more than 2^32 bytes and the prep grid
+    262,656 CTAs, so every offset must be 64-bit.  The last 4096 tokens of
+    the one call equal a resume of them from the state after the first
+    T - 4096 (an unaligned split, so the chunk boundaries differ)."""
+    T, tail = 524288 + 1000, 4096
+    args = inputs.prefill_inputs([T], seed=5, with_state=False, device=cuda_device)
+    o, s = gdn_prefill.run(*args)
+    o_tail = o[T - tail:].cpu()
+    del o
+    torch.cuda.empty_cache()
+    _, s1 = _run_range(args, 0, T - tail, None, cuda_device)
+    torch.cuda.empty_cache()
+    o2, s2 = _run_range(args, T - tail, T, s1, cuda_device)
+    torch.cuda.synchronize()
+    assert_output_close(o2.cpu(), o_tail)
+    assert_state_close(s2.cpu(), s.cpu())
+
+
 def test_prefill_chunked_and_token_serial_agree_full_size(cuda_device, monkeypatch):
     args = inputs.prefill_inputs([8192], seed=2, with_state=False, device=cuda_device)
     monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "0")
