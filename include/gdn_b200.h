@@ -247,7 +247,11 @@ size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV);
  * The first call on a device looks up the scratch array's device address
  * with that device current (the device of `stream` must be the current
  * device, as for every entry point here); make that first call before any
- * stream capture.  All calls share the one array and its contents carry over
+ * stream capture.  The address is kept for the life of the process: after a
+ * cudaDeviceReset() on a device, whose context held the array, this entry
+ * point must not be called on that device again.  Argument errors
+ * (GDN_ERR_INVALID, GDN_ERR_UNSUPPORTED) are reported before
+ * GDN_ERR_TOO_LARGE.  All calls share the one array and its contents carry over
  * from the previous call; the kernels overwrite every byte they read, so
  * nothing needs clearing, but calls whose work overlaps on the GPU (on
  * different streams, or different host threads) race on it and must be

@@ -24,6 +24,22 @@ extern "C" {
 int gdn_umma_selftest(const float *A, const float *B, float *D, int N, int K, int a_mn, int b_mn,
                       int fmt, void *stream);
 
+/* mode bits of gdn_umma_selftest_ex */
+#define GDN_SELFTEST_A_TMEM 1    /* A staged in tensor memory (TMEM-A MMA form); needs a_mn == 0 */
+#define GDN_SELFTEST_NO_ARRIVE 2 /* issue nothing: the kernel's bounded wait must run out */
+
+/*
+ * gdn_umma_selftest with a mode word and the budget of the kernel's one
+ * bounded wait in SM clock cycles (0 = the default, ~1 s).  With
+ * GDN_SELFTEST_NO_ARRIVE nothing ever arrives on the mbarrier the kernel
+ * waits for: the wait gives up after wait_cycles, the kernel records the
+ * timeout, frees its tensor memory and returns, D is left untouched and the
+ * call returns GDN_ERR_DEVICE; the context stays usable.  The unit's status
+ * word is cleared before every launch.
+ */
+int gdn_umma_selftest_ex(const float *A, const float *B, float *D, int N, int K, int a_mn, int b_mn,
+                         int fmt, int mode, long long wait_cycles, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

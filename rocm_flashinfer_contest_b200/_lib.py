@@ -48,6 +48,7 @@ SIGNATURES = {
     "gdn_mtp_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _vp, _vp, _vp, _vp, _f,
                          _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp]),
     "gdn_umma_selftest": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _vp]),
+    "gdn_umma_selftest_ex": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, ctypes.c_longlong, _vp]),
 }
 
 _lib = None

@@ -29,6 +29,29 @@ extern "C" size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV) {
     return gdn::prefill_workspace_bytes(N, T, H, HV);
 }
 
+namespace gdn {
+
+int prefill_check_args(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+                       const void* a, const float* dt_bias, const void* b, const void* cu_seqlens,
+                       int cu_seqlens_is_int64, int N, int T, int H, int HV, int K, int V, const void* out,
+                       const float* new_state) {
+    if (N < 0 || T < 0 || H <= 0 || HV <= 0) return GDN_ERR_INVALID;
+    if (cu_seqlens_is_int64 != 0 && cu_seqlens_is_int64 != 1) return GDN_ERR_INVALID;
+    if (K != kDim || V != kDim || HV % H != 0) return GDN_ERR_UNSUPPORTED;
+    if (N == 0 && T == 0) return GDN_OK;
+    if (!cu_seqlens || !A_log || !dt_bias) return GDN_ERR_INVALID;
+    if (N > 0 && !new_state) return GDN_ERR_INVALID;
+    if (T > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_INVALID;
+    if (!gdn_aligned(q, 16) || !gdn_aligned(k, 16) || !gdn_aligned(v, 16) || !gdn_aligned(out, 16) ||
+        (new_state && !gdn_aligned(new_state, 16)) || (state && !gdn_aligned(state, 16)) ||
+        !gdn_aligned(a, 2) || !gdn_aligned(b, 2) || !gdn_aligned(A_log, 4) || !gdn_aligned(dt_bias, 4) ||
+        !gdn_aligned(cu_seqlens, cu_seqlens_is_int64 ? 8 : 4))
+        return GDN_ERR_ALIGN;
+    return GDN_OK;
+}
+
+}  // namespace gdn
+
 static int prefill_impl(const void* q, const void* k, const void* v, const float* state,
                         const float* A_log, const void* a, const float* dt_bias, const void* b,
                         const void* cu_seqlens, int cu_seqlens_is_int64, int N, int T, float scale,
@@ -40,17 +63,9 @@ static int prefill_impl(const void* q, const void* k, const void* v, const float
     if (ckpt != nullptr && (ckpt_every <= 0 || ckpt_every % 64 != 0 || !ckpt_cu || ckpt_total < 0))
         return GDN_ERR_INVALID;
     if (ckpt != nullptr && (!gdn_aligned(ckpt, 16) || !gdn_aligned(ckpt_cu, 8))) return GDN_ERR_ALIGN;
-    if (cu_seqlens_is_int64 != 0 && cu_seqlens_is_int64 != 1) return GDN_ERR_INVALID;
-    if (K != gdn::kDim || V != gdn::kDim || HV % H != 0) return GDN_ERR_UNSUPPORTED;
-    if (N == 0 && T == 0) return GDN_OK;
-    if (!cu_seqlens || !A_log || !dt_bias) return GDN_ERR_INVALID;
-    if (N > 0 && !new_state) return GDN_ERR_INVALID;
-    if (T > 0 && (!q || !k || !v || !a || !b || !out)) return GDN_ERR_INVALID;
-    if (!gdn_aligned(q, 16) || !gdn_aligned(k, 16) || !gdn_aligned(v, 16) || !gdn_aligned(out, 16) || (new_state && !gdn_aligned(new_state, 16)) ||
-        (state && !gdn_aligned(state, 16)) || !gdn_aligned(v, 2) || !gdn_aligned(out, 2) ||
-        !gdn_aligned(a, 2) || !gdn_aligned(b, 2) || !gdn_aligned(A_log, 4) ||
-        !gdn_aligned(dt_bias, 4) || !gdn_aligned(cu_seqlens, cu_seqlens_is_int64 ? 8 : 4))
-        return GDN_ERR_ALIGN;
+    const int chk = gdn::prefill_check_args(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64,
+                                            N, T, H, HV, K, V, out, new_state);
+    if (chk != GDN_OK || (N == 0 && T == 0)) return chk;
     if (scale == 0.0f) scale = 1.0f / sqrtf((float)K);
 
     gdn::PrefillParams p;
@@ -88,7 +103,7 @@ static int prefill_impl(const void* q, const void* k, const void* v, const float
         const size_t need = gdn::prefill_workspace_bytes(N, T, H, HV);
         if (!workspace || workspace_bytes < need) return GDN_ERR_INVALID;
         if (!gdn_aligned(workspace, 16)) return GDN_ERR_ALIGN;
-        gdn::launch_prefill_chunk(p, workspace, st);
+        return gdn::launch_prefill_chunk(p, workspace, st);
     } else {
         gdn::launch_prefill_recurrent(p, st);
     }

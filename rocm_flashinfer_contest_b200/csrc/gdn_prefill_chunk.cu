@@ -51,6 +51,8 @@
 // Workspace slot of chunk j of sequence n: floor(cu[n] / 64) + n + j, which is
 // below floor(T / 64) + N for every chunk, so the workspace holds
 // (floor(T / 64) + N) * HV slots of kSlotBytes.
+#include <mutex>
+
 #include "gdn_prefill_common.cuh"
 #include "umma.cuh"
 
@@ -1342,22 +1344,53 @@ size_t prefill_workspace_bytes(int N, int T, int H, int HV) {
            ((size_t)HV * chunk::kSlotBytes + (size_t)H * (chunk::kTileKQ + chunk::kTileG));
 }
 
-void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st) {
-    static bool attr_set = false;
-    static int num_sms = 148;
-    if (!attr_set) {
-        cudaFuncSetAttribute(chunk::prep::gdn_prefill_chunk_prep_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::prep::SMEM_BYTES);
-        cudaFuncSetAttribute(chunk::chain::gdn_prefill_chunk_chain_kernel<64>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain::Cfg<64>::SMEM_BYTES);
-        cudaFuncSetAttribute(chunk::chain2::gdn_prefill_chunk_chain2_kernel,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain2::SMEM_BYTES);
-        int dev = 0, sms = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess &&
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0)
-            num_sms = sms;
-        attr_set = true;
-    }
+namespace {
+
+// Launch set-up of the chunked kernels, per device: the opt-in to more than
+// 48 KiB of dynamic shared memory is a property of the kernel in the context
+// of the device that is current when it is set, and the SM count steers the
+// choice of chain kernel.  Done once per device, with that device current,
+// under std::call_once (host threads may race on the first call).
+constexpr int kMaxDevices = 64;
+struct ChunkLaunchSetup {
+    std::once_flag once;
+    cudaError_t status = cudaErrorNotReady;
+    int num_sms = 0;
+};
+ChunkLaunchSetup g_setup[kMaxDevices];
+
+cudaError_t chunk_setup_current_device(int& num_sms) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    ChunkLaunchSetup& s = g_setup[dev];
+    std::call_once(s.once, [&]() {
+        cudaError_t r = cudaFuncSetAttribute(chunk::prep::gdn_prefill_chunk_prep_kernel,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)chunk::prep::SMEM_BYTES);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(chunk::chain::gdn_prefill_chunk_chain_kernel<64>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)chunk::chain::Cfg<64>::SMEM_BYTES);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(chunk::chain2::gdn_prefill_chunk_chain2_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain2::SMEM_BYTES);
+        int sms = 0;
+        if (r == cudaSuccess) r = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (r == cudaSuccess && sms <= 0) r = cudaErrorInvalidValue;
+        s.num_sms = sms;
+        s.status = r;
+    });
+    num_sms = s.num_sms;
+    return s.status;
+}
+
+}  // namespace
+
+int launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st) {
+    int num_sms = 0;
+    if (chunk_setup_current_device(num_sms) != cudaSuccess) return GDN_ERR_CUDA;
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     const long long slots = chunk::ws_slots(p.N, p.T);
     // one chain per (sequence, v-head, V tile): 32-wide tiles on the split
@@ -1376,6 +1409,7 @@ void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t 
         chunk::chain::gdn_prefill_chunk_chain_kernel<64><<<(unsigned)chains64, chunk::chain::NT,
                                                            chunk::chain::Cfg<64>::SMEM_BYTES, st>>>(p, ws);
     }
+    return gdn_launch_status();
 }
 
 }  // namespace gdn

@@ -70,8 +70,16 @@ __device__ __forceinline__ void zero_uncovered_outputs(const PrefillParams& p, i
         for (long long t = t1; t < p.T; ++t) p.out[((size_t)t * p.HV + hv) * kDim + row] = z;
 }
 
+// Argument checks shared by the prefill entry points (sizes, null pointers,
+// alignment; no CUDA call): GDN_OK or the status to return.
+int prefill_check_args(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+                       const void* a, const float* dt_bias, const void* b, const void* cu_seqlens,
+                       int cu_seqlens_is_int64, int N, int T, int H, int HV, int K, int V, const void* out,
+                       const float* new_state);
 void launch_prefill_recurrent(const PrefillParams& p, cudaStream_t st);
-void launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st);
+// Launches the chunked kernels (prep, then a chain kernel); returns a GDN_*
+// status (GDN_ERR_CUDA when the per-device launch set-up or a launch fails).
+int launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st);
 size_t prefill_workspace_bytes(int N, int T, int H, int HV);
 
 }  // namespace gdn

@@ -28,7 +28,9 @@ std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
 // Device address of g_prefill_scratch on the current device, looked up on the
-// first call made with that device current and cached afterwards.
+// first call made with that device current and cached afterwards.  A
+// cudaDeviceReset() tears down the context that holds the array, so the
+// cached address is stale afterwards: the header says so.
 int scratch_on_current_device(void** out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return GDN_ERR_CUDA;
@@ -50,9 +52,13 @@ extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void*
                                        const void* b, const void* cu_seqlens, int cu_seqlens_is_int64,
                                        int N, int T, float scale, int H, int HV, int K, int V, void* out,
                                        float* new_state, void* stream) {
-    // the size check comes first and makes no CUDA call
-    if (N >= 0 && T >= 0 && H > 0 && HV > 0 && gdn_prefill_workspace_bytes(N, T, H, HV) > kScratchBytes)
-        return GDN_ERR_TOO_LARGE;
+    // argument errors rank before the size check, as for every other prefill
+    // entry point; neither makes a CUDA call
+    const int chk = gdn::prefill_check_args(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64,
+                                            N, T, H, HV, K, V, out, new_state);
+    if (chk != GDN_OK) return chk;
+    if (gdn_prefill_workspace_bytes(N, T, H, HV) > kScratchBytes) return GDN_ERR_TOO_LARGE;
+    if (N == 0 && T == 0) return GDN_OK;
     void* scratch = nullptr;
     const int st = scratch_on_current_device(&scratch);
     if (st != GDN_OK) return st;

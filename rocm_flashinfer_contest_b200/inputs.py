@@ -51,6 +51,41 @@ def decode_inputs(B: int, H: int = 16, HV: int = 32, K: int = D, V: int = D, see
     return [q, k, v, state, A_log, a, dt_bias, b, 1.0 / math.sqrt(K)]
 
 
+def decode_inputs_for(seq_ids, H: int = 16, HV: int = 32, K: int = D, V: int = D, seed: int = 0,
+                      device="cpu", state_std: float = 0.1):
+    """Decode arguments for the sequences `seq_ids` of one large batch in which
+    sequence i is drawn from its own generator (seed, i): any subset, e.g. a
+    rank's shard, is materialised alone and equals the same rows of the whole
+    batch.  A_log and dt_bias come from the generator `seed`."""
+    g = _gen(seed, device)
+    A_log = _uniform((HV,), 0.0, math.log(16.0), g, device)
+    dt_bias = _uniform((HV,), -1.0, 1.0, g, device)
+    rows = []
+    for i in seq_ids:
+        gi = _gen(seed * 1_000_003 + 7 * int(i) + 1, device)
+        rows.append((_l2norm_bf16(_normal((1, 1, H, K), gi, device)),
+                     _l2norm_bf16(_normal((1, 1, H, K), gi, device)),
+                     _normal((1, 1, HV, V), gi, device).to(torch.bfloat16),
+                     _normal((1, HV, V, K), gi, device, state_std),
+                     _normal((1, 1, HV), gi, device).to(torch.bfloat16),
+                     _normal((1, 1, HV), gi, device).to(torch.bfloat16)))
+    cat = [torch.cat([r[j] for r in rows]) if rows else None for j in range(6)]
+    q, k, v, state, a, b = cat
+    return [q, k, v, state, A_log, a, dt_bias, b, 1.0 / math.sqrt(K)]
+
+
+def seqlens_split(total: int, num_seqs: int, seed: int):
+    """`num_seqs` positive lengths summing to `total` (seeded uniform cut
+    points): stands in for a contest workload of which only the total length
+    and the sequence count are published."""
+    if num_seqs <= 0 or total < num_seqs:
+        raise ValueError("need total >= num_seqs > 0")
+    g = _gen(seed + 104729, "cpu")
+    cuts = sorted(torch.randperm(total - 1, generator=g)[:num_seqs - 1].add(1).tolist())
+    bounds = [0] + cuts + [total]
+    return [bounds[i + 1] - bounds[i] for i in range(num_seqs)]
+
+
 def seqlens_uniform(num_seqs: int, lo: int, hi: int, seed: int, max_total: int | None = None):
     """Sequence lengths drawn uniformly from [lo, hi] (seeded); if max_total is
     given, lengths are scaled down so the total stays within it."""

@@ -162,3 +162,67 @@ def gather_prefill(shards, outs, cu, HV: int, V: int = 128, K: int = 128):
             s[seq, h0:h1] = ss[j].cpu()
             pos += n
     return o, s
+
+
+# ---------------------------------------------------------------------------
+# host-side failure handling: per-rank deadline, re-run of failed shards
+
+@dataclass(frozen=True)
+class ShardFailure:
+    rank: int
+    kind: str       # "raised" (the rank's work raised) or "timeout" (no result by the deadline)
+    detail: str
+
+
+def run_shards(work, shards, rank: int, world: int, store, timeout_s: float, poll_s: float = 0.02,
+               prefix: str = "gdn_shards"):
+    """Runs ``work(shard)`` for this rank's shard and reports through ``store``
+    (a torch.distributed Store shared by the ranks, e.g. the process group's
+    TCPStore; no collective is used, so a rank that hangs or dies cannot
+    block the others).
+
+    Every rank publishes its result (pickled) or the error it raised.  Rank 0
+    waits until ``timeout_s`` after it has finished its own shard for the
+    others, then re-runs every shard whose rank raised or missed the deadline
+    itself (a surviving rank, which here holds the full inputs), and returns
+    ``(results, failures)``: the per-shard results in rank order and a list of
+    ShardFailure.  Other ranks return None once they have published.  Work
+    inside a rank stays between kernel launches: a failure is detected on the
+    host, never by stalling a GPU kernel."""
+    import pickle
+    import time
+
+    key = lambda r, what: f"{prefix}/{r}/{what}"  # noqa: E731
+    try:
+        mine = work(shards[rank])
+        store.set(key(rank, "ok"), pickle.dumps(mine))
+    except Exception as e:  # noqa: BLE001 - any failure of the work is reported, not raised
+        mine = None
+        store.set(key(rank, "err"), repr(e)[:500])
+        if rank != 0:
+            return None
+    if rank != 0:
+        return None
+    results = [None] * world
+    failures = []
+    pending = set(range(1, world))
+    if mine is None:
+        failures.append(ShardFailure(0, "raised", store.get(key(0, "err")).decode()))
+    else:
+        results[0] = mine
+    deadline = time.monotonic() + timeout_s
+    while pending and time.monotonic() < deadline:
+        for r in sorted(pending):
+            if store.check([key(r, "ok")]):
+                results[r] = pickle.loads(store.get(key(r, "ok")))
+                pending.discard(r)
+            elif store.check([key(r, "err")]):
+                failures.append(ShardFailure(r, "raised", store.get(key(r, "err")).decode()))
+                pending.discard(r)
+        if pending:
+            time.sleep(poll_s)
+    for r in sorted(pending):
+        failures.append(ShardFailure(r, "timeout", f"no result within {timeout_s:.1f} s"))
+    for f in failures:  # re-run each failed shard here, on a surviving rank
+        results[f.rank] = work(shards[f.rank])
+    return results, sorted(failures, key=lambda f: f.rank)

@@ -136,6 +136,33 @@ def test_prefill_rejects_bad_arguments(over, code):
     assert _prefill(**over) == code
 
 
+def _prefill_noalloc(**over):
+    d = dict(q=16, k=16, v=16, state=16, A_log=16, a=16, dt_bias=16, b=16, cu=16, cu64=1,
+             N=1, T=4096, scale=0.0, H=16, HV=32, K=128, V=128, out=16, new_state=16, stream=None)
+    d.update(over)
+    return _lib.lib().gdn_prefill_fwd_noalloc(*d.values())
+
+
+@pytest.mark.parametrize("over,code", [
+    # argument errors come before the scratch-size check (these sizes are too large)
+    (dict(K=64), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(V=96), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(H=5, HV=32), _lib.GDN_ERR_UNSUPPORTED),
+    (dict(N=-1), _lib.GDN_ERR_INVALID),
+    (dict(H=0), _lib.GDN_ERR_INVALID),
+    (dict(cu64=2), _lib.GDN_ERR_INVALID),
+    (dict(cu=None), _lib.GDN_ERR_INVALID),
+    (dict(q=None), _lib.GDN_ERR_INVALID),
+    (dict(new_state=None), _lib.GDN_ERR_INVALID),
+    (dict(q=24), _lib.GDN_ERR_ALIGN),
+    (dict(cu=20, cu64=1), _lib.GDN_ERR_ALIGN),
+    (dict(), _lib.GDN_ERR_TOO_LARGE),                     # 65 slots x (32 x 17,424 + 16 x 49,152) B
+    (dict(N=0, T=0), _lib.GDN_OK),                       # nothing to do: no CUDA call
+])
+def test_prefill_noalloc_rejects_bad_arguments(over, code):
+    assert _prefill_noalloc(**over) == code
+
+
 def _mtp(**over):
     d = dict(q=16, k=16, v=16, pool_in=4096, pool_out=4096, bf16=0, idx=16, out_idx=None, idx64=0,
              A_log=16, a=16, dt_bias=16, b=16, scale=0.0, B=2, T=3, H=1, HV=2, K=128, V=128, pool=4,
@@ -274,3 +301,12 @@ def test_error_is_raised_as_exception():
     with pytest.raises(_lib.GDNError) as ei:
         _lib.check("gdn_decode_fwd", _decode(K=64))
     assert ei.value.status == _lib.GDN_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("mode,wait,a_mn,code", [
+    (4, 0, 0, _lib.GDN_ERR_INVALID),        # unknown mode bit
+    (2, -1, 0, _lib.GDN_ERR_INVALID),       # negative wait budget
+    (1, 0, 1, _lib.GDN_ERR_UNSUPPORTED),    # a TMEM-resident A is K-major
+])
+def test_selftest_ex_rejects_bad_arguments(mode, wait, a_mn, code):
+    assert _lib.lib().gdn_umma_selftest_ex(16, 16, 16, 64, 64, a_mn, 0, 0, mode, wait, None) == code

@@ -74,10 +74,17 @@ def test_prefill_config3_varlen_16(cuda_device, path):
     _check(args, cuda_device)
 
 
+def test_prefill_config2_8k(cuda_device, path):
+    """Benchmark config 2: one 8192-token sequence, zero initial state, all
+    16 q/k heads (32 v-heads) checked against the oracle."""
+    args = inputs.prefill_inputs([8192], seed=2, with_state=False)
+    _check(args, cuda_device)
+
+
 @pytest.mark.parametrize("j", [0, 11])
-def test_prefill_config2_8k(cuda_device, path, j):
-    """Benchmark config 2: one 8192-token sequence, zero initial state (the
-    oracle checks two v-heads of q/k head j; all heads run on the GPU)."""
+def test_prefill_config2_8k_head_subset(cuda_device, path, j):
+    """The oracle restricted to the v-heads of q/k head j (its inputs sliced)
+    agrees with the same heads of the full GPU run: heads are independent."""
     args = inputs.prefill_inputs([8192], seed=2, with_state=False)
     _check(args, cuda_device, head_subset=j)
 
