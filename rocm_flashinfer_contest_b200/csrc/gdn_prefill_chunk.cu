@@ -24,33 +24,39 @@
 // the decay.  Tokens past the end of the sequence get k = q = v = beta = 0 and
 // log g = 0, which leaves every formula exact for a partial last chunk.
 //
-// Two kernels:
+// A prep kernel and one of two chain kernels:
 //  * prep  (one CTA per (chunk, v-head), all chunks of all sequences at once):
 //      the state-independent part — gates, gamma, MMA [K ; Q] K^T (bf16 as
 //      given), the decay masks, T = (I + A)^-1 by a blocked solve on the CUDA
 //      cores in fp32, and P' = P T on the tensor cores — and writes the f16
 //      operand tile [T ; P'] (already in its shared-memory swizzled layout)
-//      and the chunk's gate factors into a workspace slot.
-//  * chain (one CTA per (sequence, v-head, 64-wide V tile), 8 warps): walks
-//      the chunks in order with the state resident in TMEM (fp32):
+//      and the chunk's gate factors into a workspace slot; per q/k head it
+//      also publishes the chunk's f16 [K ; Q] tile and the cross-Gram tile
+//      G_j = [K ; Q]_j K_{j-1}^T.
+//  * a chain walks the chunks of a (sequence, v-head) in order:
 //        MMA_1 : [K ; Q] x S     -> KS (rows 0-63: Y = beta (V - e^gamma KS)), QS (rows 64-127)
 //        MMA_2 : [T ; P'] x Y    -> Delta (rows 0-63), P'Y (rows 64-127);
 //                                   O = scale e^gamma QS + P'Y
 //        MMA_3 : K^T x Delta~ with Delta~ = diag(e^{gamma_C - gamma}) Delta,
 //                S = e^{gamma_C} S + K^T Delta~  (= K~^T Delta)
-//      The diagonal scalings of Q and K are applied to rows of the products
-//      instead of to the operands, so [K ; Q] is a plain f16 copy of the
-//      input rows; and since the K rows of that K-major tile have exactly the
-//      bytes of an MN-major K^T tile whose two 64-wide blocks sit 16 KiB
-//      apart, MMA_3 reads K^T from the same tile.  The next chunk's rows and
-//      workspace slot stream in with cp.async and are converted while MMA_3
-//      of the current chunk runs.
+//      with MMA_1 of the next chunk split as [K ; Q]_{j+1} (e^{gamma_C} S_j)
+//      (issued early) plus G_{j+1} Delta~_j, so two tensor-core round trips
+//      remain on the critical path.  The diagonal scalings of Q and K act on
+//      rows of the products, so [K ; Q] is a plain f16 copy of the input rows,
+//      and its K rows are byte for byte an MN-major K^T tile, which MMA_3
+//      reads in place.  chain2 splits a head's V columns over four CTAs
+//      (32-wide tiles; for few, long sequences); chain3 keeps a whole head in
+//      one CTA, transposed so the state-side operands live in tensor memory
+//      (for batches of sequences).
 // Operands are f16 except in the prep MMA (bf16 inputs as given); every
 // accumulation is fp32 and the state carried between chunks is fp32.
 //
 // Workspace slot of chunk j of sequence n: floor(cu[n] / 64) + n + j, which is
 // below floor(T / 64) + N for every chunk, so the workspace holds
 // (floor(T / 64) + N) * HV slots of kSlotBytes.
+#include <cuda.h>
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "gdn_prefill_common.cuh"
@@ -279,7 +285,8 @@ constexpr bool t_rows_are_mn_major() {
 }
 static_assert(t_rows_are_mn_major(), "T rows of the [T ; P] tile double as the MN-major B operand");
 
-__global__ void __launch_bounds__(NT, 4) gdn_prefill_chunk_prep_kernel(const PrefillParams p, unsigned char* ws) {
+__global__ void __launch_bounds__(NT, 4) gdn_prefill_chunk_prep_kernel(const PrefillParams p, unsigned char* ws,
+                                                                      long long slot_base) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -287,7 +294,7 @@ __global__ void __launch_bounds__(NT, 4) gdn_prefill_chunk_prep_kernel(const Pre
     __shared__ uint32_t tmem_base_sh;
 
     const int tid = threadIdx.x, warp = tid >> 5;
-    const long long s = blockIdx.x / p.HV;
+    const long long s = slot_base + blockIdx.x / p.HV;
     const int hv = blockIdx.x % p.HV, hq = hv / p.rep;
 
     // locate the chunk: the largest n with floor(cu[n] / 64) + n <= s, then j
@@ -549,335 +556,6 @@ done:
 }
 
 }  // namespace prep
-
-// ============================================================================
-// chain kernel
-// ============================================================================
-namespace chain {
-
-constexpr int NT = 256;  // 8 warps: TMEM lane quarter = warp % 4, column half = warp / 4
-constexpr int NBUF = 3;  // data of chunk j lives in buffer j % 3
-constexpr uint32_t TM_1 = 0, TM_2 = 64, TM_3 = 128, TM_S = 192, TM_COLS = 256;
-constexpr int kLowerBarrier = 1;  // named barrier of the four warps on TMEM lanes 0-63
-
-// VT state columns (v) per CTA: 64, or 32 when a 64-wide split would leave
-// SMs idle (few sequences x v-heads).  The B operands S, Y and Delta~ have
-// N = VT and are MN-major: 128-byte swizzle for 64 columns, 64-byte for 32.
-template <int VT>
-struct Cfg {
-    static constexpr int HALF = VT / 2;                     // columns per thread
-    static constexpr uint32_t VROW = VT * 2 + 16;           // raw v row stride (padded)
-    static constexpr uint32_t S_BYTES = VT * kDim * 2;      // S f16 tile
-    static constexpr uint32_t YD_BYTES = VT * C * 2;        // Y / Delta~ f16 tiles
-    static constexpr uint32_t OFF_KQ = 0;                         // [K ; Q] (workspace copy), 3 bufs
-    static constexpr uint32_t OFF_TP = OFF_KQ + NBUF * kTileKQ;   // [T ; P'] (workspace copy), 3 bufs
-    static constexpr uint32_t OFF_SH = OFF_TP + NBUF * kTileTP;   // S, MN-major (v x k)
-    static constexpr uint32_t OFF_Y = OFF_SH + S_BYTES;           // Y, MN-major (v x token)
-    static constexpr uint32_t OFF_DL = OFF_Y + YD_BYTES;          // Delta~, MN-major (v x token)
-    static constexpr uint32_t OFF_RV = OFF_DL + YD_BYTES;         // v rows bf16 [3][64][VROW]
-    static constexpr uint32_t OFF_GB = OFF_RV + NBUF * C * VROW;  // gate records, 3 bufs
-    static constexpr uint32_t SMEM_BYTES = OFF_GB + NBUF * kGateBytes + 1024;
-    static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
-    static_assert(OFF_Y % 1024 == 0 && OFF_DL % 1024 == 0 && OFF_RV % 16 == 0, "tile alignment");
-
-    // byte offset of element (v, k) of an MN-major B tile whose K extent is kext
-    static __device__ __forceinline__ uint32_t b_off(uint32_t v, uint32_t k, uint32_t kext) {
-        if constexpr (VT == 32) return umma::mnmaj64_off(v, k);
-        else return umma::mnmaj_off(v, k, kext);
-    }
-    static __device__ __forceinline__ uint64_t b_desc(uint32_t tile, uint32_t kext, uint32_t k0) {
-        if constexpr (VT == 32) return umma::desc_mnmaj64(tile, k0);
-        else return umma::desc_mnmaj(tile, kext, k0);
-    }
-    // byte offset of the K step at k0 from the descriptor b_desc(tile, kext, 0)
-    static __host__ __device__ constexpr uint32_t b_koff(uint32_t k0) {
-        return VT == 32 ? umma::koff_mnmaj64(k0) : umma::koff_mnmaj(k0);
-    }
-    static __device__ __forceinline__ void ld(uint32_t taddr, float (&v)[HALF]) {
-        if constexpr (HALF == 16) umma::tmem_ld16(taddr, v);
-        else umma::tmem_ld32(taddr, v);
-    }
-    static __device__ __forceinline__ void ld2(uint32_t ta, uint32_t tb, float (&va)[HALF], float (&vb)[HALF]) {
-        if constexpr (HALF == 16) umma::tmem_ld16x2(ta, tb, va, vb);
-        else umma::tmem_ld32x2(ta, tb, va, vb);
-    }
-    static __device__ __forceinline__ void st(uint32_t taddr, const float (&v)[HALF]) {
-        if constexpr (HALF == 16) umma::tmem_st16(taddr, v);
-        else umma::tmem_st32(taddr, v);
-    }
-};
-
-__device__ __forceinline__ void lower_sync() {
-    asm volatile("bar.sync %0, %1;" ::"r"(kLowerBarrier), "r"(128) : "memory");
-}
-
-// Copies of chunk [tc, tc + len) (workspace slot `slot`) into buffer `buf`:
-// the loader warp starts three bulk copies of the [K ; Q] and [T ; P'] tiles
-// and the gates, completing on `bar`; every thread copies its share of the v
-// rows with cp.async (rows past len zero-filled) as one commit group.
-template <int VT>
-__device__ __forceinline__ void issue_loads(const PrefillParams& p, const unsigned char* ws, unsigned char* sm,
-                                            uint64_t* bar, int buf, long long tc, int len, long long slot,
-                                            int hq, int hv, int v0, int tid, bool loader) {
-    if (loader) {
-        const int lane = tid & 31;
-        using G = Cfg<VT>;
-        if (lane == 0) umma::mbar_arrive_expect_tx(bar, kTileKQ + kTileTP + kGateBytes);
-        __syncwarp();
-        const unsigned char* rec = ws + ((size_t)slot * p.HV + hv) * kSlotBytes;
-        const unsigned char* kq = ws_kq(p, ws) + ((size_t)slot * p.H + hq) * kTileKQ;
-        if (lane == 0) umma::bulk_g2s(umma::smem_u32(sm + G::OFF_KQ + buf * kTileKQ), kq, kTileKQ / 2, bar);
-        if (lane == 1)
-            umma::bulk_g2s(umma::smem_u32(sm + G::OFF_KQ + buf * kTileKQ + kTileKQ / 2), kq + kTileKQ / 2,
-                           kTileKQ / 2, bar);
-        if (lane == 2) umma::bulk_g2s(umma::smem_u32(sm + G::OFF_TP + buf * kTileTP), rec, kTileTP, bar);
-        if (lane == 3)
-            umma::bulk_g2s(umma::smem_u32(sm + G::OFF_GB + buf * kGateBytes), rec + kTileTP, kGateBytes, bar);
-    }
-    constexpr uint32_t VROW = Cfg<VT>::VROW;
-    const uint32_t rv = umma::smem_u32(sm + Cfg<VT>::OFF_RV) + buf * (C * VROW);
-#pragma unroll
-    for (int it = 0; it < C * (VT / 8) / NT; ++it) {
-        const int idx = tid + it * NT, r = idx / (VT / 8), c = idx % (VT / 8);
-        const bool ok = r < len;
-        const size_t off = ok ? ((size_t)(tc + r) * p.HV + hv) * kDim + v0 + c * 8 : 0;
-        cp_async16(rv + r * VROW + c * 16, p.v + off, ok);
-    }
-    cp_async_commit();
-}
-
-template <int VT>
-__global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain_kernel(const PrefillParams p,
-                                                                        const unsigned char* ws) {
-    using G = Cfg<VT>;
-    constexpr int HALF = G::HALF;
-    constexpr uint32_t VROW = G::VROW;
-    constexpr uint32_t OFF_KQ = G::OFF_KQ, OFF_TP = G::OFF_TP, OFF_SH = G::OFF_SH, OFF_Y = G::OFF_Y;
-    constexpr uint32_t OFF_DL = G::OFF_DL, OFF_RV = G::OFF_RV, OFF_GB = G::OFF_GB;
-    extern __shared__ unsigned char smem_raw[];
-    unsigned char* sm = reinterpret_cast<unsigned char*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t mbar[3];   // MMA_1, MMA_2, MMA_3 completion
-    __shared__ uint64_t ldbar[NBUF];  // chunk data of buffer 0 / 1 / 2 landed
-    __shared__ uint32_t tmem_base_sh;
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quarter = warp & 3, half = warp >> 2;
-    const bool lower = quarter < 2;       // TMEM lanes 0-63: the K rows (Y, Delta~)
-    const int row = 32 * quarter + lane;  // TMEM lane owned by this thread
-    const int vt = blockIdx.x % (kDim / VT);
-    const long long nh = blockIdx.x / (kDim / VT);
-    const int hv = (int)(nh % p.HV), n = (int)(nh / p.HV);
-    const int hq = hv / p.rep;
-    const int v0 = vt * VT;
-    const int cb = HALF * half;  // this thread's first column within the tile
-    constexpr int kLoader = 2;   // warp issuing the bulk copies
-
-    long long t0, t1;
-    seq_bounds(p, n, t0, t1);
-    if (tid < VT) zero_uncovered_outputs(p, n, t0, t1, hv, v0 + tid, true);
-    const size_t state_off = ((size_t)nh * kDim + v0) * kDim;  // [n][hv][v0][0]
-    if (t1 == t0) {  // empty sequence: the final state stays zero
-        for (int idx = tid; idx < VT * kDim / 4; idx += NT)
-            reinterpret_cast<float4*>(p.new_state + state_off)[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
-        return;
-    }
-    const long long slot0 = t0 / C + n;
-    const long long nchunks = (t1 - t0 + C - 1) / C;
-    auto chunk_len = [&](long long j) { const long long r = t1 - t0 - C * j; return (int)(r < C ? r : C); };
-
-    if (warp == 0) {
-        umma::tmem_alloc(&tmem_base_sh, TM_COLS);
-        umma::tmem_relinquish();
-    }
-    if (tid == 0) {
-#pragma unroll
-        for (int b = 0; b < 3; ++b) umma::mbar_init(&mbar[b], 1);
-#pragma unroll
-        for (int b = 0; b < NBUF; ++b) umma::mbar_init(&ldbar[b], 1);
-        umma::fence_mbar_init();
-    }
-    __syncthreads();
-    issue_loads<VT>(p, ws, sm, &ldbar[0], 0, t0, chunk_len(0), slot0, hq, hv, v0, tid, warp == kLoader);
-    if (nchunks > 1)
-        issue_loads<VT>(p, ws, sm, &ldbar[1], 1, t0 + C, chunk_len(1), slot0 + 1, hq, hv, v0, tid, warp == kLoader);
-    umma::fence_after_sync();
-    const uint32_t tmem = tmem_base_sh;
-    const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);  // this warp's lane quarter
-
-    // initial state: S[k = row][v] for this thread's 32 columns -> TMEM (fp32) and f16 operand
-    {
-        float sv[HALF];
-#pragma unroll
-        for (int e = 0; e < HALF; ++e) sv[e] = p.state ? p.state[state_off + (size_t)(cb + e) * kDim + row] : 0.f;
-        G::st(tl + TM_S + cb, sv);
-#pragma unroll
-        for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, G::b_off(cb + c8, row, kDim), sv + c8);
-    }
-    // chunk 0's v rows (copied by all threads) become visible at the barrier
-    if (nchunks > 1) cp_async_wait_n<1>(); else cp_async_wait_n<0>();
-    sync_for_mma();
-    bool failed = false;
-
-    const uint32_t sKQ0 = umma::smem_u32(sm + OFF_KQ), sTP0 = umma::smem_u32(sm + OFF_TP);
-    const uint32_t sSH = umma::smem_u32(sm + OFF_SH), sY = umma::smem_u32(sm + OFF_Y);
-    const uint32_t sDL = umma::smem_u32(sm + OFF_DL);
-    constexpr uint32_t ID_S = umma::idesc_f16(128, VT, 0, 0, 0, 1);  // [K;Q] x S (MN-major B)
-    constexpr uint32_t ID_Y = umma::idesc_f16(128, VT, 0, 0, 0, 1);  // [T;P'] x Y (MN-major B)
-    constexpr uint32_t ID_D = umma::idesc_f16(128, VT, 0, 0, 1, 1);  // K^T x Delta~ (both MN-major)
-    // operand descriptors, built once; every K step and buffer is a constant offset
-    const uint64_t dKQ0 = umma::desc_kmaj(sKQ0, 128, 0), dKT0 = umma::desc_sw128(sKQ0, 16384u, 1024u);
-    const uint64_t dTP0 = umma::desc_kmaj(sTP0, 128, 0);
-    const uint64_t dSH = G::b_desc(sSH, kDim, 0), dY = G::b_desc(sY, C, 0), dDL = G::b_desc(sDL, C, 0);
-
-    for (long long j = 0; j < nchunks; ++j) {
-        const int b = (int)(j % NBUF);
-        const uint32_t par = (uint32_t)(j & 1), lpar = (uint32_t)((j / NBUF) & 1);
-        const long long tc = t0 + C * j;
-        const int len = chunk_len(j);
-        wait_local(&ldbar[b], lpar, failed);
-        const float* gr = reinterpret_cast<const float*>(sm + OFF_GB + b * kGateBytes);
-
-        // ---- MMA_1: [K ; Q] S ----
-        if (tid == 0) {
-            umma::fence_after_sync();
-#pragma unroll
-            for (int k0 = 0; k0 < kDim; k0 += 16)
-                umma::mma_f16(tmem + TM_1, umma::desc_add(dKQ0, b * kTileKQ + umma::koff_kmaj(128, k0)),
-                              umma::desc_add(dSH, G::b_koff(k0)), ID_S, k0 > 0);
-            umma::mma_commit(&mbar[0]);
-        }
-        // while MMA_1 runs: stream in chunk j + 2 (its buffer was chunk j - 1's)
-        if (j + 2 < nchunks)
-            issue_loads<VT>(p, ws, sm, &ldbar[(j + 2) % NBUF], (int)((j + 2) % NBUF), tc + 2 * C, chunk_len(j + 2),
-                        slot0 + j + 2, hq, hv, v0, tid, warp == kLoader);
-        wait_local(&mbar[0], par, failed);
-        umma::fence_after_sync();
-
-        // ---- lower: Y = beta (V - e^gamma KS) -> MMA_2;  upper: keep QS ----
-        float qs[HALF];
-        {
-            float d[HALF];
-            G::ld(tl + TM_1 + cb, d);
-            if (lower) {
-                const int i = row;
-                const bool live = i < len;
-                const float beg = gr[GR_BEG + i], b_i = gr[GR_BETA + i];
-                const unsigned char* vrow = sm + OFF_RV + b * (C * VROW) + i * VROW + cb * 2;
-#pragma unroll
-                for (int c8 = 0; c8 < HALF; c8 += 8) {
-                    float vv[8], y[8];
-                    unpack_bf16x8(*reinterpret_cast<const uint4*>(vrow + c8 * 2), vv);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) y[e] = live ? fmaf(-beg, d[c8 + e], b_i * vv[e]) : 0.f;
-                    st_f16x8(sm + OFF_Y, G::b_off(cb + c8, i, C), y);
-                }
-                umma::fence_proxy_async_smem();
-                umma::fence_before_sync();
-                lower_sync();
-                if (tid == 0) {
-                    umma::fence_after_sync();
-#pragma unroll
-                    for (int k0 = 0; k0 < C; k0 += 16)
-                        umma::mma_f16(tmem + TM_2, umma::desc_add(dTP0, b * kTileTP + umma::koff_kmaj(128, k0)),
-                                      umma::desc_add(dY, G::b_koff(k0)), ID_Y, k0 > 0);
-                    umma::mma_commit(&mbar[1]);
-                }
-            } else {
-#pragma unroll
-                for (int e = 0; e < HALF; ++e) qs[e] = d[e];
-            }
-        }
-        wait_local(&mbar[1], par, failed);
-        umma::fence_after_sync();
-
-        // ---- lower: Delta~ = e^{gamma_C - gamma} Delta -> MMA_3;  upper: outputs ----
-        {
-            float d[HALF];
-            G::ld(tl + TM_2 + cb, d);
-            if (lower) {
-                const float fk = gr[GR_FK + row];
-#pragma unroll
-                for (int e = 0; e < HALF; ++e) d[e] *= fk;
-#pragma unroll
-                for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_DL, G::b_off(cb + c8, row, C), d + c8);
-                umma::fence_proxy_async_smem();
-                umma::fence_before_sync();
-                lower_sync();
-                if (tid == 0) {
-                    // K^T read as MN-major from the [K ; Q] tile: its two 64-wide k
-                    // blocks are the tile's 16 KiB slabs
-                    umma::fence_after_sync();
-#pragma unroll
-                    for (int k0 = 0; k0 < C; k0 += 16)
-                        umma::mma_f16(tmem + TM_3, umma::desc_add(dKT0, b * kTileKQ + umma::koff_mnmaj(k0)),
-                                      umma::desc_add(dDL, G::b_koff(k0)), ID_D, k0 > 0);
-                    umma::mma_commit(&mbar[2]);
-                }
-            } else {
-                const int i = row - 64;
-                if (i < len) {
-                    const float fq = gr[GR_FQ + i];  // scale e^{gamma_i}
-                    __nv_bfloat16* op = p.out + ((size_t)(tc + i) * p.HV + hv) * kDim + v0 + cb;
-#pragma unroll
-                    for (int c8 = 0; c8 < HALF; c8 += 8) {
-                        __nv_bfloat162 o[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            o[e] = __floats2bfloat162_rn(fmaf(fq, qs[c8 + 2 * e], d[c8 + 2 * e]),
-                                                         fmaf(fq, qs[c8 + 2 * e + 1], d[c8 + 2 * e + 1]));
-                        *reinterpret_cast<uint4*>(op + c8) = *reinterpret_cast<uint4*>(o);
-                    }
-                }
-            }
-        }
-        wait_local(&mbar[2], par, failed);
-        umma::fence_after_sync();
-
-        // ---- S = e^{gamma_C} S + K^T Delta~ (TMEM, fp32) and its f16 operand copy ----
-        {
-            const float decay = gr[GR_DECAY];
-            float sv[HALF], d[HALF];
-            G::ld2(tl + TM_S + cb, tl + TM_3 + cb, sv, d);
-#pragma unroll
-            for (int e = 0; e < HALF; ++e) sv[e] = fmaf(decay, sv[e], d[e]);
-            G::st(tl + TM_S + cb, sv);
-#pragma unroll
-            for (int c8 = 0; c8 < HALF; c8 += 8) st_f16x8(sm + OFF_SH, G::b_off(cb + c8, row, kDim), sv + c8);
-            // checkpoint: a full chunk that ends on a multiple of ckpt_every
-            if (p.ckpt != nullptr && len == C && (C * (j + 1)) % p.ckpt_every == 0) {
-                float* cd = ckpt_dst(p, n, hv, C * (j + 1));
-                if (cd != nullptr) {
-#pragma unroll
-                    for (int e = 0; e < HALF; ++e) __stcs(cd + (size_t)(v0 + cb + e) * kDim + row, sv[e]);
-                }
-            }
-        }
-        // the next chunk's v rows (copied by all threads) become visible at this barrier;
-        // the CTA stops here if any wait of this chunk timed out
-        if (j + 2 < nchunks) cp_async_wait_n<1>(); else cp_async_wait_n<0>();
-        umma::fence_proxy_async_smem();
-        umma::fence_before_sync();
-        if (__syncthreads_or(failed)) goto done;
-        umma::fence_after_sync();
-    }
-
-    // final state (fp32, k-last): for each v, consecutive threads write consecutive k
-    {
-        float sv[HALF];
-        G::ld(tl + TM_S + cb, sv);
-#pragma unroll
-        for (int e = 0; e < HALF; ++e) __stcs(p.new_state + state_off + (size_t)(cb + e) * kDim + row, sv[e]);
-    }
-
-done:
-    cp_async_wait_all();  // no copy may still target shared memory when the CTA exits
-    umma::fence_before_sync();
-    __syncthreads();
-    if (warp == 0) umma::tmem_dealloc(tmem, TM_COLS);
-}
-
-}  // namespace chain
 
 // ============================================================================
 // chain kernel, split-path form (32-wide V tiles)
@@ -1337,6 +1015,538 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain2_kernel(const P
 }
 
 }  // namespace chain2
+
+// ============================================================================
+// chain kernel, transposed form: one CTA per (sequence, v-head), all 128 v
+// ============================================================================
+// The chain's products are taken transposed, with the state's V index as the
+// MMA's M dimension (M = 128 = all of V), so the per-step operands that come
+// from the state side live in tensor memory as A operands and the chunk's
+// tiles from the prep are B operands with N = 128:
+//   MMA_1a(j+1): R^T  = (e^{gamma_C,j} S_j)^T [K;Q]_{j+1}^T   (A = S^T f16 in TMEM)
+//   MMA_1b(j+1): R^T += Dt_j^T G_{j+1}^T                      (A = Dt^T f16 in TMEM)
+//   MMA_2(j)   : [Delta | P'Y]^T = Y_j^T [T;P']_j^T           (A = Y^T f16 in TMEM)
+//   MMA_3(j)   : S^T  += Dt_j^T K_j   (fp32 state accumulated in TMEM; the
+//                state threads first scale it by e^{gamma_C,j})
+// R^T (lane v, columns t': K S, then Q S), Y^T, Dt^T and the outputs are
+// handled one state row v per thread, each token half of a chunk by its own
+// warp.  Each chunk tile is read from shared memory once per head (against
+// four times with 32-wide V tiles) and the A operands cost no shared-memory
+// bandwidth, so one CTA serves a whole head: this is the chain for batches
+// of sequences, where (sequence, v-head) pairs fill the SMs.  The critical
+// path per chunk is two tensor-core round trips
+// (R -> Y -> MMA_2 -> Dt -> MMA_1b -> R).
+//
+// Warp roles (TMEM lane quarter = warp % 4, thread = state row v = 32 * quarter + lane):
+//   warps 0-7    Y_j and Dt_j (tokens 0-31: warps 0-3, 32-63: warps 4-7);
+//   warps 8-15   the outputs O = scale e^gamma QS + P'Y of the same token
+//                halves, staged in shared memory and stored as coalesced
+//                16-byte rows;
+//   warps 16-19  the state: scale S by e^{gamma_C} in TMEM, its f16 A copy,
+//                checkpoints and the final state;
+//   warp 20      one thread issues every MMA, in one order (an accumulator is
+//                only ever written by this thread, and its commits cover all
+//                earlier MMAs);
+//   warp 21      bulk copies of the chunk tiles and gates, a tensor copy of the v rows.
+// (Folding the state work into the output warps, 18 warps at 96 registers,
+// measured 2-7 % slower: the state path then waits for the outputs.)
+namespace chain3 {
+
+constexpr int NT = 704;                  // 22 warps
+constexpr int kYThreads = 256, kOThreads = 256, kSThreads = 128;
+constexpr int kOBase = 256;
+constexpr int kIssuer = 640;             // warp 20, lane 0
+constexpr int kLoaderWarp = 21;
+constexpr int NA = 3;                    // [K;Q] and gate buffers (chunk i in i % 3)
+constexpr int NB = 2;                    // [T;P'], G and v-row buffers (chunk i in i % 2)
+constexpr uint32_t TM_R = 0, TM_D2 = 128, TM_S = 256, TM_SA = 384, TM_YA = 448, TM_DA = 480;
+constexpr uint32_t TM_COLS = 512;
+constexpr uint32_t kVRow = kDim * 2;      // one token's v row, bf16
+constexpr uint32_t kTileV = C * kVRow;    // 16 KiB
+constexpr uint32_t OFF_KQ = 0;
+constexpr uint32_t OFF_TP = OFF_KQ + NA * kTileKQ;
+constexpr uint32_t OFF_G = OFF_TP + NB * kTileTP;
+constexpr uint32_t OFF_V = OFF_G + NB * kTileG;
+constexpr uint32_t OFF_O = OFF_V + NB * kTileV;  // a chunk's output rows, bf16 [t][v]
+constexpr uint32_t OFF_GB = OFF_O + kTileV;
+constexpr uint32_t SMEM_BYTES = OFF_GB + NA * kGateBytes + 1024;
+static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
+static_assert(OFF_TP % 1024 == 0 && OFF_G % 1024 == 0 && OFF_V % 1024 == 0 && OFF_O % 16 == 0 && OFF_GB % 16 == 0,
+              "tile alignment");
+constexpr int kBarO = 1;  // named barrier of the output warps
+// one CTA of this kernel and no prep CTA fit on an SM together, so the 512
+// TMEM columns are never contended
+static_assert(SMEM_BYTES + prep::SMEM_BYTES > 233472, "chain CTA alone on its SM");
+
+constexpr uint32_t ID_K = umma::idesc_f16(128, 128, 0, 0, 0, 0);  // A (TMEM) x K-major B
+constexpr uint32_t ID_M = umma::idesc_f16(128, 128, 0, 0, 0, 1);  // A (TMEM) x MN-major B (K_j for MMA_3)
+
+struct Bars {
+    uint64_t ldA[NA];    // [K;Q] + gates of the chunk in buffer i % 3 landed
+    uint64_t ldB[NB];    // [T;P'] + G (bulk) + v rows (tensor copy) of the chunk in buffer i % 2 landed
+    uint64_t freeA[NA];  // Y, output and state threads done with the gates of buffer i % 3
+    uint64_t mR[2];      // R_i complete (i % 2)
+    uint64_t m2[2];      // MMA_2(i) complete
+    uint64_t m3[2];      // MMA_3(i) complete
+    uint64_t rc;         // Y and output threads have read R_i
+    uint64_t yr;         // Y_i in TMEM
+    uint64_t dr;         // Dt_i in TMEM
+    uint64_t od;         // output threads have read P'Y_i
+    uint64_t sr;         // state scaled and its f16 copy written, phases 0 .. chunks
+    uint64_t fin;        // drain of the issuer's MMAs
+};
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ uint64_t dadd(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
+__device__ __forceinline__ uint32_t ph(long long use) { return (uint32_t)(use & 1); }
+__device__ __forceinline__ void arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(umma::smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ float bf16_bits_to_f32(unsigned short b) { return __uint_as_float((uint32_t)b << 16); }
+// Named barrier of `count` threads that also ors their `pred`s: every
+// participant gets the same answer, so a group leaves its loop together.
+__device__ __forceinline__ bool group_sync_or(int id, int count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(count) : "memory");
+    return r != 0;
+}
+
+// TMA load of one chunk's v rows: box {128 v, 1 head, 64 tokens} of the
+// [T, HV, 128] bf16 tensor at (0, hv, tc) -> shared memory as [t][v]; rows at
+// or past T are zero-filled, rows past the sequence are read but carry beta = 0
+__device__ __forceinline__ void tma_load_v(uint32_t dst, const CUtensorMap* map, int hv, int tc, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        :: "r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(hv), "r"(tc), "r"(umma::smem_u32(bar))
+        : "memory");
+}
+
+__global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain3_kernel(const PrefillParams p,
+                                                                       const unsigned char* ws,
+                                                                       const __grid_constant__ CUtensorMap tmap_v) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ Bars B;
+    __shared__ uint32_t tmem_base_sh;
+    __shared__ volatile int abort_flag;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quarter = warp & 3;
+    const int v = 32 * quarter + lane;  // state row (TMEM lane) of this thread
+    const int hv = (int)(blockIdx.x % p.HV), n = (int)(blockIdx.x / p.HV);
+    const int hq = hv / p.rep;
+
+    long long t0, t1;
+    seq_bounds(p, n, t0, t1);
+    if (tid < kDim) zero_uncovered_outputs(p, n, t0, t1, hv, tid, true);
+    const size_t state_off = ((size_t)n * p.HV + hv) * kDim * kDim;  // [n][hv][v][k]
+    const long long slot0 = t0 / C + n;
+    const long long nchunks = (t1 - t0 + C - 1) / C;
+    if (nchunks == 0) {  // empty sequence: the final state is zero
+        for (int idx = tid; idx < kDim * kDim / 4; idx += NT)
+            reinterpret_cast<float4*>(p.new_state + state_off)[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
+        return;
+    }
+    const int ni = (int)nchunks;
+    auto chunk_len = [&](long long j) { const long long r = t1 - t0 - C * j; return (int)(r < C ? r : C); };
+    auto gates_of = [&](int i) { return reinterpret_cast<const float*>(sm + OFF_GB + (i % NA) * kGateBytes); };
+
+    if (warp == 0) {
+        umma::tmem_alloc(&tmem_base_sh, TM_COLS);
+        umma::tmem_relinquish();
+    }
+    if (tid == 0) {
+        for (int b = 0; b < NA; ++b) {
+            umma::mbar_init(&B.ldA[b], 1);
+            umma::mbar_init(&B.freeA[b], kYThreads + kOThreads + kSThreads);
+        }
+        for (int b = 0; b < NB; ++b) umma::mbar_init(&B.ldB[b], 1);
+        for (int b = 0; b < 2; ++b) {
+            umma::mbar_init(&B.mR[b], 1);
+            umma::mbar_init(&B.m2[b], 1);
+            umma::mbar_init(&B.m3[b], 1);
+        }
+        umma::mbar_init(&B.rc, kYThreads + kOThreads);
+        umma::mbar_init(&B.yr, kYThreads);
+        umma::mbar_init(&B.dr, kYThreads);
+        umma::mbar_init(&B.od, kOThreads);
+        umma::mbar_init(&B.sr, kSThreads);
+        umma::mbar_init(&B.fin, 1);
+        umma::fence_mbar_init();
+        abort_flag = 0;
+    }
+    __syncthreads();
+    umma::fence_after_sync();
+    const uint32_t tmem = tmem_base_sh;
+    const uint32_t tl = tmem + ((uint32_t)(32 * quarter) << 16);
+    bool failed = false;
+    // bounded wait; a failure is remembered (and every later wait then fails at once)
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+        if (failed || abort_flag) { failed = true; return; }
+        if (!umma::mbar_wait(bar, parity, kWaitBudget)) { failed = true; abort_flag = 1; }
+    };
+    int issuedA = 0, issuedB = 0;  // loads issued by the loader warp (chunks 0 .. issued - 1)
+
+    if (warp == kLoaderWarp) {
+        // ---- A = [K;Q] + gates (bulk, 3 buffers); B = [T;P'] + G (bulk) + v rows (tensor copy), 2 buffers ----
+        auto loadA = [&](int i) {
+            const long long j = i, slot = slot0 + j;
+            const int b = i % NA;
+            if (lane == 0) {
+                umma::mbar_arrive_expect_tx(&B.ldA[b], kTileKQ + kGateBytes);
+                const unsigned char* kq = ws_kq(p, ws) + ((size_t)slot * p.H + hq) * kTileKQ;
+                const unsigned char* rec = ws + ((size_t)slot * p.HV + hv) * kSlotBytes;
+                umma::bulk_g2s(umma::smem_u32(sm + OFF_KQ + b * kTileKQ), kq, kTileKQ / 2, &B.ldA[b]);
+                umma::bulk_g2s(umma::smem_u32(sm + OFF_KQ + b * kTileKQ + kTileKQ / 2), kq + kTileKQ / 2,
+                               kTileKQ / 2, &B.ldA[b]);
+                umma::bulk_g2s(umma::smem_u32(sm + OFF_GB + b * kGateBytes), rec + kTileTP, kGateBytes, &B.ldA[b]);
+            }
+            __syncwarp();
+        };
+        auto loadB = [&](int i) {
+            const long long j = i, slot = slot0 + j, tc = t0 + C * j;
+            const int b = i % NB;
+            const bool g = i > 0;  // G_j only feeds MMA_1b(j), which the first chunk of a launch has not
+            if (lane == 0) {
+                umma::mbar_arrive_expect_tx(&B.ldB[b], kTileTP + (g ? kTileG : 0) + kTileV);
+                const unsigned char* rec = ws + ((size_t)slot * p.HV + hv) * kSlotBytes;
+                umma::bulk_g2s(umma::smem_u32(sm + OFF_TP + b * kTileTP), rec, kTileTP, &B.ldB[b]);
+                if (g)
+                    umma::bulk_g2s(umma::smem_u32(sm + OFF_G + b * kTileG),
+                                   ws_g(p, ws) + ((size_t)slot * p.H + hq) * kTileG, kTileG, &B.ldB[b]);
+                tma_load_v(umma::smem_u32(sm + OFF_V + b * kTileV), &tmap_v, hv, (int)tc, &B.ldB[b]);
+            }
+            __syncwarp();
+        };
+        for (int i = 0; i < NA && i < ni; ++i) loadA(i);
+        for (int i = 0; i < NB && i < ni; ++i) loadB(i);
+        issuedA = ni < NA ? ni : NA;
+        issuedB = ni < NB ? ni : NB;
+        for (int i = 0; i < ni && !failed; ++i) {
+            if (i + NB < ni) {  // buffer of chunk i: MMA_2(i) done (after MMA_1b(i) and the Y threads' reads)
+                wait(&B.m2[i % 2], ph(i / 2));
+                if (failed) break;
+                loadB(i + NB);
+                issuedB = i + NB + 1;
+            }
+            if (i + NA < ni) {  // MMA_3(i) done (after MMA_1a(i)) and every thread done with the gates
+                wait(&B.m3[i % 2], ph(i / 2));
+                wait(&B.freeA[i % NA], ph(i / NA));
+                if (failed) break;
+                loadA(i + NA);
+                issuedA = i + NA + 1;
+            }
+        }
+    } else if (tid == kIssuer) {
+        // ---- the MMA issuer ----
+        const uint64_t dKQ0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_KQ), 128, 0);
+        const uint64_t dKT0 = umma::desc_sw128(umma::smem_u32(sm + OFF_KQ), 16384u, 1024u);
+        const uint64_t dTP0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_TP), 128, 0);
+        const uint64_t dG0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_G), 128, 0);
+        auto mma_1a = [&](int i) {  // R^T = SA [K;Q]_i^T (overwrites R)
+            const uint64_t b0 = dadd(dKQ0, (uint32_t)(i % NA) * kTileKQ);
+#pragma unroll
+            for (int k0 = 0; k0 < kDim; k0 += 16)
+                umma::mma_f16_ts(tmem + TM_R, tmem + TM_SA + k0 / 2, dadd(b0, umma::koff_kmaj(128, k0)), ID_K,
+                                 k0 > 0);
+        };
+        wait(&B.sr, 0);
+        wait(&B.ldA[0], 0);
+        if (!failed) {
+            umma::fence_after_sync();
+            mma_1a(0);
+            umma::mma_commit(&B.mR[0]);
+        }
+        for (int i = 0; i < ni && !failed; ++i) {
+            // MMA_2(i): [Delta | P'Y]^T = Y^T [T;P']_i^T, once Y_i is in TMEM and P'Y_{i-1} has been read
+            wait(&B.yr, ph(i));
+            wait(&B.ldB[i % NB], ph(i / NB));
+            if (i > 0) wait(&B.od, ph(i - 1));
+            if (failed) break;
+            umma::fence_after_sync();
+            {
+                const uint64_t b0 = dadd(dTP0, (uint32_t)(i % NB) * kTileTP);
+#pragma unroll
+                for (int k0 = 0; k0 < C; k0 += 16)
+                    umma::mma_f16_ts(tmem + TM_D2, tmem + TM_YA + k0 / 2, dadd(b0, umma::koff_kmaj(128, k0)), ID_K,
+                                     k0 > 0);
+                umma::mma_commit(&B.m2[i % 2]);
+            }
+            if (i + 1 < ni) {
+                // MMA_1a(i+1) once R_i has been read and the scaled state's f16 copy is written
+                wait(&B.rc, ph(i));
+                wait(&B.sr, ph(i + 1));
+                wait(&B.ldA[(i + 1) % NA], ph((i + 1) / NA));
+                if (failed) break;
+                umma::fence_after_sync();
+                mma_1a(i + 1);
+                // MMA_1b(i+1): R^T += Dt_i^T G_{i+1}^T
+                wait(&B.dr, ph(i));
+                wait(&B.ldB[(i + 1) % NB], ph((i + 1) / NB));
+                if (failed) break;
+                umma::fence_after_sync();
+                const uint64_t b0 = dadd(dG0, (uint32_t)((i + 1) % NB) * kTileG);
+#pragma unroll
+                for (int k0 = 0; k0 < C; k0 += 16)
+                    umma::mma_f16_ts(tmem + TM_R, tmem + TM_DA + k0 / 2, dadd(b0, umma::koff_kmaj(128, k0)), ID_K,
+                                     true);
+                umma::mma_commit(&B.mR[(i + 1) % 2]);
+            } else {
+                wait(&B.dr, ph(i));
+                wait(&B.sr, ph(i + 1));
+                if (failed) break;
+                umma::fence_after_sync();
+            }
+            // MMA_3(i): S^T += Dt_i^T K_i onto the state the state threads scaled by e^{gamma_C,i}
+            const uint64_t b0 = dadd(dKT0, (uint32_t)(i % NA) * kTileKQ);
+#pragma unroll
+            for (int k0 = 0; k0 < C; k0 += 16)
+                umma::mma_f16_ts(tmem + TM_S, tmem + TM_DA + k0 / 2, dadd(b0, umma::koff_mnmaj(k0)), ID_M, true);
+            umma::mma_commit(&B.m3[i % 2]);
+        }
+        // drain: every MMA issued here completes before the CTA exits
+        umma::mma_commit(&B.fin);
+        if (!umma::mbar_wait(&B.fin, 0, kWaitBudget)) failed = true;
+    } else if (warp < 8) {
+        // ---- Y_i = beta (V - e^gamma KS) and Dt_i = e^{gamma_C - gamma} Delta, row v, 32 tokens ----
+        const int h0 = 32 * (warp >> 2);  // this warp's first token of the chunk
+        for (int i = 0; i < ni && !failed; ++i) {
+            wait(&B.ldA[i % NA], ph(i / NA));
+            wait(&B.ldB[i % NB], ph(i / NB));
+            if (failed) break;
+            const float* gr = gates_of(i);
+            wait(&B.mR[i % 2], ph(i / 2));
+            if (failed) break;
+            umma::fence_after_sync();
+            {
+                float ks[32];
+                umma::tmem_ld32(tl + TM_R + h0, ks);
+                umma::fence_before_sync();
+                arrive(&B.rc);
+                uint32_t y[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) {
+                    const float4 be = *reinterpret_cast<const float4*>(gr + GR_BEG + h0 + e);
+                    const float4 bt = *reinterpret_cast<const float4*>(gr + GR_BETA + h0 + e);
+                    const unsigned short* vcol =
+                        reinterpret_cast<const unsigned short*>(sm + OFF_V + (i % NB) * kTileV) + (h0 + e) * kDim + v;
+                    const float2 bv01 = __fmul2_rn(make_float2(bt.x, bt.y), make_float2(bf16_bits_to_f32(vcol[0]), bf16_bits_to_f32(vcol[kDim])));
+                    const float2 bv23 = __fmul2_rn(make_float2(bt.z, bt.w), make_float2(bf16_bits_to_f32(vcol[2 * kDim]), bf16_bits_to_f32(vcol[3 * kDim])));
+                    const float2 y01 = __ffma2_rn(make_float2(-be.x, -be.y), make_float2(ks[e], ks[e + 1]), bv01);
+                    const float2 y23 = __ffma2_rn(make_float2(-be.z, -be.w), make_float2(ks[e + 2], ks[e + 3]), bv23);
+                    y[e / 2] = pack_f16x2(y01.x, y01.y);
+                    y[e / 2 + 1] = pack_f16x2(y23.x, y23.y);
+                }
+                umma::tmem_st16_u32_nowait(tl + TM_YA + h0 / 2, y);
+                umma::tmem_wait_st();
+                umma::fence_before_sync();
+                arrive(&B.yr);
+            }
+            wait(&B.m2[i % 2], ph(i / 2));
+            if (failed) break;
+            umma::fence_after_sync();
+            {
+                float dl[32];
+                umma::tmem_ld32(tl + TM_D2 + h0, dl);
+                uint32_t d[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) {
+                    const float4 fk = *reinterpret_cast<const float4*>(gr + GR_FK + h0 + e);
+                    const float2 d01 = __fmul2_rn(make_float2(fk.x, fk.y), make_float2(dl[e], dl[e + 1]));
+                    const float2 d23 = __fmul2_rn(make_float2(fk.z, fk.w), make_float2(dl[e + 2], dl[e + 3]));
+                    d[e / 2] = pack_f16x2(d01.x, d01.y);
+                    d[e / 2 + 1] = pack_f16x2(d23.x, d23.y);
+                }
+                umma::tmem_st16_u32_nowait(tl + TM_DA + h0 / 2, d);
+                umma::tmem_wait_st();
+                umma::fence_before_sync();
+                arrive(&B.dr);
+                arrive(&B.freeA[i % NA]);
+            }
+        }
+    } else if (warp < 16) {
+        // ---- outputs O[t][v] = scale e^{gamma_t} QS + P'Y (32 tokens per warp): staged
+        // as bf16 rows in shared memory, then written back as coalesced 16-byte stores ----
+        const int h0 = 32 * ((warp - 8) >> 2);
+        const int o = tid - kOBase;
+        unsigned char* otile = sm + OFF_O;
+        for (int i = 0; i < ni; ++i) {
+            const long long j = i, tc = t0 + C * j;
+            const int len = chunk_len(j);
+            wait(&B.ldA[i % NA], ph(i / NA));
+            wait(&B.mR[i % 2], ph(i / 2));
+            float qs[32];
+            if (!failed) {
+                umma::fence_after_sync();
+                umma::tmem_ld32(tl + TM_R + 64 + h0, qs);
+                umma::fence_before_sync();
+                arrive(&B.rc);
+            }
+            wait(&B.m2[i % 2], ph(i / 2));
+            // every output thread has copied the previous chunk's rows out of the tile
+            if (group_sync_or(kBarO, kOThreads, failed)) break;
+            umma::fence_after_sync();
+            const float* gr = gates_of(i);
+            unsigned short* ocol = reinterpret_cast<unsigned short*>(otile) + h0 * kDim + v;
+#pragma unroll
+            for (int hh = 0; hh < 32; hh += 16) {
+                float py[16];
+                umma::tmem_ld16(tl + TM_D2 + 64 + h0 + hh, py);
+                if (hh == 16) {
+                    umma::fence_before_sync();
+                    arrive(&B.od);
+                }
+#pragma unroll
+                for (int e = 0; e < 16; e += 4) {
+                    const float4 fq = *reinterpret_cast<const float4*>(gr + GR_FQ + h0 + hh + e);
+                    const float2 o01 = __ffma2_rn(make_float2(fq.x, fq.y), make_float2(qs[hh + e], qs[hh + e + 1]),
+                                                  make_float2(py[e], py[e + 1]));
+                    const float2 o23 = __ffma2_rn(make_float2(fq.z, fq.w), make_float2(qs[hh + e + 2], qs[hh + e + 3]),
+                                                  make_float2(py[e + 2], py[e + 3]));
+                    ocol[(hh + e) * kDim] = __bfloat16_as_ushort(__float2bfloat16_rn(o01.x));
+                    ocol[(hh + e + 1) * kDim] = __bfloat16_as_ushort(__float2bfloat16_rn(o01.y));
+                    ocol[(hh + e + 2) * kDim] = __bfloat16_as_ushort(__float2bfloat16_rn(o23.x));
+                    ocol[(hh + e + 3) * kDim] = __bfloat16_as_ushort(__float2bfloat16_rn(o23.y));
+                }
+            }
+            arrive(&B.freeA[i % NA]);
+            if (group_sync_or(kBarO, kOThreads, failed)) break;  // the tile holds the chunk's rows
+            // 16 threads per 256-byte token row: coalesced 16-byte stores
+#pragma unroll 1
+            for (int c = o; c < C * 16; c += kOThreads) {
+                const int r = c >> 4, q = c & 15;
+                if (r < len)
+                    __stcs(reinterpret_cast<uint4*>(p.out + ((size_t)(tc + r) * p.HV + hv) * kDim) + q,
+                           *reinterpret_cast<const uint4*>(otile + r * kVRow + q * 16));
+            }
+        }
+    } else if (warp < 20) {
+        // ---- the state (fp32 in TMEM): scale by e^{gamma_C}, f16 A copy, checkpoints, final ----
+        const float* srow = p.state ? p.state + state_off + (size_t)v * kDim : nullptr;
+        float* drow = p.new_state + state_off + (size_t)v * kDim;
+        auto ckpt_store = [&](long long done, int c16, const float* x) {
+            float* cd = ckpt_dst(p, n, hv, done);
+            if (cd != nullptr) {
+#pragma unroll
+                for (int e = 0; e < 16; e += 4)
+                    __stcs(reinterpret_cast<float4*>(cd + (size_t)v * kDim + c16 + e), make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]));
+            }
+        };
+        wait(&B.ldA[0], 0);
+        if (!failed) {
+            const float decay = gates_of(0)[GR_DECAY];
+            // S_0 -> TMEM (scaled by e^{gamma_C}) and its f16 copy (unscaled, for MMA_1a of the first chunk)
+#pragma unroll 1
+            for (int c = 0; c < kDim; c += 32) {
+                float x[32];
+#pragma unroll
+                for (int e = 0; e < 32; e += 4) {
+                    const float4 f = srow ? *reinterpret_cast<const float4*>(srow + c + e) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    x[e] = f.x; x[e + 1] = f.y; x[e + 2] = f.z; x[e + 3] = f.w;
+                }
+                uint32_t h[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) h[e] = pack_f16x2(x[2 * e], x[2 * e + 1]);
+                umma::tmem_st16_u32_nowait(tl + TM_SA + c / 2, h);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) x[e] *= decay;
+                umma::tmem_st32_nowait(tl + TM_S + c, x);
+            }
+            umma::tmem_wait_st();
+            umma::fence_before_sync();
+            arrive(&B.sr);                       // phase 0
+        }
+        wait(&B.mR[0], 0);                       // MMA_1a of the first chunk has read the copy
+        if (!failed) {
+            umma::fence_after_sync();
+#pragma unroll 1
+            for (int c = 0; c < kDim; c += 32) {  // f16 copy of e^{gamma_C} S for MMA_1a of the next chunk
+                float x[32];
+                umma::tmem_ld32(tl + TM_S + c, x);
+                uint32_t h[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) h[e] = pack_f16x2(x[2 * e], x[2 * e + 1]);
+                umma::tmem_st16_u32_nowait(tl + TM_SA + c / 2, h);
+            }
+            umma::tmem_wait_st();
+            umma::fence_before_sync();
+            arrive(&B.sr);                       // phase 1
+            arrive(&B.freeA[0]);
+        }
+        for (int i = 1; i < ni && !failed; ++i) {
+            // MMA_3(i - 1) done: TMEM holds S_i; scale it, f16 copy for MMA_1a(i+1)
+            wait(&B.m3[(i - 1) % 2], ph((i - 1) / 2));
+            wait(&B.ldA[i % NA], ph(i / NA));
+            if (failed) break;
+            umma::fence_after_sync();
+            const long long j = i;
+            const bool ck = p.ckpt != nullptr && chunk_len(j - 1) == C && (C * j) % p.ckpt_every == 0;
+            const float decay = gates_of(i)[GR_DECAY];
+#pragma unroll 1
+            for (int c = 0; c < kDim; c += 32) {
+                float x[32];
+                umma::tmem_ld32(tl + TM_S + c, x);
+                if (ck) {
+                    ckpt_store(C * j, c, x);
+                    ckpt_store(C * j, c + 16, x + 16);
+                }
+#pragma unroll
+                for (int e = 0; e < 32; ++e) x[e] *= decay;
+                umma::tmem_st32_nowait(tl + TM_S + c, x);
+                uint32_t h[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) h[e] = pack_f16x2(x[2 * e], x[2 * e + 1]);
+                umma::tmem_st16_u32_nowait(tl + TM_SA + c / 2, h);
+            }
+            umma::tmem_wait_st();
+            umma::fence_before_sync();
+            arrive(&B.sr);                       // phase i + 1
+            arrive(&B.freeA[i % NA]);
+        }
+        // the final state -> new_state, and its checkpoint
+        wait(&B.m3[(ni - 1) % 2], ph((ni - 1) / 2));
+        if (!failed) {
+            umma::fence_after_sync();
+            const bool ck = p.ckpt != nullptr && chunk_len(nchunks - 1) == C && (C * nchunks) % p.ckpt_every == 0;
+#pragma unroll 1
+            for (int c = 0; c < kDim; c += 32) {
+                float x[32];
+                umma::tmem_ld32(tl + TM_S + c, x);
+                if (ck) {
+                    ckpt_store(C * nchunks, c, x);
+                    ckpt_store(C * nchunks, c + 16, x + 16);
+                }
+#pragma unroll
+                for (int e = 0; e < 32; e += 4)
+                    __stcs(reinterpret_cast<float4*>(drow + c + e), make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]));
+            }
+        }
+    }
+
+    // ---- exit: copies in flight land first ----
+    umma::fence_before_sync();
+    failed = __syncthreads_or(failed) || abort_flag;
+    if (failed && warp == kLoaderWarp) {
+        if (lane == 0) atomicOr(&g_device_status, kDevStatTimeout);
+        for (int i = (issuedA > NA ? issuedA - NA : 0); i < issuedA; ++i)
+            umma::mbar_wait(&B.ldA[i % NA], ph(i / NA), kWaitBudget);
+        for (int i = (issuedB > NB ? issuedB - NB : 0); i < issuedB; ++i)
+            umma::mbar_wait(&B.ldB[i % NB], ph(i / NB), kWaitBudget);
+    }
+    __syncthreads();
+    if (warp == 0) umma::tmem_dealloc(tmem, TM_COLS);
+}
+
+}  // namespace chain3
 }  // namespace chunk
 
 size_t prefill_workspace_bytes(int N, int T, int H, int HV) {
@@ -1370,12 +1580,11 @@ cudaError_t chunk_setup_current_device(int& num_sms) {
                                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)chunk::prep::SMEM_BYTES);
         if (r == cudaSuccess)
-            r = cudaFuncSetAttribute(chunk::chain::gdn_prefill_chunk_chain_kernel<64>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)chunk::chain::Cfg<64>::SMEM_BYTES);
-        if (r == cudaSuccess)
             r = cudaFuncSetAttribute(chunk::chain2::gdn_prefill_chunk_chain2_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain2::SMEM_BYTES);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(chunk::chain3::gdn_prefill_chunk_chain3_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain3::SMEM_BYTES);
         int sms = 0;
         if (r == cudaSuccess) r = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (r == cudaSuccess && sms <= 0) r = cudaErrorInvalidValue;
@@ -1386,6 +1595,40 @@ cudaError_t chunk_setup_current_device(int& num_sms) {
     return s.status;
 }
 
+// The driver's tensor-map encoder, looked up through the runtime once, so
+// the library has no link-time dependency on the driver library (it then
+// also loads on machines without a GPU driver, where nothing is launched).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled_fn() {
+    static std::once_flag once;
+    static EncodeTiledFn fn = nullptr;
+    std::call_once(once, []() {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    });
+    return fn;
+}
+
+// Tensor map of the v input [T, HV, 128] bf16 for the chain's TMA loads:
+// dimensions (128, HV, T), box (128, 1, 64).  Encoding is a host-side
+// computation (no device call).
+bool encode_v_map(const PrefillParams& p, CUtensorMap* map) {
+    const EncodeTiledFn encode = encode_tiled_fn();
+    if (encode == nullptr) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)kDim, (cuuint64_t)p.HV, (cuuint64_t)p.T};
+    const cuuint64_t strides[2] = {(cuuint64_t)kDim * 2, (cuuint64_t)p.HV * kDim * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)kDim, 1u, (cuuint32_t)chunk::C};
+    const cuuint32_t estr[3] = {1u, 1u, 1u};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<__nv_bfloat16*>(p.v), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 int launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st) {
@@ -1393,21 +1636,31 @@ int launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t s
     if (chunk_setup_current_device(num_sms) != cudaSuccess) return GDN_ERR_CUDA;
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     const long long slots = chunk::ws_slots(p.N, p.T);
-    // one chain per (sequence, v-head, V tile): 32-wide tiles on the split
-    // critical path when 64-wide ones would not cover the SMs (e.g. a single
-    // long sequence); that path needs the prep's cross-Gram tiles
-    const long long chains64 = (long long)p.N * p.HV * (kDim / 64);
-    const bool split = chains64 < num_sms;
+    // Chain kernel: the split-path chain (four 32-wide V tiles per head, one
+    // CTA per SM) when all its CTAs fit in one wave, i.e. few (sequence,
+    // v-head) pairs such as one long sequence: four SMs then share each
+    // head's per-chunk work.  Otherwise the transposed chain, one CTA per
+    // (sequence, v-head).  Measured on B200 (ms): one 8192-token sequence at
+    // HV = 32: split 0.310, transposed 0.425; 16 sequences (8,184 tokens,
+    // HV = 32): split 0.374, transposed 0.267.  GDN_PREFILL_CHAIN = 2 or 3
+    // forces one of them (both compute the same result; the tests run
+    // every chunked case through each).
+    const long long pairs = (long long)p.N * p.HV;
+    int which = 4 * pairs <= num_sms ? 2 : 3;
+    const char* sel = getenv("GDN_PREFILL_CHAIN");
+    if (sel && (sel[0] == '2' || sel[0] == '3') && sel[1] == '\0') which = sel[0] - '0';
     PrefillParams q = p;
-    q.cross_gram = split ? 1 : 0;
+    q.cross_gram = 1;  // both chains take the next chunk's R through the cross-Gram tiles
     chunk::prep::gdn_prefill_chunk_prep_kernel<<<(unsigned)(slots * p.HV), chunk::prep::NT,
-                                                 chunk::prep::SMEM_BYTES, st>>>(q, ws);
-    if (split) {
-        chunk::chain2::gdn_prefill_chunk_chain2_kernel<<<(unsigned)(chains64 * 2), chunk::chain2::NT,
-                                                         chunk::chain2::SMEM_BYTES, st>>>(q, ws);
+                                                 chunk::prep::SMEM_BYTES, st>>>(q, ws, 0);
+    if (which == 2) {
+        chunk::chain2::gdn_prefill_chunk_chain2_kernel<<<(unsigned)(pairs * (kDim / chunk::chain2::VT)),
+                                                         chunk::chain2::NT, chunk::chain2::SMEM_BYTES, st>>>(q, ws);
     } else {
-        chunk::chain::gdn_prefill_chunk_chain_kernel<64><<<(unsigned)chains64, chunk::chain::NT,
-                                                           chunk::chain::Cfg<64>::SMEM_BYTES, st>>>(p, ws);
+        CUtensorMap tmap_v;
+        if (!encode_v_map(p, &tmap_v)) return GDN_ERR_CUDA;
+        chunk::chain3::gdn_prefill_chunk_chain3_kernel<<<(unsigned)pairs, chunk::chain3::NT,
+                                                         chunk::chain3::SMEM_BYTES, st>>>(q, ws, tmap_v);
     }
     return gdn_launch_status();
 }

@@ -17,11 +17,16 @@ from rocm_flashinfer_contest_b200 import gdn_prefill, inputs
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["chunk", "recurrent"])
+@pytest.fixture(params=["chunk2", "chunk3", "recurrent"])
 def path(request, monkeypatch):
-    """Runs a test through the chunked tensor-core kernel (threshold 0) or the
+    """Runs a test through the chunked tensor-core kernels (threshold 0) with
+    either chain kernel forced (split-path chain2, transposed chain3), or the
     token-serial kernel (threshold above any T used here)."""
-    monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "0" if request.param == "chunk" else "1000000000")
+    if request.param == "recurrent":
+        monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "1000000000")
+    else:
+        monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "0")
+        monkeypatch.setenv("GDN_PREFILL_CHAIN", request.param[-1])
     return request.param
 
 
