@@ -100,10 +100,12 @@ static int prefill_impl(const void* q, const void* k, const void* v, const float
         return e == cudaSuccess ? GDN_OK : GDN_ERR_CUDA;
     }
     if (T > 0 && use_chunk_path(T)) {
-        const size_t need = gdn::prefill_workspace_bytes(N, T, H, HV);
+        // the split-path layout is the least a chunked call runs in; a
+        // workspace of gdn_prefill_workspace_bytes also admits the scan chain
+        const size_t need = gdn::prefill_workspace_bytes_split(N, T, H, HV);
         if (!workspace || workspace_bytes < need) return GDN_ERR_INVALID;
         if (!gdn_aligned(workspace, 16)) return GDN_ERR_ALIGN;
-        return gdn::launch_prefill_chunk(p, workspace, st);
+        return gdn::launch_prefill_chunk(p, workspace, workspace_bytes, st);
     } else {
         gdn::launch_prefill_recurrent(p, st);
     }

@@ -1547,11 +1547,19 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_chunk_chain3_kernel(const P
 }
 
 }  // namespace chain3
+
+#include "gdn_prefill_scan.cuh"
+
 }  // namespace chunk
 
-size_t prefill_workspace_bytes(int N, int T, int H, int HV) {
+size_t prefill_workspace_bytes_split(int N, int T, int H, int HV) {
     return (size_t)chunk::ws_slots(N, T) *
            ((size_t)HV * chunk::kSlotBytes + (size_t)H * (chunk::kTileKQ + chunk::kTileG));
+}
+
+size_t prefill_workspace_bytes(int N, int T, int H, int HV) {
+    const size_t a = prefill_workspace_bytes_split(N, T, H, HV), b = chunk::scan::workspace_bytes(N, T, HV);
+    return a > b ? a : b;
 }
 
 namespace {
@@ -1585,6 +1593,12 @@ cudaError_t chunk_setup_current_device(int& num_sms) {
         if (r == cudaSuccess)
             r = cudaFuncSetAttribute(chunk::chain3::gdn_prefill_chunk_chain3_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain3::SMEM_BYTES);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(chunk::scan::prep::gdn_prefill_scan_prep_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::scan::prep::SMEM_BYTES);
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(chunk::scan::chain::gdn_prefill_scan_chain_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::scan::chain::SMEM_BYTES);
         int sms = 0;
         if (r == cudaSuccess) r = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (r == cudaSuccess && sms <= 0) r = cudaErrorInvalidValue;
@@ -1631,7 +1645,7 @@ bool encode_v_map(const PrefillParams& p, CUtensorMap* map) {
 
 }  // namespace
 
-int launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st) {
+int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspace_bytes, cudaStream_t st) {
     int num_sms = 0;
     if (chunk_setup_current_device(num_sms) != cudaSuccess) return GDN_ERR_CUDA;
     unsigned char* ws = static_cast<unsigned char*>(workspace);
@@ -1642,13 +1656,24 @@ int launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t s
     // head's per-chunk work.  Otherwise the transposed chain, one CTA per
     // (sequence, v-head).  Measured on B200 (ms): one 8192-token sequence at
     // HV = 32: split 0.310, transposed 0.425; 16 sequences (8,184 tokens,
-    // HV = 32): split 0.374, transposed 0.267.  GDN_PREFILL_CHAIN = 2 or 3
-    // forces one of them (both compute the same result; the tests run
-    // every chunked case through each).
+    // HV = 32): split 0.374, transposed 0.267.  GDN_PREFILL_CHAIN = 2, 3 or
+    // 4 forces one of them (4: the scan over per-chunk transitions, which
+    // needs the larger workspace; all compute the same result within the
+    // operand rounding, and the tests run every chunked case through each).
     const long long pairs = (long long)p.N * p.HV;
+    const bool scan_fits = workspace_bytes >= chunk::scan::workspace_bytes(p.N, p.T, p.HV);
     int which = 4 * pairs <= num_sms ? 2 : 3;
     const char* sel = getenv("GDN_PREFILL_CHAIN");
-    if (sel && (sel[0] == '2' || sel[0] == '3') && sel[1] == '\0') which = sel[0] - '0';
+    if (sel && sel[0] >= '2' && sel[0] <= '4' && sel[1] == '\0' && (sel[0] != '4' || scan_fits)) which = sel[0] - '0';
+    if (which == 4) {
+        CUtensorMap tmap_v;
+        if (!encode_v_map(p, &tmap_v)) return GDN_ERR_CUDA;
+        chunk::scan::prep::gdn_prefill_scan_prep_kernel<<<(unsigned)(slots * p.HV), chunk::scan::prep::NT,
+                                                          chunk::scan::prep::SMEM_BYTES, st>>>(p, ws);
+        chunk::scan::chain::gdn_prefill_scan_chain_kernel<<<(unsigned)pairs, chunk::scan::chain::NT,
+                                                            chunk::scan::chain::SMEM_BYTES, st>>>(p, ws, tmap_v);
+        return gdn_launch_status();
+    }
     PrefillParams q = p;
     q.cross_gram = 1;  // both chains take the next chunk's R through the cross-Gram tiles
     chunk::prep::gdn_prefill_chunk_prep_kernel<<<(unsigned)(slots * p.HV), chunk::prep::NT,

@@ -79,7 +79,13 @@ int prefill_check_args(const void* q, const void* k, const void* v, const float*
 void launch_prefill_recurrent(const PrefillParams& p, cudaStream_t st);
 // Launches the chunked kernels (prep, then a chain kernel); returns a GDN_*
 // status (GDN_ERR_CUDA when the per-device launch set-up or a launch fails).
-int launch_prefill_chunk(const PrefillParams& p, void* workspace, cudaStream_t st);
+// `workspace_bytes` steers the choice of chain: the scan chain needs the
+// larger of the two workspace layouts.
+int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspace_bytes, cudaStream_t st);
+// Workspace of the chunked path: enough for every chain (the scan chain's
+// layout is the larger one), and the split-path layout alone (the least a
+// chunked call can run in).
 size_t prefill_workspace_bytes(int N, int T, int H, int HV);
+size_t prefill_workspace_bytes_split(int N, int T, int H, int HV);
 
 }  // namespace gdn

@@ -57,7 +57,7 @@ extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void*
     const int chk = gdn::prefill_check_args(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64,
                                             N, T, H, HV, K, V, out, new_state);
     if (chk != GDN_OK) return chk;
-    if (gdn_prefill_workspace_bytes(N, T, H, HV) > kScratchBytes) return GDN_ERR_TOO_LARGE;
+    if (gdn::prefill_workspace_bytes_split(N, T, H, HV) > kScratchBytes) return GDN_ERR_TOO_LARGE;
     if (N == 0 && T == 0) return GDN_OK;
     void* scratch = nullptr;
     const int st = scratch_on_current_device(&scratch);

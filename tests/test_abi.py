@@ -286,8 +286,11 @@ def test_prefill_host_workspace_bytes():
 
 
 def test_prefill_workspace_size(monkeypatch):
+    """The workspace covers both layouts of the chunked path: per 64-token
+    slot, the split/transposed chains' [T;P'] records and [K;Q] + G tiles,
+    and the scan chain's 73,744-byte transition records per v-head."""
     ws = _lib.lib().gdn_prefill_workspace_bytes
-    per_slot = lambda H, HV: HV * 17424 + H * (32768 + 16384)  # noqa: E731
+    per_slot = lambda H, HV: max(HV * 17424 + H * (32768 + 16384), HV * 73744)  # noqa: E731
     monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "128")
     assert ws(1, 8192, 16, 32) == (8192 // 64 + 1) * per_slot(16, 32)
     assert ws(16, 5000, 4, 8) == (5000 // 64 + 16) * per_slot(4, 8)
@@ -295,6 +298,7 @@ def test_prefill_workspace_size(monkeypatch):
     assert ws(0, 0, 4, 8) == 0
     monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "0")
     assert ws(3, 100, 4, 8) == (100 // 64 + 3) * per_slot(4, 8)
+    assert ws(2, 640, 16, 16) == (640 // 64 + 2) * per_slot(16, 16)   # H == HV: the split layout is larger
 
 
 def test_error_is_raised_as_exception():

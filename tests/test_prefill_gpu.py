@@ -17,11 +17,12 @@ from rocm_flashinfer_contest_b200 import gdn_prefill, inputs
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["chunk2", "chunk3", "recurrent"])
+@pytest.fixture(params=["chunk2", "chunk3", "chunk4", "recurrent"])
 def path(request, monkeypatch):
     """Runs a test through the chunked tensor-core kernels (threshold 0) with
-    either chain kernel forced (split-path chain2, transposed chain3), or the
-    token-serial kernel (threshold above any T used here)."""
+    one chain kernel forced (split-path chain2, transposed chain3, scan over
+    per-chunk transitions chain4), or the token-serial kernel (threshold
+    above any T used here)."""
     if request.param == "recurrent":
         monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "1000000000")
     else:

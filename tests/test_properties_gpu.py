@@ -5,7 +5,7 @@ the public entry points, held to the parity bar of tests/parity.py.
 * resume: prefilling tokens [0, T) in one call equals prefilling [0, t) and
   then [t, T) from the first call's final state (chunk-aligned and unaligned
   split points) — the recurrence is a left fold over tokens;
-* the chunked tensor-core kernels (with either chain kernel) and the
+* the chunked tensor-core kernels (with each chain kernel) and the
   token-serial kernel agree on the whole config-2 sequence (8192 tokens, all
   32 v-heads) and on config 3;
 * a prefill of one-token sequences equals one decode step, and a
@@ -58,7 +58,7 @@ def test_prefill_resume_past_32_bit_offsets(cuda_device):
     assert_state_close(s2.cpu(), s.cpu())
 
 
-@pytest.mark.parametrize("chain", ["2", "3"])
+@pytest.mark.parametrize("chain", ["2", "3", "4"])
 def test_prefill_chunked_and_token_serial_agree_full_size(cuda_device, monkeypatch, chain):
     args = inputs.prefill_inputs([8192], seed=2, with_state=False, device=cuda_device)
     monkeypatch.setenv("GDN_PREFILL_CHAIN", chain)
@@ -71,7 +71,7 @@ def test_prefill_chunked_and_token_serial_agree_full_size(cuda_device, monkeypat
     assert_state_close(sc.cpu(), sr.cpu())
 
 
-@pytest.mark.parametrize("chain", ["2", "3"])
+@pytest.mark.parametrize("chain", ["2", "3", "4"])
 def test_prefill_varlen_chunked_and_token_serial_agree(cuda_device, monkeypatch, chain):
     """Config 3 (16 sequences, lengths U[1, 1024], non-zero states)."""
     lens = inputs.seqlens_uniform(16, 1, 1024, seed=0, max_total=8192)
@@ -86,7 +86,7 @@ def test_prefill_varlen_chunked_and_token_serial_agree(cuda_device, monkeypatch,
     assert_state_close(sc.cpu(), sr.cpu())
 
 
-@pytest.mark.parametrize("path", ["chunk2", "chunk3", "recurrent"])
+@pytest.mark.parametrize("path", ["chunk2", "chunk3", "chunk4", "recurrent"])
 def test_one_token_prefills_equal_a_decode_step(cuda_device, monkeypatch, path):
     B = 64
     monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "1000000000" if path == "recurrent" else "0")
