@@ -1609,6 +1609,32 @@ cudaError_t chunk_setup_current_device(int& num_sms) {
     return s.status;
 }
 
+// The scan path's second stream, per device: its prep runs there beside the
+// chain (fork and join by events), created on first use with that device
+// current.  The mutex keeps one call's record / wait / launch sequence whole
+// when host threads share a device.
+struct ScanStreams {
+    std::once_flag once;
+    cudaError_t status = cudaErrorNotReady;
+    cudaStream_t aux = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+    std::mutex mu;
+};
+ScanStreams g_scan_streams[kMaxDevices];
+
+ScanStreams* scan_streams_current_device() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    ScanStreams& s = g_scan_streams[dev];
+    std::call_once(s.once, [&]() {
+        cudaError_t r = cudaStreamCreateWithFlags(&s.aux, cudaStreamNonBlocking);
+        if (r == cudaSuccess) r = cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming);
+        if (r == cudaSuccess) r = cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming);
+        s.status = r;
+    });
+    return s.status == cudaSuccess ? &s : nullptr;
+}
+
 // The driver's tensor-map encoder, looked up through the runtime once, so
 // the library has no link-time dependency on the driver library (it then
 // also loads on machines without a GPU driver, where nothing is launched).
@@ -1643,6 +1669,35 @@ bool encode_v_map(const PrefillParams& p, CUtensorMap* map) {
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The same tensor for the scan chain: box (64, 1, 64) with the 128-byte
+// swizzle, so two boxes per chunk land as the MN-major operand layout (line
+// t = token, 64 v per line).
+bool encode_v_map_sw128(const PrefillParams& p, CUtensorMap* map) {
+    const EncodeTiledFn encode = encode_tiled_fn();
+    if (encode == nullptr) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)kDim, (cuuint64_t)p.HV, (cuuint64_t)p.T};
+    const cuuint64_t strides[2] = {(cuuint64_t)kDim * 2, (cuuint64_t)p.HV * kDim * 2};
+    const cuuint32_t box[3] = {64u, 1u, (cuuint32_t)chunk::C};
+    const cuuint32_t estr[3] = {1u, 1u, 1u};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<__nv_bfloat16*>(p.v), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The output [T, HV, 128] bf16 for the scan chain's tensor stores of full
+// chunks: box (128, 1, 64), no swizzle (the staged tile is [token][v]).
+bool encode_o_map(const PrefillParams& p, CUtensorMap* map) {
+    const EncodeTiledFn encode = encode_tiled_fn();
+    if (encode == nullptr) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)kDim, (cuuint64_t)p.HV, (cuuint64_t)p.T};
+    const cuuint64_t strides[2] = {(cuuint64_t)kDim * 2, (cuuint64_t)p.HV * kDim * 2};
+    const cuuint32_t box[3] = {(cuuint32_t)kDim, 1u, (cuuint32_t)chunk::C};
+    const cuuint32_t estr[3] = {1u, 1u, 1u};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, p.out, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspace_bytes, cudaStream_t st) {
@@ -1650,28 +1705,66 @@ int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspa
     if (chunk_setup_current_device(num_sms) != cudaSuccess) return GDN_ERR_CUDA;
     unsigned char* ws = static_cast<unsigned char*>(workspace);
     const long long slots = chunk::ws_slots(p.N, p.T);
-    // Chain kernel: the split-path chain (four 32-wide V tiles per head, one
-    // CTA per SM) when all its CTAs fit in one wave, i.e. few (sequence,
-    // v-head) pairs such as one long sequence: four SMs then share each
-    // head's per-chunk work.  Otherwise the transposed chain, one CTA per
-    // (sequence, v-head).  Measured on B200 (ms): one 8192-token sequence at
-    // HV = 32: split 0.310, transposed 0.425; 16 sequences (8,184 tokens,
-    // HV = 32): split 0.374, transposed 0.267.  GDN_PREFILL_CHAIN = 2, 3 or
-    // 4 forces one of them (4: the scan over per-chunk transitions, which
-    // needs the larger workspace; all compute the same result within the
-    // operand rounding, and the tests run every chunked case through each).
+    // Chain kernel, by measurement on B200 (ms, CUDA events, L2 flushed):
+    //  * one sequence whose chain leaves at least half of the SMs free (2 HV <=
+    //    SMs): the scan chain (4), its prep running beside it on the free SMs
+    //    (HV = 32: 1,024 tokens 0.062 against 0.060 for the split chain, 4,096
+    //    0.156 / 0.169, 8,192 0.279 / 0.312; HV = 16, 8,192 tokens: 0.223 /
+    //    0.263; HV = 8: 0.215 / 0.224);
+    //  * otherwise the split-path chain (2: four 32-wide V tiles per head, one
+    //    CTA per SM) when all its CTAs fit in one wave, i.e. few (sequence,
+    //    v-head) pairs: four SMs share each head's per-chunk work;
+    //  * otherwise the transposed chain (3), one CTA per (sequence, v-head):
+    //    16 sequences of config 3 (8,184 tokens, HV = 32) 0.267 against 0.374
+    //    (split) and 0.337 (scan, whose prep finishes a sequence's chunks
+    //    only after the earlier sequences' and so cannot run ahead of
+    //    every chain at once).
+    // GDN_PREFILL_CHAIN = 2, 3 or 4 forces one of them (all compute the same
+    // result within the operand rounding; the tests run every chunked case
+    // through each); the scan chain needs the larger workspace layout.
     const long long pairs = (long long)p.N * p.HV;
     const bool scan_fits = workspace_bytes >= chunk::scan::workspace_bytes(p.N, p.T, p.HV);
-    int which = 4 * pairs <= num_sms ? 2 : 3;
+    int which = (p.N == 1 && 2 * pairs <= num_sms && scan_fits) ? 4 : 4 * pairs <= num_sms ? 2 : 3;
     const char* sel = getenv("GDN_PREFILL_CHAIN");
     if (sel && sel[0] >= '2' && sel[0] <= '4' && sel[1] == '\0' && (sel[0] != '4' || scan_fits)) which = sel[0] - '0';
     if (which == 4) {
-        CUtensorMap tmap_v;
-        if (!encode_v_map(p, &tmap_v)) return GDN_ERR_CUDA;
-        chunk::scan::prep::gdn_prefill_scan_prep_kernel<<<(unsigned)(slots * p.HV), chunk::scan::prep::NT,
-                                                          chunk::scan::prep::SMEM_BYTES, st>>>(p, ws);
-        chunk::scan::chain::gdn_prefill_scan_chain_kernel<<<(unsigned)pairs, chunk::scan::chain::NT,
-                                                            chunk::scan::chain::SMEM_BYTES, st>>>(p, ws, tmap_v);
+        CUtensorMap tmap_v, tmap_o;
+        if (!encode_v_map_sw128(p, &tmap_v) || !encode_o_map(p, &tmap_o)) return GDN_ERR_CUDA;
+        if (cudaMemsetAsync(ws + chunk::scan::records_bytes(p.N, p.T, p.HV), 0,
+                            chunk::scan::flags_bytes(p.N, p.T, p.HV), st) != cudaSuccess)
+            return GDN_ERR_CUDA;
+        const unsigned prep_grid = (unsigned)(slots * p.HV);
+        auto prep = [&](cudaStream_t s) {
+            chunk::scan::prep::gdn_prefill_scan_prep_kernel<<<prep_grid, chunk::scan::prep::NT,
+                                                              chunk::scan::prep::SMEM_BYTES, s>>>(p, ws);
+        };
+        auto chain = [&]() {
+            chunk::scan::chain::gdn_prefill_scan_chain_kernel<<<(unsigned)pairs, chunk::scan::chain::NT,
+                                                                chunk::scan::chain::SMEM_BYTES, st>>>(p, ws, tmap_v,
+                                                                                                      tmap_o);
+        };
+        // The chain waits on each record's ready flag, so the prep may run
+        // beside it: on a second stream, launched after the chain, when the
+        // chain's CTAs (one per SM) leave at least half of the SMs to the
+        // prep, whose CTAs never wait and therefore always finish.  Otherwise
+        // (many (sequence, v-head) pairs, or a stream being captured into a
+        // graph) the prep runs first on the caller's stream.
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) return GDN_ERR_CUDA;
+        ScanStreams* ss = (cap == cudaStreamCaptureStatusNone && 2 * pairs <= num_sms)
+                              ? scan_streams_current_device() : nullptr;
+        if (ss != nullptr) {
+            std::lock_guard<std::mutex> lock(ss->mu);
+            if (cudaEventRecord(ss->fork, st) != cudaSuccess) return GDN_ERR_CUDA;
+            chain();
+            if (cudaStreamWaitEvent(ss->aux, ss->fork, 0) != cudaSuccess) return GDN_ERR_CUDA;
+            prep(ss->aux);
+            if (cudaEventRecord(ss->join, ss->aux) != cudaSuccess || cudaStreamWaitEvent(st, ss->join, 0) != cudaSuccess)
+                return GDN_ERR_CUDA;
+        } else {
+            prep(st);
+            chain();
+        }
         return gdn_launch_status();
     }
     PrefillParams q = p;

@@ -25,18 +25,53 @@
 namespace scan {
 
 // Record of one (chunk, v-head) in the workspace, written by the prep and
-// read by the chain with one bulk copy; every tile is in the 128-byte-swizzled
-// K-major layout the chain's MMAs read (B operands):
-//   -Abar  rows k', columns k       128 x 128  32 KiB
-//   Et     rows k, columns token    128 x 64   16 KiB
-//   Qt     rows token, columns k     64 x 128  16 KiB
-//   Pt     rows token i, columns j   64 x 64    8 KiB
-//   e^{gamma_C} (fp32), padding                 16 B
-constexpr uint32_t REC_ABAR = 0, REC_E = 32768, REC_QT = 49152, REC_P = 65536, REC_DECAY = 73728;
+// read by the chain; both tiles are in the 128-byte-swizzled K-major layout
+// of the chain's B operands, with 192 rows so that one N = 192 product
+// yields the state update and the outputs together:
+//   [-Abar ; Qt]  rows 0-127: -Abar row k'; rows 128-191: Qt row (token);
+//                 columns k (two 64-column slabs of 24 KiB)     48 KiB
+//   [Et ; Pt]     rows 0-127: Et row k; rows 128-191: Pt row (token i);
+//                 columns token (j)                             24 KiB
+//   e^{gamma_C} (fp32), padding                                  16 B
+constexpr uint32_t REC_AQ = 0, REC_EP = 49152, REC_DECAY = 73728;
 constexpr uint32_t kRecBytes = 73744;
+constexpr uint32_t kRecRows = 192;
 
-__host__ __device__ inline size_t workspace_bytes(int N, int T, int HV) {
+// The records, then one ready flag (uint32) per record: the prep sets it
+// (release, device scope) once the record is written, the chain acquires it
+// before reading the record, so the two kernels may run concurrently.  The
+// host zeroes the flags before each launch pair.
+__host__ __device__ inline size_t records_bytes(int N, int T, int HV) {
     return (size_t)ws_slots(N, T) * HV * kRecBytes;
+}
+__host__ __device__ inline size_t flags_bytes(int N, int T, int HV) {
+    return ((size_t)ws_slots(N, T) * HV * 4 + 255) / 256 * 256;
+}
+__host__ __device__ inline size_t workspace_bytes(int N, int T, int HV) {
+    return records_bytes(N, T, HV) + flags_bytes(N, T, HV);
+}
+__device__ __forceinline__ unsigned int* ready_flag(const PrefillParams& p, const unsigned char* ws, long long slot,
+                                                    int hv) {
+    return reinterpret_cast<unsigned int*>(const_cast<unsigned char*>(ws) + records_bytes(p.N, p.T, p.HV)) +
+           (size_t)slot * p.HV + hv;
+}
+__device__ __forceinline__ unsigned int ld_acquire(const unsigned int* a) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+    return v;
+}
+// Bounded wait for a record's ready flag (acquire); false after ~kWaitBudget cycles.
+__device__ __forceinline__ bool wait_ready(const unsigned int* flag) {
+    if (ld_acquire(flag) != 0u) return true;
+    const long long t0 = clock64();
+    while (ld_acquire(flag) == 0u) {
+        if (clock64() - t0 > kWaitBudget) {
+            atomicOr(&g_device_status, kDevStatTimeout);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
 }
 
 // ============================================================================
@@ -176,29 +211,54 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
     if (!wait_mma(&mbar[0], 0)) goto done;
     umma::fence_after_sync();
 
-    // A = beta_i e^{gamma_i - gamma_j} k_i.k_j (j < i), rows 0-63 (warps 0, 1)
-    if (tid < 64) {
-        const int i = tid;
-        const float gi = sG[i], bi = sBeta[i];
+    // Both masks in one pass, each read from its own TMEM lanes:
+    //   A = beta_i e^{gamma_i - gamma_j} k_i.k_j (j < i), rows 0-63 (warps 0, 1),
+    //       into the strictly lower part of sA (whole float4 groups below the
+    //       diagonal, i.e. columns < ceil4(i));
+    //   P = scale e^{gamma_i - gamma_j} q_i.k_j (j <= i), rows 64-127 (warps 2, 3),
+    //       as f16 into the part of sA the solve never touches: P row i (i + 1
+    //       values) in row 63 - i from column ceil4(63 - i) on, which leaves
+    //       4 (i + 2) bytes of room (with the padding columns 64-67).
+    // P reaches its tile after the solve, once sA is free.
+    {
+        const int i = tid & 63;
+        const bool arow = tid < 64;
+        const float gi = sG[i];
+        const float coef = arow ? sBeta[i] : p.scale;
+        const int lim = arow ? i : i + 1;  // columns jj < lim are kept
+        unsigned char* prow = reinterpret_cast<unsigned char*>(sA + ix(63 - i, ((63 - i) + 3) & ~3));
 #pragma unroll 1
         for (int c16 = 0; c16 < C; c16 += 16) {
+            // the warp's rows are 32 * (warp % 2) .. + 31: blocks of columns
+            // past them are zero for all of its threads (a warp-uniform exit,
+            // as tcgen05.ld is executed by whole warps)
+            if (c16 > 32 * (warp & 1) + 31) break;
             float d[16], r[16];
             umma::tmem_ld16(tmem + lane_base + c16, d);
+            if (c16 >= lim) continue;
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
                 const int jj = c16 + e;
-                r[e] = (jj < i) ? bi * __expf(fminf(gi - sG[jj], 0.f)) * d[e] : 0.f;
+                r[e] = (jj < lim) ? coef * __expf(fminf(gi - sG[jj], 0.f)) * d[e] : 0.f;
             }
+            if (arow) {
 #pragma unroll
-            for (int e = 0; e < 16; e += 4)
-                *reinterpret_cast<float4*>(sA + ix(i, c16 + e)) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
+                for (int e = 0; e < 16; e += 4)
+                    if (c16 + e < i)
+                        *reinterpret_cast<float4*>(sA + ix(i, c16 + e)) = make_float4(r[e], r[e + 1], r[e + 2], r[e + 3]);
+            } else {
+                st_f16x8(prow, 2 * c16, r);
+                if (c16 + 8 < lim) st_f16x8(prow, 2 * c16 + 16, r + 8);
+            }
         }
     }
     __syncthreads();
     ::gdn::chunk::prep::solve_T(sA, sT, tid);
 
     // f16 copies of T: T diag(beta) -> rows 0-63 of [T ; P] (the B operand of
-    // MMA_P, read MN-major from those rows) and diag(f_K) T diag(beta) -> T1
+    // MMA_P, read MN-major from those rows) and diag(f_K) T diag(beta) -> T1;
+    // the P rows from their place in sA -> rows 64-127 of [T ; P].  Every
+    // thread reads its part first: the tiles overlay sA and sT.
     {
         const int i = tid >> 1, h = (tid & 1) * 32;  // row i, columns h..h+31
         float t[32];
@@ -216,7 +276,16 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
             }
         }
         const float fk = __expf(fminf(sG[C - 1] - sG[i], 0.f));
-        __syncthreads();  // T1 overwrites part of sT
+        // P row pi (threads 64-127): 8 chunks of 8 f16, chunks past the diagonal zero
+        const int pi = tid - 64;
+        uint4 pr[8];
+        if (tid >= 64) {
+            const unsigned char* prow = reinterpret_cast<const unsigned char*>(sA + ix(63 - pi, ((63 - pi) + 3) & ~3));
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                pr[c] = 8 * c <= pi ? *reinterpret_cast<const uint4*>(prow + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
+        }
+        __syncthreads();  // the tiles below overwrite sA and part of sT
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
             float x[8], y[8];
@@ -228,23 +297,10 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
             st_f16x8(sm + OFF_TP, umma::kmaj_off(i, h + c, 128), x);
             st_f16x8(sm + OFF_T1, umma::kmaj_off(i, h + c, 64), y);
         }
-    }
-    // P = scale e^{gamma_i - gamma_j} q_i.k_j (j <= i) -> rows 64-127 of [T ; P]
-    // (warps 2, 3 read TMEM lanes 64-127 of MMA_G)
-    if (tid >= 64) {
-        const int i = tid - 64;
-        const float gi = sG[i];
-#pragma unroll 1
-        for (int c16 = 0; c16 < C; c16 += 16) {
-            float d[16], r[16];
-            umma::tmem_ld16(tmem + lane_base + c16, d);
+        if (tid >= 64) {
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const int jj = c16 + e;
-                r[e] = (jj <= i) ? p.scale * __expf(fminf(gi - sG[jj], 0.f)) * d[e] : 0.f;
-            }
-            st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16, 128), r);
-            st_f16x8(sm + OFF_TP, umma::kmaj_off(64 + i, c16 + 8, 128), r + 8);
+            for (int c = 0; c < 8; ++c)
+                *reinterpret_cast<uint4*>(sm + OFF_TP + umma::kmaj_off(64 + pi, 8 * c, 128)) = pr[c];
         }
     }
     sync_for_mma();
@@ -270,8 +326,9 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
     if (!wait_mma(&mbar[1], 0)) goto done;
     umma::fence_after_sync();
 
-    // Pt (record) and Pt diag(e^gamma) (rows 128-191 of [E2 ; P2]); Et
-    // (record) and Et diag(e^gamma) (rows 0-127).  Thread = TMEM lane.
+    // Pt (record rows 128-191 of [Et ; Pt]) and Pt diag(e^gamma) (rows 128-191
+    // of [E2 ; P2]); Et (record rows 0-127) and Et diag(e^gamma) (rows 0-127).
+    // Thread = TMEM lane.
     {
         float eg[16];
         if (tid >= 64) {
@@ -282,8 +339,8 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
                 umma::tmem_ld16(tmem + lane_base + c16, d);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) eg[e] = __expf(sG[c16 + e]);
-                st_f16x8(rec + REC_P, umma::kmaj_off(i, c16, 64), d);
-                st_f16x8(rec + REC_P, umma::kmaj_off(i, c16 + 8, 64), d + 8);
+                st_f16x8(rec + REC_EP, umma::kmaj_off(128 + i, c16, kRecRows), d);
+                st_f16x8(rec + REC_EP, umma::kmaj_off(128 + i, c16 + 8, kRecRows), d + 8);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) d[e] *= eg[e];
                 st_f16x8(sm + OFF_EP, umma::kmaj_off(128 + i, c16, 192), d);
@@ -296,8 +353,8 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
             umma::tmem_ld16(tmem + lane_base + 64 + c16, d);
 #pragma unroll
             for (int e = 0; e < 16; ++e) eg[e] = __expf(sG[c16 + e]);
-            st_f16x8(rec + REC_E, umma::kmaj_off(tid, c16, 128), d);
-            st_f16x8(rec + REC_E, umma::kmaj_off(tid, c16 + 8, 128), d + 8);
+            st_f16x8(rec + REC_EP, umma::kmaj_off(tid, c16, kRecRows), d);
+            st_f16x8(rec + REC_EP, umma::kmaj_off(tid, c16 + 8, kRecRows), d + 8);
 #pragma unroll
             for (int e = 0; e < 16; ++e) d[e] *= eg[e];
             st_f16x8(sm + OFF_EP, umma::kmaj_off(tid, c16, 192), d);
@@ -319,7 +376,7 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
     }
     if (!wait_mma(&mbar[2], 0)) goto done;
     umma::fence_after_sync();
-    // -Abar row k' = tid -> record (two 64-column slabs)
+    // -Abar row k' = tid -> record rows 0-127 of [-Abar ; Qt]
 #pragma unroll 1
     for (int c32 = 0; c32 < kDim; c32 += 32) {
         float d[32];
@@ -327,7 +384,7 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
 #pragma unroll
         for (int e = 0; e < 32; ++e) d[e] = -d[e];
 #pragma unroll
-        for (int e = 0; e < 32; e += 8) st_f16x8(rec + REC_ABAR, umma::kmaj_off(tid, c32 + e, 128), d + e);
+        for (int e = 0; e < 32; e += 8) st_f16x8(rec + REC_AQ, umma::kmaj_off(tid, c32 + e, kRecRows), d + e);
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -345,7 +402,7 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
     }
     if (!wait_mma(&mbar[3], 0)) goto done;
     umma::fence_after_sync();
-    // Qt row i = scale e^{gamma_i} q_i - (Pt diag(e^gamma) K)_i -> record
+    // Qt row i = scale e^{gamma_i} q_i - (Pt diag(e^gamma) K)_i -> record rows 128-191 of [-Abar ; Qt]
     if (tid >= 64) {
         const int i = tid - 64;
         const float fq = p.scale * __expf(sG[i]);
@@ -364,9 +421,16 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
                     x[2 * u] = fmaf(fq, q2.x, -d[e + 2 * u]);
                     x[2 * u + 1] = fmaf(fq, q2.y, -d[e + 2 * u + 1]);
                 }
-                st_f16x8(rec + REC_QT, umma::kmaj_off(i, c32 + e, 64), x);
+                st_f16x8(rec + REC_AQ, umma::kmaj_off(128 + i, c32 + e, kRecRows), x);
             }
         }
+    }
+
+    // every thread's record writes, then the ready flag (release, device scope)
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(ready_flag(p, ws, s, hv)), "r"(1u) : "memory");
     }
 
 done:
@@ -377,30 +441,44 @@ done:
 
 }  // namespace prep
 
+
 // ============================================================================
 // chain: one CTA per (sequence, v-head), state transposed (state row v =
 // TMEM lane v, as the k-last storage S^T[v][k])
 // ============================================================================
-// Per chunk j, with the state's f16 copy SA_j = S_j^T and the v rows' f16
-// copy VA_j = V_j^T as A operands in tensor memory and the record's tiles as
-// B operands in shared memory:
-//   X2(j): X  = VA_j Et_j^T                 (issued as soon as VA_j is ready)
-//   X1(j): X += SA_j (-Abar_j)^T            (the one product on the critical path)
-//   O(j) : O  = SA_j Qt_j^T + VA_j Pt_j^T   (the chunk's outputs, [v][token])
-// and the state threads form S_{j+1}^T = e^{gamma_C} S_j^T + X in fp32
-// registers and its f16 copy for X1(j+1).
+// Per chunk j, with the state's f16 copy SA = S_j^T in tensor memory, the v
+// rows V_j (f16, MN-major: v contiguous) in shared memory as A operands, and
+// the record's two 192-row tiles as B operands, two groups of N = 192
+// products fill one accumulator [X | O] (128 + 64 columns):
+//   MMA_V(j): [X | O]  = V_j^T [Et ; Pt]^T       (issued as soon as V_j is in)
+//   MMA_S(j): [X | O] += SA [-Abar ; Qt]^T       (the critical path)
+// X = -Abar S_j + Et V_j (the state update) and O = Qt S_j + Pt V_j (the
+// chunk's outputs, [v][token]); the state threads then form S_{j+1}^T =
+// e^{gamma_C} S_j^T + X in fp32 registers and its f16 copy for MMA_S(j+1).
+// Twelve products and four waits per chunk for the one issuing thread.
+//
+// Tensor memory: [X | O] twice (chunk j in j % 2, 2 x 192 columns) and SA
+// (64 columns: the next copy is written only after MMA_S(j) completes).
+//
+// Shared memory: the record's two tiles in rings of two ([-Abar ; Qt] 48 KiB,
+// [Et ; Pt] 24 KiB, both freed when MMA_S(j) completes; e^{gamma_C} is read
+// from global memory by the state threads), the v rows in a
+// ring of four (two 64-wide TMA boxes with the 128-byte swizzle per chunk:
+// the MN-major operand layout; converted from bf16 to f16 in place, tokens
+// past the chunk's end zeroed), and one output tile staged as bf16 rows so
+// that the stores are coalesced 16-byte rows (one 2-byte store per token and
+// thread measured ~3,700 cycles per chunk: it was the step's bound).
 //
 // Warp roles (TMEM lane quarter = warp % 4, thread = state row v = 32 * quarter + lane):
 //   warps 0-7    the state: fp32 in registers, 64 columns k per thread
 //                (warps 0-3 columns 0-63, warps 4-7 columns 64-127);
-//                checkpoints and the final state;
-//   warps 8-11   the outputs (64 tokens of row v per thread, bf16 stores,
-//                32 consecutive v per warp store) and the f16 A copy of
-//                the next chunks' v rows;
+//                checkpoints and the final state; after each state update,
+//                the f16 conversion of the v rows (two chunks ahead);
+//   warps 8-11   the outputs: staged as bf16 rows, one TMA tensor store per
+//                full chunk (16-byte thread stores for a partial one);
 //   warp 12      one thread issues every MMA, in one order;
-//   warp 13      one thread loads the records (one bulk copy per chunk, two
-//                buffers) and the v rows (one TMA tensor copy per chunk,
-//                three buffers).
+//   warp 13      one thread loads the two record tiles and the v rows
+//                (TMA tensor copies, four chunks ahead).
 namespace chain {
 
 constexpr int NT = 448;                  // 14 warps
@@ -408,32 +486,39 @@ constexpr int kSThreads = 256, kOThreads = 128;
 constexpr int kOBase = 256;
 constexpr int kIssuer = 384;             // warp 12, lane 0
 constexpr int kLoaderWarp = 13;
-constexpr int NB = 2;                    // record buffers (chunk i in i % 2)
-constexpr int NV = 3;                    // v-row buffers (chunk i in i % 3)
-constexpr uint32_t kRecStride = (kRecBytes + 1023) / 1024 * 1024;
-constexpr uint32_t kTileV = C * kDim * 2;  // 16 KiB, bf16 [token][v]
-constexpr uint32_t OFF_REC = 0;
-constexpr uint32_t OFF_V = NB * kRecStride;
-constexpr uint32_t SMEM_BYTES = OFF_V + NV * kTileV + 1024;
-static_assert(SMEM_BYTES <= 232448, "dynamic shared memory limit");
-static_assert(kRecStride % 1024 == 0 && OFF_V % 1024 == 0, "tile alignment");
-// no prep CTA fits beside a chain CTA, so the chain's 512 TMEM columns are
-// never contended
+constexpr int NA = 2;                    // [-Abar ; Qt] buffers (chunk i in i % 2)
+constexpr int NE = 2;                    // [Et ; Pt] buffers (chunk i in i % 2)
+constexpr int NV = 4;                    // v-row buffers (chunk i in i % 4)
+constexpr uint32_t kTileAQ = REC_EP - REC_AQ;      // 48 KiB
+constexpr uint32_t kTileEP = REC_DECAY - REC_EP;   // 24 KiB
+constexpr uint32_t kTileV = C * kDim * 2;          // 16 KiB: two MN-major 64-v blocks of 64 tokens
+constexpr uint32_t kTileO = C * kDim * 2;          // 16 KiB, bf16 [token][v]
+constexpr uint32_t OFF_AQ = 0;
+constexpr uint32_t OFF_EP = NA * kTileAQ;
+constexpr uint32_t OFF_V = OFF_EP + NE * kTileEP;
+constexpr uint32_t OFF_O = OFF_V + NV * kTileV;
+constexpr uint32_t SMEM_BYTES = OFF_O + kTileO + 1024;
+static_assert(SMEM_BYTES <= 232448 - 512, "dynamic shared memory limit (with the static barriers)");
+static_assert(kTileAQ % 1024 == 0 && kTileEP % 1024 == 0 && OFF_EP % 1024 == 0 && OFF_V % 1024 == 0 &&
+              OFF_O % 1024 == 0, "tile alignment");
+// no prep CTA fits beside a chain CTA, so the chain's TMEM columns are never contended
 static_assert(SMEM_BYTES + prep::SMEM_BYTES > 233472, "chain CTA alone on its SM");
-constexpr uint32_t TM_X = 0, TM_O = 128, TM_SA = 256, TM_VA = 384, TM_COLS = 512;
+constexpr uint32_t kXO = 192;            // [X | O] columns
+constexpr uint32_t TM_XO = 0, TM_SA = 2 * kXO, TM_COLS = 512;
+static_assert(TM_SA + 64 <= TM_COLS, "tensor memory budget");
+constexpr int kBarO = 1;                 // named barrier of the output warps
 
-constexpr uint32_t ID_N128 = umma::idesc_f16(128, 128, 0, 0, 0, 0);  // A (TMEM) x K-major B, N = 128
-constexpr uint32_t ID_N64 = umma::idesc_f16(128, 64, 0, 0, 0, 0);    // N = 64
+constexpr uint32_t ID_S = umma::idesc_f16(128, kXO, 0, 0, 0, 0);  // A (TMEM) x K-major B, N = 192
+constexpr uint32_t ID_V = umma::idesc_f16(128, kXO, 0, 0, 1, 0);  // MN-major A (shared) x K-major B
 
 struct Bars {
-    uint64_t ldR[NB];   // record of the chunk in buffer i % 2 landed
-    uint64_t ldV[NV];   // v rows of the chunk in buffer i % 3 landed
-    uint64_t vr[2];     // VA[i % 2] written (output threads)
-    uint64_t sr[2];     // SA[i % 2] written (state threads)
-    uint64_t mX;        // X1(i) complete
-    uint64_t xr;        // state threads have read X_i
-    uint64_t mO[2];     // O(i) complete
-    uint64_t od[2];     // output threads have read O[i % 2]
+    uint64_t ldA[NA];   // [-Abar ; Qt] of the chunk in buffer i % 2 landed
+    uint64_t ldE[NE];   // [Et ; Pt] of the chunk in buffer i % 2 landed
+    uint64_t ldV[NV];   // v rows of the chunk in buffer i % 4 landed
+    uint64_t vr[2];     // v rows of chunk i converted to f16 (state threads)
+    uint64_t sr;        // SA written (state threads), once per chunk
+    uint64_t mXO[2];    // MMA_S(i) complete: [X | O] of chunk i ready, its tiles, v rows and SA read
+    uint64_t xo[2];     // state and output threads have read [X | O][i % 2]
     uint64_t fin;       // drain of the issuer's MMAs
 };
 
@@ -445,10 +530,33 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
 }
+// TMA load of one chunk's v rows as two 64-wide boxes {64 v, 1 head, 64
+// tokens} of the [T, HV, 128] bf16 tensor (128-byte swizzle) at (64h, hv,
+// tc) -> half h of the tile: line t = token, the MN-major operand layout.
+// Rows at or past T are zero-filled.
+__device__ __forceinline__ void tma_load_v_sw(uint32_t dst, const CUtensorMap* map, int hv, int tc, uint64_t* bar) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        asm volatile(
+            "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+            :: "r"(dst + h * (kTileV / 2)), "l"(reinterpret_cast<uint64_t>(map)), "r"(64 * h), "r"(hv), "r"(tc),
+               "r"(umma::smem_u32(bar))
+            : "memory");
+}
+
+// TMA store of one full chunk's output rows (bf16 [token][v], 256-byte rows)
+// as the box {128 v, 1 head, 64 tokens} of the [T, HV, 128] output tensor at
+// (0, hv, tc), in a bulk group of the issuing thread.
+__device__ __forceinline__ void tma_store_o(const CUtensorMap* map, uint32_t src, int hv, int tc) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                 :: "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(hv), "r"(tc), "r"(src) : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
 
 __global__ void __launch_bounds__(NT, 1) gdn_prefill_scan_chain_kernel(const PrefillParams p,
                                                                      const unsigned char* ws,
-                                                                     const __grid_constant__ CUtensorMap tmap_v) {
+                                                                     const __grid_constant__ CUtensorMap tmap_v,
+                                                                     const __grid_constant__ CUtensorMap tmap_o) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -474,23 +582,22 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_scan_chain_kernel(const Pre
     }
     const int ni = (int)nchunks;
     auto chunk_len = [&](long long j) { const long long r = t1 - t0 - C * j; return (int)(r < C ? r : C); };
-    auto rec_of = [&](int i) { return sm + OFF_REC + (i % NB) * kRecStride; };
+    auto rec_g = [&](int i) { return ws + ((size_t)(slot0 + i) * p.HV + hv) * kRecBytes; };
 
     if (warp == 0) {
         umma::tmem_alloc(&tmem_base_sh, TM_COLS);
         umma::tmem_relinquish();
     }
     if (tid == 0) {
-        for (int b = 0; b < NB; ++b) umma::mbar_init(&B.ldR[b], 1);
         for (int b = 0; b < NV; ++b) umma::mbar_init(&B.ldV[b], 1);
         for (int b = 0; b < 2; ++b) {
-            umma::mbar_init(&B.vr[b], kOThreads);
-            umma::mbar_init(&B.sr[b], kSThreads);
-            umma::mbar_init(&B.mO[b], 1);
-            umma::mbar_init(&B.od[b], kOThreads);
+            umma::mbar_init(&B.ldA[b], 1);
+            umma::mbar_init(&B.ldE[b], 1);
+            umma::mbar_init(&B.vr[b], kSThreads);
+            umma::mbar_init(&B.mXO[b], 1);
+            umma::mbar_init(&B.xo[b], kSThreads + kOThreads);
         }
-        umma::mbar_init(&B.mX, 1);
-        umma::mbar_init(&B.xr, kSThreads);
+        umma::mbar_init(&B.sr, kSThreads);
         umma::mbar_init(&B.fin, 1);
         umma::fence_mbar_init();
         abort_flag = 0;
@@ -505,93 +612,121 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_scan_chain_kernel(const Pre
         if (failed || abort_flag) { failed = true; return; }
         if (!umma::mbar_wait(bar, parity, kWaitBudget)) { failed = true; abort_flag = 1; }
     };
-    int issuedR = 0, issuedV = 0;  // loads issued by the loader warp (chunks 0 .. issued - 1)
+    // loads issued by the loader warp (chunks 0 .. issued - 1)
+    int issuedA = 0, issuedE = 0, issuedV = 0;
 
     if (warp == kLoaderWarp) {
-        // ---- records (bulk, 2 buffers) and v rows (tensor copy, 3 buffers) ----
-        auto loadR = [&](int i) {
+        // ---- the record's two tiles (bulk copies) and the v rows (tensor copies) ----
+        auto load = [&](int i) {
+            bool ok = true;
             if (lane == 0) {
-                umma::mbar_arrive_expect_tx(&B.ldR[i % NB], kRecBytes);
-                umma::bulk_g2s(umma::smem_u32(rec_of(i)), ws + ((size_t)(slot0 + i) * p.HV + hv) * kRecBytes,
-                               kRecBytes, &B.ldR[i % NB]);
+                const unsigned char* r = rec_g(i);
+                // the record is complete (its prep may run beside this kernel);
+                // the bulk copies below read it through the async proxy
+                ok = wait_ready(ready_flag(p, ws, slot0 + i, hv));
+                if (ok) {
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                    umma::mbar_arrive_expect_tx(&B.ldE[i % NE], kTileEP);
+                    umma::bulk_g2s(umma::smem_u32(sm + OFF_EP + (i % NE) * kTileEP), r + REC_EP, kTileEP,
+                                   &B.ldE[i % NE]);
+                    umma::mbar_arrive_expect_tx(&B.ldA[i % NA], kTileAQ);
+                    umma::bulk_g2s(umma::smem_u32(sm + OFF_AQ + (i % NA) * kTileAQ), r + REC_AQ, kTileAQ,
+                                   &B.ldA[i % NA]);
+                }
             }
-            __syncwarp();
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (ok) {
+                issuedA = issuedE = i + 1;
+            } else {
+                failed = true;
+                abort_flag = 1;
+            }
         };
-        auto loadV = [&](int i) {
+        auto load_v = [&](int i) {  // chunk i's v rows into buffer i % 4
             if (lane == 0) {
                 umma::mbar_arrive_expect_tx(&B.ldV[i % NV], kTileV);
-                ::gdn::chunk::chain3::tma_load_v(umma::smem_u32(sm + OFF_V + (i % NV) * kTileV), &tmap_v, hv,
-                                                 (int)(t0 + C * (long long)i), &B.ldV[i % NV]);
+                tma_load_v_sw(umma::smem_u32(sm + OFF_V + (i % NV) * kTileV), &tmap_v, hv,
+                              (int)(t0 + C * (long long)i), &B.ldV[i % NV]);
             }
             __syncwarp();
+            issuedV = i + 1;
         };
-        for (int i = 0; i < NB && i < ni; ++i) loadR(i);
-        for (int i = 0; i < NV && i < ni; ++i) loadV(i);
-        issuedR = ni < NB ? ni : NB;
-        issuedV = ni < NV ? ni : NV;
-        for (int i = 0; i < ni && !failed; ++i) {
-            if (i + NV < ni) {  // v rows of chunk i copied into VA
-                wait(&B.vr[i % 2], ph(i / 2));
-                if (failed) break;
-                loadV(i + NV);
-                issuedV = i + NV + 1;
-            }
-            if (i + NB < ni) {
-                // record buffer of chunk i: every MMA of chunk i done, and the
-                // state threads have read its e^{gamma_C} (before S_{i+1})
-                wait(&B.mO[i % 2], ph(i / 2));
-                wait(&B.sr[(i + 1) % 2], ph((i + 1) / 2));
-                if (failed) break;
-                loadR(i + NB);
-                issuedR = i + NB + 1;
-            }
+        for (int i = 0; i < NV && i < ni; ++i) load_v(i);
+        for (int i = 0; i < NA && i < ni && !failed; ++i) load(i);
+        for (int i = 0; i + NA < ni && !failed; ++i) {
+            // MMA_V(i) and MMA_S(i) have read chunk i's tiles and v rows
+            wait(&B.mXO[i % 2], ph(i / 2));
+            if (failed) break;
+            if (i + NV < ni) load_v(i + NV);
+            load(i + NA);
         }
     } else if (tid == kIssuer) {
         // ---- the MMA issuer: descriptors built once, stepped by constant offsets ----
-        const uint64_t dR0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_REC), 128, 0);
-        const uint64_t dQ0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_REC + REC_QT), 64, 0);
-        const uint64_t dP0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_REC + REC_P), 64, 0);
-        for (int i = 0; i < ni && !failed; ++i) {
-            const uint32_t rb = (uint32_t)(i % NB) * kRecStride;
-            const uint32_t sa = tmem + TM_SA + (uint32_t)(i % 2) * 64, va = tmem + TM_VA + (uint32_t)(i % 2) * 32;
-            // X2(i): X = VA_i Et_i^T, once the record and VA_i are in and X_{i-1} has been read
-            wait(&B.ldR[i % NB], ph(i / NB));
+        const uint64_t dA0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_AQ), kRecRows, 0);
+        const uint64_t dE0 = umma::desc_kmaj(umma::smem_u32(sm + OFF_EP), kRecRows, 0);
+        const uint64_t dV0 = umma::desc_mnmaj(umma::smem_u32(sm + OFF_V), C, 0);
+        const uint32_t sa = tmem + TM_SA;
+        // MMA_V(i): [X | O][i % 2] = V_i^T [Et ; Pt]_i^T, once the tile and the
+        // converted v rows are in and [X | O] of chunk i - 2 has been read
+        auto mma_v = [&](int i) {
+            wait(&B.ldE[i % NE], ph(i / NE));
             wait(&B.vr[i % 2], ph(i / 2));
-            if (i > 0) wait(&B.xr, ph(i - 1));
-            if (failed) break;
+            if (i >= 2) wait(&B.xo[i % 2], ph((i - 2) / 2));
+            if (failed) return;
             umma::fence_after_sync();
+            const uint32_t d = tmem + TM_XO + (uint32_t)(i % 2) * kXO;
+            const uint32_t eb = (uint32_t)(i % NE) * kTileEP, vb = (uint32_t)(i % NV) * kTileV;
 #pragma unroll
             for (int k0 = 0; k0 < C; k0 += 16)
-                umma::mma_f16_ts(tmem + TM_X, va + k0 / 2, umma::desc_add(dR0, rb + REC_E + umma::koff_kmaj(128, k0)),
-                                 ID_N128, k0 > 0);
-            // X1(i): X += SA_i (-Abar_i)^T, once S_i's f16 copy is written
-            wait(&B.sr[i % 2], ph(i / 2));
+                umma::mma_f16(d, umma::desc_add(dV0, vb + umma::koff_mnmaj(k0)),
+                              umma::desc_add(dE0, eb + umma::koff_kmaj(kRecRows, k0)), ID_V, k0 > 0);
+        };
+        mma_v(0);
+        for (int i = 0; i < ni && !failed; ++i) {
+            // MMA_S(i): [X | O][i % 2] += SA [-Abar ; Qt]_i^T, once S_i's f16 copy is written
+            wait(&B.ldA[i % NA], ph(i / NA));
+            wait(&B.sr, ph(i));
             if (failed) break;
             umma::fence_after_sync();
+            const uint32_t d = tmem + TM_XO + (uint32_t)(i % 2) * kXO;
+            const uint32_t ab = (uint32_t)(i % NA) * kTileAQ;
 #pragma unroll
             for (int k0 = 0; k0 < kDim; k0 += 16)
-                umma::mma_f16_ts(tmem + TM_X, sa + k0 / 2, umma::desc_add(dR0, rb + umma::koff_kmaj(128, k0)),
-                                 ID_N128, true);
-            umma::mma_commit(&B.mX);
-            // O(i) = SA_i Qt_i^T + VA_i Pt_i^T, once O[i % 2] has been read (chunk i - 2)
-            if (i >= 2) wait(&B.od[i % 2], ph((i - 2) / 2));
-            if (failed) break;
-            umma::fence_after_sync();
-            const uint32_t od = tmem + TM_O + (uint32_t)(i % 2) * 64;
-#pragma unroll
-            for (int k0 = 0; k0 < kDim; k0 += 16)
-                umma::mma_f16_ts(od, sa + k0 / 2, umma::desc_add(dQ0, rb + umma::koff_kmaj(64, k0)), ID_N64, k0 > 0);
-#pragma unroll
-            for (int k0 = 0; k0 < C; k0 += 16)
-                umma::mma_f16_ts(od, va + k0 / 2, umma::desc_add(dP0, rb + umma::koff_kmaj(64, k0)), ID_N64, true);
-            umma::mma_commit(&B.mO[i % 2]);
+                umma::mma_f16_ts(d, sa + k0 / 2, umma::desc_add(dA0, ab + umma::koff_kmaj(kRecRows, k0)), ID_S,
+                                 true);
+            umma::mma_commit(&B.mXO[i % 2]);
+            if (i + 1 < ni) mma_v(i + 1);
         }
         // drain: every MMA issued here completes before the CTA exits
         umma::mma_commit(&B.fin);
         if (!umma::mbar_wait(&B.fin, 0, kWaitBudget)) failed = true;
     } else if (warp < 8) {
-        // ---- the state: row v, columns c0 .. c0 + 63, fp32 in registers ----
+        // ---- the state: row v, columns c0 .. c0 + 63, fp32 in registers;
+        // off the critical path, the f16 conversion of the v rows (two
+        // chunks ahead) ----
         const int c0 = 64 * (warp >> 2);
+        // chunk i's v rows -> f16 in place; tokens past the chunk's end are
+        // zero (line t of each 64-v block is token t)
+        auto convert_v = [&](int i) {
+            wait(&B.ldV[i % NV], ph(i / NV));
+            if (failed) return;
+            const int len = chunk_len(i);
+            uint4* tile = reinterpret_cast<uint4*>(sm + OFF_V + (i % NV) * kTileV);
+#pragma unroll
+            for (int it = 0; it < (int)(kTileV / 16 / kSThreads); ++it) {
+                const int idx = tid + it * kSThreads;
+                const int t = (idx >> 3) & 63;
+                float x[8];
+                unpack_bf16x8(tile[idx], x);
+                if (t >= len) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) x[e] = 0.f;
+                }
+                st_f16x8(reinterpret_cast<unsigned char*>(tile + idx), 0, x);
+            }
+            umma::fence_proxy_async_smem();  // generic writes -> the MMA's operand reads
+            arrive(&B.vr[i % 2]);
+        };
         float s[64];
         {
             const float* srow = p.state ? p.state + state_off + (size_t)v * kDim + c0 : nullptr;
@@ -605,21 +740,36 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_scan_chain_kernel(const Pre
             for (int e = 0; e < 32; ++e) h[e] = pack_f16x2(s[2 * e], s[2 * e + 1]);
             umma::tmem_st32_u32(tl + TM_SA + c0 / 2, h);
             umma::fence_before_sync();
-            arrive(&B.sr[0]);
+            arrive(&B.sr);
         }
+        convert_v(0);
+        if (ni > 1) convert_v(1);
+        // e^{gamma_C} of each chunk straight from the record in global memory
+        // (after acquiring its ready flag), one chunk ahead.
+        // The state threads wait on no barrier of the record tiles: they are
+        // refilled as soon as MMA_S is done, and a thread held up by its
+        // checkpoint stores could then see a barrier two phases ahead.
+        auto decay_of = [&](int i) {
+            if (!wait_ready(ready_flag(p, ws, slot0 + i, hv))) { failed = true; abort_flag = 1; return 0.f; }
+            float d;
+            asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(d) : "l"(rec_g(i) + REC_DECAY) : "memory");
+            return d;
+        };
+        float decay_next = decay_of(0);
         for (int i = 0; i < ni && !failed; ++i) {
-            wait(&B.mX, ph(i));
-            wait(&B.ldR[i % NB], ph(i / NB));
+            const float decay = decay_next;
+            if (i + 1 < ni) decay_next = decay_of(i + 1);
+            wait(&B.mXO[i % 2], ph(i / 2));
             if (failed) break;
             umma::fence_after_sync();
-            const float decay = *reinterpret_cast<const float*>(rec_of(i) + REC_DECAY);
+            const uint32_t x0 = tl + TM_XO + (uint32_t)(i % 2) * kXO + c0;
 #pragma unroll
             for (int hh = 0; hh < 64; hh += 32) {  // two 32-column halves keep fewer registers live
                 float x[32];
-                umma::tmem_ld32(tl + TM_X + c0 + hh, x);
+                umma::tmem_ld32(x0 + hh, x);
                 if (hh == 32) {
                     umma::fence_before_sync();
-                    arrive(&B.xr);
+                    arrive(&B.xo[i % 2]);
                 }
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
@@ -628,6 +778,16 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_scan_chain_kernel(const Pre
                     s[hh + e] = r.x; s[hh + e + 1] = r.y;
                 }
             }
+            if (i + 1 < ni) {  // MMA_S(i) has read SA: the next copy replaces it
+                uint32_t h[32];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) h[e] = pack_f16x2(s[2 * e], s[2 * e + 1]);
+                umma::tmem_st32_u32(tl + TM_SA + c0 / 2, h);
+                umma::fence_before_sync();
+                arrive(&B.sr);
+            }
+            // the v rows of chunk i + 2 for MMA_V(i + 2)
+            if (i + 2 < ni) convert_v(i + 2);
             const long long done_tok = C * (long long)(i + 1);
             if (p.ckpt != nullptr && chunk_len(i) == C && done_tok % p.ckpt_every == 0) {
                 float* cd = ckpt_dst(p, n, hv, done_tok);
@@ -638,14 +798,6 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_scan_chain_kernel(const Pre
                                make_float4(s[e], s[e + 1], s[e + 2], s[e + 3]));
                 }
             }
-            if (i + 1 < ni) {
-                uint32_t h[32];
-#pragma unroll
-                for (int e = 0; e < 32; ++e) h[e] = pack_f16x2(s[2 * e], s[2 * e + 1]);
-                umma::tmem_st32_u32(tl + TM_SA + (uint32_t)((i + 1) % 2) * 64 + c0 / 2, h);
-                umma::fence_before_sync();
-                arrive(&B.sr[(i + 1) % 2]);
-            }
         }
         if (!failed) {  // the final state, fp32 k-last
             float* drow = p.new_state + state_off + (size_t)v * kDim + c0;
@@ -654,62 +806,69 @@ __global__ void __launch_bounds__(NT, 1) gdn_prefill_scan_chain_kernel(const Pre
                 __stcs(reinterpret_cast<float4*>(drow + e), make_float4(s[e], s[e + 1], s[e + 2], s[e + 3]));
         }
     } else if (warp < 12) {
-        // ---- outputs and the f16 copies of the v rows ----
-        // VA_i[v][t] = v rows of chunk i (f16, pairs of tokens per 32-bit
-        // column); tokens past the chunk's end are zero
-        auto copy_v = [&](int i) {
-            wait(&B.ldV[i % NV], ph(i / NV));
-            if (failed) return;
-            const int len = chunk_len(i);
-            const unsigned short* col = reinterpret_cast<const unsigned short*>(sm + OFF_V + (i % NV) * kTileV) + v;
-            uint32_t h[32];
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const float lo = 2 * e < len ? __uint_as_float((uint32_t)col[(2 * e) * kDim] << 16) : 0.f;
-                const float hi = 2 * e + 1 < len ? __uint_as_float((uint32_t)col[(2 * e + 1) * kDim] << 16) : 0.f;
-                h[e] = pack_f16x2(lo, hi);
-            }
-            umma::tmem_st32_u32(tl + TM_VA + (uint32_t)(i % 2) * 32, h);
-            umma::fence_before_sync();
-            arrive(&B.vr[i % 2]);
-        };
-        copy_v(0);
-        if (ni > 1) copy_v(1);
-        for (int i = 0; i < ni && !failed; ++i) {
+        // ---- the outputs ----
+        // Every exit from this role's loop is decided together (named barrier
+        // with an or of the failures), so no output thread is left at a
+        // barrier that the others have abandoned.
+        const int o = tid - kOBase;
+        const bool olead = o == 0;
+        unsigned short* otile = reinterpret_cast<unsigned short*>(sm + OFF_O);
+        for (int i = 0; i < ni; ++i) {
             const long long tc = t0 + C * (long long)i;
             const int len = chunk_len(i);
-            wait(&B.mO[i % 2], ph(i / 2));
-            if (failed) break;
+            wait(&B.mXO[i % 2], ph(i / 2));
+            if (olead) umma::bulk_wait_read0();  // the previous chunk's TMA store has read the tile
+            // orders that (and the previous chunk's thread stores) before the writes below
+            if (::gdn::chunk::chain3::group_sync_or(kBarO, kOThreads, failed)) break;
             umma::fence_after_sync();
-            float o[64];
             {
-                float oa[32], ob[32];
-                umma::tmem_ld32x2(tl + TM_O + (uint32_t)(i % 2) * 64, tl + TM_O + (uint32_t)(i % 2) * 64 + 32, oa, ob);
+                const uint32_t o0 = tl + TM_XO + (uint32_t)(i % 2) * kXO + 128;
 #pragma unroll
-                for (int e = 0; e < 32; ++e) { o[e] = oa[e]; o[32 + e] = ob[e]; }
+                for (int hh = 0; hh < 64; hh += 32) {
+                    float ov[32];
+                    umma::tmem_ld32(o0 + hh, ov);
+                    if (hh == 32) {
+                        umma::fence_before_sync();
+                        arrive(&B.xo[i % 2]);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        otile[(hh + e) * kDim + v] = __bfloat16_as_ushort(__float2bfloat16_rn(ov[e]));
+                }
             }
-            umma::fence_before_sync();
-            arrive(&B.od[i % 2]);
-            // VA[i % 2] is free (X2(i) and O(i) are done): the v rows of chunk i + 2
-            if (i + 2 < ni) copy_v(i + 2);
-            // a warp stores 32 consecutive v of one token row per instruction
-            __nv_bfloat16* op = p.out + ((size_t)tc * p.HV + hv) * kDim + v;
-            const size_t stride = (size_t)p.HV * kDim;
-#pragma unroll
-            for (int t = 0; t < 64; ++t)
-                if (t < len) op[(size_t)t * stride] = __float2bfloat16_rn(o[t]);
+            umma::fence_proxy_async_smem();  // the staged rows -> the TMA store
+            if (::gdn::chunk::chain3::group_sync_or(kBarO, kOThreads, failed)) break;
+            if (len == C) {
+                // a full chunk: one tensor store of its 64 rows
+                if (olead) tma_store_o(&tmap_o, umma::smem_u32(otile), hv, (int)tc);
+            } else {
+                // the sequence's last, partial chunk: the rows past its end
+                // belong to the next sequence, so only rows < len are stored
+#pragma unroll 1
+                for (int c = o; c < C * 16; c += kOThreads) {
+                    const int r = c >> 4, q = c & 15;
+                    if (r < len)
+                        __stcs(reinterpret_cast<uint4*>(p.out + ((size_t)(tc + r) * p.HV + hv) * kDim) + q,
+                               reinterpret_cast<const uint4*>(otile + r * kDim)[q]);
+                }
+            }
         }
+        if (olead) umma::bulk_wait_read0();  // the tile stays in shared memory until the last store has read it
     }
 
     // ---- exit: copies in flight land first ----
     umma::fence_before_sync();
     failed = __syncthreads_or(failed) || abort_flag;
-    if (failed && warp == kLoaderWarp) {
-        if (lane == 0) atomicOr(&g_device_status, kDevStatTimeout);
-        for (int i = (issuedR > NB ? issuedR - NB : 0); i < issuedR; ++i)
-            umma::mbar_wait(&B.ldR[i % NB], ph(i / NB), kWaitBudget);
-        for (int i = (issuedV > NV ? issuedV - NV : 0); i < issuedV; ++i)
-            umma::mbar_wait(&B.ldV[i % NV], ph(i / NV), kWaitBudget);
+    if (failed) {
+        if (tid == 0) atomicOr(&g_device_status, kDevStatTimeout);
+        if (warp == kLoaderWarp) {
+            for (int i = (issuedA > NA ? issuedA - NA : 0); i < issuedA; ++i) {
+                umma::mbar_wait(&B.ldA[i % NA], ph(i / NA), kWaitBudget);
+                umma::mbar_wait(&B.ldE[i % NE], ph(i / NE), kWaitBudget);
+            }
+            for (int i = (issuedV > NV ? issuedV - NV : 0); i < issuedV; ++i)
+                umma::mbar_wait(&B.ldV[i % NV], ph(i / NV), kWaitBudget);
+        }
     }
     __syncthreads();
     if (warp == 0) umma::tmem_dealloc(tmem, TM_COLS);
