@@ -800,7 +800,7 @@ def bench_ours(args, rank, world, local):
             "roofline": {"bound": "tensor", "achieved": round(pre_achieved, 3),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(pre_achieved / peaks["bf16_tflops"], 5),
-                         "traffic": profile_traffic("gdn_prefill_T8192_ncu.txt"),
+                         "traffic": profile_traffic("gdn_prefill_scan_T8192_ncu.txt"),
                          "alg_flops_per_launch": pre_flops, "peak_src": peaks["src"]},
             "e2e": {"value": round(PREFILL_T * world / (pe2e_step_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": p_h2d, "d2h_bytes_per_step": p_d2h,

@@ -124,10 +124,14 @@ size_t gdn_decode_host_workspace_bytes(int B, int H, int HV);
  * new_state may equal state (in-place update).
  *
  * T >= GDN_PREFILL_CHUNK_MIN (environment, default 128) runs the chunked
- * tensor-core kernels, which need a device workspace of at least
- * gdn_prefill_workspace_bytes(N, T, H, HV) bytes (16-byte aligned; its contents
- * on entry do not matter); shorter batches run the token-serial kernel and
- * need none (workspace may then be NULL).
+ * tensor-core kernels, which need a device workspace (16-byte aligned; its
+ * contents on entry do not matter) of gdn_prefill_workspace_bytes(N, T, H, HV)
+ * bytes; a smaller one of at least (floor(T/64) + N) * (17,424 * HV + 49,152 * H)
+ * bytes restricts the call to the kernels whose layout fits it.  Shorter
+ * batches run the token-serial kernel and need none (workspace may then be
+ * NULL).  For one sequence the call may run part of its work on two library
+ * streams forked from `stream` and joined back into it by events (created on
+ * the first such call on a device); the caller sees only `stream`.
  */
 int gdn_prefill_fwd(const void *q, const void *k, const void *v, const float *state,
                     const float *A_log, const void *a, const float *dt_bias, const void *b,
@@ -214,11 +218,13 @@ size_t gdn_prefill_host_workspace_bytes(int N, int T, int H, int HV, int segment
 /*
  * Workspace bytes gdn_prefill_fwd needs for (N, T, H, HV): 0 when the call
  * will take the token-serial kernel.  For each of floor(T/64) + N chunk slots
- * the chunked kernels keep, per v-head, the chunk's [T ; P'] operand tile and
- * gates (17,424 bytes) and, per q/k head, its f16 [K ; Q] operand tile
- * (32,768 bytes) and its cross-Gram tile [K ; Q] K_prev^T (16,384 bytes).
- * No counterpart in the reference, whose AITER kernels allocate their
- * intermediates with torch.
+ * the chunked kernels keep either, per v-head, the chunk's [T ; P'] operand
+ * tile and gates (17,424 bytes) and, per q/k head, its f16 [K ; Q] operand
+ * tile (32,768 bytes) and its cross-Gram tile [K ; Q] K_prev^T (16,384 bytes);
+ * or (the scan kernels) per v-head the chunk's state-transition record
+ * (73,744 bytes) and a 4-byte ready flag (the flags rounded up to 256 bytes).
+ * The value is the larger of the two layouts.  No counterpart in the
+ * reference, whose AITER kernels allocate their intermediates with torch.
  */
 size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV);
 
@@ -237,12 +243,12 @@ size_t gdn_prefill_workspace_bytes(int N, int T, int H, int HV);
  * holds those 16 MiB until the process exits.  It calls no cudaMalloc,
  * cudaFree or other allocating routine.
  *
- * Limit: gdn_prefill_workspace_bytes(N, T, H, HV) must not exceed 16 MiB
- * (16,777,216 bytes), i.e. (floor(T/64) + N) * (17,424 * HV + 49,152 * H)
- * <= 16 MiB when the chunked kernels run (for example T < 768 at N = 1,
- * H = 16, HV = 32, or T < 2,944 at N = 4, H = 4, HV = 8); larger problems
- * return GDN_ERR_TOO_LARGE before anything is launched.  Problems below the
- * chunk threshold need no scratch at all.
+ * Limit: (floor(T/64) + N) * (17,424 * HV + 49,152 * H) must not exceed
+ * 16 MiB (16,777,216 bytes) when the chunked kernels run (for example T < 768
+ * at N = 1, H = 16, HV = 32, or T < 2,944 at N = 4, H = 4, HV = 8); larger
+ * problems return GDN_ERR_TOO_LARGE before anything is launched.  Problems
+ * below the chunk threshold need no scratch at all.  Every launch goes to
+ * `stream` (no library stream or event is created).
  *
  * The first call on a device looks up the scratch array's device address
  * with that device current (the device of `stream` must be the current

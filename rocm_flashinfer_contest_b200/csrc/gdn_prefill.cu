@@ -57,7 +57,7 @@ static int prefill_impl(const void* q, const void* k, const void* v, const float
                         const void* cu_seqlens, int cu_seqlens_is_int64, int N, int T, float scale,
                         int H, int HV, int K, int V, void* out, float* new_state, float* ckpt,
                         const int64_t* ckpt_cu, long long ckpt_total, int ckpt_every, int flags,
-                        void* workspace, size_t workspace_bytes, void* stream) {
+                        void* workspace, size_t workspace_bytes, void* stream, bool aux_streams = true) {
     if (N < 0 || T < 0 || H <= 0 || HV <= 0) return GDN_ERR_INVALID;
     if (flags & ~GDN_PREFILL_QK_L2NORM) return GDN_ERR_INVALID;
     if (ckpt != nullptr && (ckpt_every <= 0 || ckpt_every % 64 != 0 || !ckpt_cu || ckpt_total < 0))
@@ -105,12 +105,22 @@ static int prefill_impl(const void* q, const void* k, const void* v, const float
         const size_t need = gdn::prefill_workspace_bytes_split(N, T, H, HV);
         if (!workspace || workspace_bytes < need) return GDN_ERR_INVALID;
         if (!gdn_aligned(workspace, 16)) return GDN_ERR_ALIGN;
-        return gdn::launch_prefill_chunk(p, workspace, workspace_bytes, st);
+        return gdn::launch_prefill_chunk(p, workspace, workspace_bytes, st, aux_streams);
     } else {
         gdn::launch_prefill_recurrent(p, st);
     }
     return gdn_launch_status();
 }
+
+namespace gdn {
+int prefill_fwd_one_stream(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+                           const void* a, const float* dt_bias, const void* b, const void* cu_seqlens,
+                           int cu_seqlens_is_int64, int N, int T, float scale, int H, int HV, int K, int V,
+                           void* out, float* new_state, void* workspace, size_t workspace_bytes, void* stream) {
+    return prefill_impl(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64, N, T, scale, H, HV, K,
+                        V, out, new_state, nullptr, nullptr, 0, 0, 0, workspace, workspace_bytes, stream, false);
+}
+}  // namespace gdn
 
 extern "C" int gdn_prefill_fwd(const void* q, const void* k, const void* v, const float* state,
                                const float* A_log, const void* a, const float* dt_bias,

@@ -1594,8 +1594,13 @@ cudaError_t chunk_setup_current_device(int& num_sms) {
             r = cudaFuncSetAttribute(chunk::chain3::gdn_prefill_chunk_chain3_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::chain3::SMEM_BYTES);
         if (r == cudaSuccess)
-            r = cudaFuncSetAttribute(chunk::scan::prep::gdn_prefill_scan_prep_kernel,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::scan::prep::SMEM_BYTES);
+            r = cudaFuncSetAttribute(chunk::scan::prep::gdn_prefill_scan_prep_kernel<1>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)chunk::scan::prep::smem_bytes<1>());
+        if (r == cudaSuccess)
+            r = cudaFuncSetAttribute(chunk::scan::prep::gdn_prefill_scan_prep_kernel<2>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)chunk::scan::prep::smem_bytes<2>());
         if (r == cudaSuccess)
             r = cudaFuncSetAttribute(chunk::scan::chain::gdn_prefill_scan_chain_kernel,
                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chunk::scan::chain::SMEM_BYTES);
@@ -1609,15 +1614,16 @@ cudaError_t chunk_setup_current_device(int& num_sms) {
     return s.status;
 }
 
-// The scan path's second stream, per device: its prep runs there beside the
-// chain (fork and join by events), created on first use with that device
-// current.  The mutex keeps one call's record / wait / launch sequence whole
-// when host threads share a device.
+// The scan path's streams, per device: the prep runs on a low-priority
+// stream and the chain on a high-priority one, both forked from the caller's
+// stream and joined back into it by events; created on first use with that
+// device current.  The mutex keeps one call's record / wait / launch sequence
+// whole when host threads share a device.
 struct ScanStreams {
     std::once_flag once;
     cudaError_t status = cudaErrorNotReady;
-    cudaStream_t aux = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
+    cudaStream_t lo = nullptr, hi = nullptr;
+    cudaEvent_t fork = nullptr, join_lo = nullptr, join_hi = nullptr;
     std::mutex mu;
 };
 ScanStreams g_scan_streams[kMaxDevices];
@@ -1627,9 +1633,13 @@ ScanStreams* scan_streams_current_device() {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
     ScanStreams& s = g_scan_streams[dev];
     std::call_once(s.once, [&]() {
-        cudaError_t r = cudaStreamCreateWithFlags(&s.aux, cudaStreamNonBlocking);
+        int least = 0, greatest = 0;
+        cudaError_t r = cudaDeviceGetStreamPriorityRange(&least, &greatest);
+        if (r == cudaSuccess) r = cudaStreamCreateWithPriority(&s.lo, cudaStreamNonBlocking, least);
+        if (r == cudaSuccess) r = cudaStreamCreateWithPriority(&s.hi, cudaStreamNonBlocking, greatest);
         if (r == cudaSuccess) r = cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming);
-        if (r == cudaSuccess) r = cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming);
+        if (r == cudaSuccess) r = cudaEventCreateWithFlags(&s.join_lo, cudaEventDisableTiming);
+        if (r == cudaSuccess) r = cudaEventCreateWithFlags(&s.join_hi, cudaEventDisableTiming);
         s.status = r;
     });
     return s.status == cudaSuccess ? &s : nullptr;
@@ -1700,7 +1710,8 @@ bool encode_o_map(const PrefillParams& p, CUtensorMap* map) {
 
 }  // namespace
 
-int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspace_bytes, cudaStream_t st,
+                         bool aux_streams) {
     int num_sms = 0;
     if (chunk_setup_current_device(num_sms) != cudaSuccess) return GDN_ERR_CUDA;
     unsigned char* ws = static_cast<unsigned char*>(workspace);
@@ -1733,37 +1744,48 @@ int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspa
         if (cudaMemsetAsync(ws + chunk::scan::records_bytes(p.N, p.T, p.HV), 0,
                             chunk::scan::flags_bytes(p.N, p.T, p.HV), st) != cudaSuccess)
             return GDN_ERR_CUDA;
-        const unsigned prep_grid = (unsigned)(slots * p.HV);
+        // the two v-heads of a q/k head share one prep CTA when HV / H is even
+        const bool pair = p.rep % 2 == 0;
         auto prep = [&](cudaStream_t s) {
-            chunk::scan::prep::gdn_prefill_scan_prep_kernel<<<prep_grid, chunk::scan::prep::NT,
-                                                              chunk::scan::prep::SMEM_BYTES, s>>>(p, ws);
+            if (pair)
+                chunk::scan::prep::gdn_prefill_scan_prep_kernel<2><<<(unsigned)(slots * p.HV / 2), 256,
+                                                                     chunk::scan::prep::smem_bytes<2>(), s>>>(p, ws);
+            else
+                chunk::scan::prep::gdn_prefill_scan_prep_kernel<1><<<(unsigned)(slots * p.HV), 128,
+                                                                     chunk::scan::prep::smem_bytes<1>(), s>>>(p, ws);
         };
-        auto chain = [&]() {
+        auto chain = [&](cudaStream_t s) {
             chunk::scan::chain::gdn_prefill_scan_chain_kernel<<<(unsigned)pairs, chunk::scan::chain::NT,
-                                                                chunk::scan::chain::SMEM_BYTES, st>>>(p, ws, tmap_v,
-                                                                                                      tmap_o);
+                                                                chunk::scan::chain::SMEM_BYTES, s>>>(p, ws, tmap_v,
+                                                                                                     tmap_o);
         };
         // The chain waits on each record's ready flag, so the prep may run
-        // beside it: on a second stream, launched after the chain, when the
-        // chain's CTAs (one per SM) leave at least half of the SMs to the
-        // prep, whose CTAs never wait and therefore always finish.  Otherwise
-        // (many (sequence, v-head) pairs, or a stream being captured into a
-        // graph) the prep runs first on the caller's stream.
+        // beside it.  The prep is launched first, on a low-priority stream,
+        // and never waits: the results are right whether or not the two
+        // kernels overlap (a profiler or CUDA_LAUNCH_BLOCKING runs them one
+        // after the other).  The chain follows on a high-priority stream, so
+        // its CTAs (one per SM) take the first SMs the prep's CTAs free.
+        // This pays when the chain leaves at least half of the SMs to the
+        // prep; otherwise, while the caller's stream is being captured into
+        // a graph, and for callers that allocate nothing (no library stream
+        // or event), both run in order on the caller's stream.
         cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
         if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) return GDN_ERR_CUDA;
-        ScanStreams* ss = (cap == cudaStreamCaptureStatusNone && 2 * pairs <= num_sms)
+        ScanStreams* ss = (aux_streams && cap == cudaStreamCaptureStatusNone && 2 * pairs <= num_sms)
                               ? scan_streams_current_device() : nullptr;
         if (ss != nullptr) {
             std::lock_guard<std::mutex> lock(ss->mu);
-            if (cudaEventRecord(ss->fork, st) != cudaSuccess) return GDN_ERR_CUDA;
-            chain();
-            if (cudaStreamWaitEvent(ss->aux, ss->fork, 0) != cudaSuccess) return GDN_ERR_CUDA;
-            prep(ss->aux);
-            if (cudaEventRecord(ss->join, ss->aux) != cudaSuccess || cudaStreamWaitEvent(st, ss->join, 0) != cudaSuccess)
+            if (cudaEventRecord(ss->fork, st) != cudaSuccess || cudaStreamWaitEvent(ss->lo, ss->fork, 0) != cudaSuccess ||
+                cudaStreamWaitEvent(ss->hi, ss->fork, 0) != cudaSuccess)
+                return GDN_ERR_CUDA;
+            prep(ss->lo);
+            chain(ss->hi);
+            if (cudaEventRecord(ss->join_lo, ss->lo) != cudaSuccess || cudaEventRecord(ss->join_hi, ss->hi) != cudaSuccess ||
+                cudaStreamWaitEvent(st, ss->join_lo, 0) != cudaSuccess || cudaStreamWaitEvent(st, ss->join_hi, 0) != cudaSuccess)
                 return GDN_ERR_CUDA;
         } else {
             prep(st);
-            chain();
+            chain(st);
         }
         return gdn_launch_status();
     }

@@ -80,8 +80,17 @@ void launch_prefill_recurrent(const PrefillParams& p, cudaStream_t st);
 // Launches the chunked kernels (prep, then a chain kernel); returns a GDN_*
 // status (GDN_ERR_CUDA when the per-device launch set-up or a launch fails).
 // `workspace_bytes` steers the choice of chain: the scan chain needs the
-// larger of the two workspace layouts.
-int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspace_bytes, cudaStream_t st);
+// larger of the two workspace layouts.  With `aux_streams` the scan chain's
+// prep may run on library streams beside it (created on first use);
+// without, everything runs in order on `st`.
+int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspace_bytes, cudaStream_t st,
+                         bool aux_streams);
+// gdn_prefill_fwd restricted to the caller's stream (no library stream or
+// event is created): the entry point for callers that allocate nothing.
+int prefill_fwd_one_stream(const void* q, const void* k, const void* v, const float* state, const float* A_log,
+                           const void* a, const float* dt_bias, const void* b, const void* cu_seqlens,
+                           int cu_seqlens_is_int64, int N, int T, float scale, int H, int HV, int K, int V,
+                           void* out, float* new_state, void* workspace, size_t workspace_bytes, void* stream);
 // Workspace of the chunked path: enough for every chain (the scan chain's
 // layout is the larger one), and the split-path layout alone (the least a
 // chunked call can run in).

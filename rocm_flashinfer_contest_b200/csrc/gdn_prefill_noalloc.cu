@@ -62,6 +62,6 @@ extern "C" int gdn_prefill_fwd_noalloc(const void* q, const void* k, const void*
     void* scratch = nullptr;
     const int st = scratch_on_current_device(&scratch);
     if (st != GDN_OK) return st;
-    return gdn_prefill_fwd(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64, N, T,
-                           scale, H, HV, K, V, out, new_state, scratch, kScratchBytes, stream);
+    return gdn::prefill_fwd_one_stream(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, cu_seqlens_is_int64, N, T,
+                                       scale, H, HV, K, V, out, new_state, scratch, kScratchBytes, stream);
 }

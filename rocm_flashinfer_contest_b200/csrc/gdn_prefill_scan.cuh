@@ -75,26 +75,32 @@ __device__ __forceinline__ bool wait_ready(const unsigned int* flag) {
 }
 
 // ============================================================================
-// prep: one CTA per (chunk, v-head), 128 threads, three CTAs per SM
+// prep: one CTA per chunk and one or two v-heads of a q/k head
 // ============================================================================
 namespace prep {
 
 using ::gdn::chunk::prep::ix;
-constexpr int NT = 128;
+// A CTA builds the records of NU v-heads of one chunk that share a q/k head
+// (NU = 2 when HV / H is even): one [K ; Q] tile, its f16 conversion and its
+// Gram product serve both; each v-head (a group of 128 threads, its own
+// shared-memory region and 128 TMEM columns) then takes its masks, solve and
+// products.  Per group, the solve matrices' 34 KiB hold the f16 operand
+// tiles once the solve is done.
 constexpr uint32_t OFF_KQ = 0;                      // [K ; Q] f16 K-major 128 x 128, whole kernel
-constexpr uint32_t OFF_A = kTileKQ;                 // A fp32 [64][LDA] during the solve
-constexpr uint32_t OFF_T = OFF_A + 64 * LDA * 4;    // T fp32 [64][LDA] during the solve
-// after the solve the two fp32 matrices' 34 KiB hold the f16 operand tiles
-constexpr uint32_t OFF_TP = OFF_A;                  // [T diag(beta) ; P] K-major 128 x 64       16 KiB
-constexpr uint32_t OFF_T1 = 51200;                  // diag(f_K) T diag(beta), 64 x 64 (MN-major B) 8 KiB
-constexpr uint32_t OFF_EP = OFF_A;                  // [Et diag(e^g) ; Pt diag(e^g)] K-major 192 x 64, 24 KiB
-constexpr uint32_t OFF_GM = OFF_T + 64 * LDA * 4;   // gamma[64], beta[64]
-constexpr uint32_t SMEM_BYTES = OFF_GM + 512 + 1024;  // + alignment slack
-static_assert(OFF_A % 1024 == 0 && OFF_T1 % 1024 == 0, "tile alignment");
-static_assert(OFF_T1 >= OFF_TP + kTileTP && OFF_T1 + 8192 <= OFF_GM, "T1 after [T ; P], before the gates");
-static_assert(OFF_EP + 24576 <= OFF_GM, "[E2 ; P2] inside the solve matrices' space");
-static_assert(3 * (SMEM_BYTES + 1024) <= 233472, "three CTAs per SM");
-constexpr uint32_t TM_COLS = 128;  // 3 CTAs x 128 columns fit the SM's 512
+constexpr uint32_t kGroupBytes = 35840;             // per v-head region (1 KiB multiple)
+constexpr uint32_t G_A = 0;                         // A fp32 [64][LDA] during the solve
+constexpr uint32_t G_T = 64 * LDA * 4;              // T fp32 [64][LDA] during the solve
+constexpr uint32_t G_TP = 0;                        // [T diag(beta) ; P] K-major 128 x 64       16 KiB
+constexpr uint32_t G_T1 = 18432;                    // diag(f_K) T diag(beta), 64 x 64 (MN-major B) 8 KiB
+constexpr uint32_t G_EP = 0;                        // [Et diag(e^g) ; Pt diag(e^g)] K-major 192 x 64, 24 KiB
+constexpr uint32_t G_GM = 2 * 64 * LDA * 4;         // gamma[64], beta[64]
+static_assert(G_T1 % 1024 == 0 && G_T1 >= G_TP + kTileTP && G_T1 + 8192 <= G_GM, "T1 after [T ; P], before the gates");
+static_assert(G_EP + 24576 <= G_GM && G_GM + 512 <= kGroupBytes && kGroupBytes % 1024 == 0, "group region");
+template <int NU> constexpr uint32_t smem_bytes() { return kTileKQ + NU * kGroupBytes + 1024; }  // + alignment slack
+template <int NU> constexpr int ctas_per_sm() { return NU == 1 ? 3 : 2; }
+static_assert(3 * (smem_bytes<1>() + 1024) <= 233472 && 2 * (smem_bytes<2>() + 1024) <= 233472,
+              "three one-head or two two-head CTAs per SM");
+static_assert(3 * 128 <= 512 && 2 * 256 <= 512, "their TMEM columns fit the SM's 512");
 
 // MMA_E reads T1 = diag(f_K) T diag(beta) MN-major (k = token i, n = token j):
 // a row-major 64 x 64 tile in the K-major layout of 64 rows is that operand.
@@ -106,7 +112,11 @@ constexpr bool rows64_are_mn_major() {
 }
 static_assert(rows64_are_mn_major(), "a K-major 64-row tile doubles as the MN-major B operand");
 
-__global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const PrefillParams p, unsigned char* ws) {
+template <int NU>
+__global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_prep_kernel(const PrefillParams p,
+                                                                                        unsigned char* ws) {
+    constexpr int NT = 128 * NU;
+    constexpr uint32_t TM_COLS = 128 * NU;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -114,8 +124,11 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
     __shared__ uint32_t tmem_base_sh;
 
     const int tid = threadIdx.x, warp = tid >> 5;
-    const long long s = blockIdx.x / p.HV;
-    const int hv = blockIdx.x % p.HV, hq = hv / p.rep;
+    const int g = tid >> 7, gt = tid & 127, gwarp = warp & 3;  // v-head group, thread and warp within it
+    const int groups = p.HV / NU;
+    const long long s = blockIdx.x / groups;
+    const int hv0 = (int)(blockIdx.x % groups) * NU;
+    const int hv = hv0 + g, hq = hv0 / p.rep;
 
     // locate the chunk: the largest n with floor(cu[n] / 64) + n <= s, then j
     int lo = 0, hi = p.N - 1;
@@ -133,9 +146,10 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
     const long long tc = t0 + C * j;
     const int len = (int)((t1 - tc) < C ? (t1 - tc) : C);
 
-    float* sA = reinterpret_cast<float*>(sm + OFF_A);
-    float* sT = reinterpret_cast<float*>(sm + OFF_T);
-    float* sG = reinterpret_cast<float*>(sm + OFF_GM);
+    unsigned char* gm = sm + kTileKQ + g * kGroupBytes;  // this v-head's region
+    float* sA = reinterpret_cast<float*>(gm + G_A);
+    float* sT = reinterpret_cast<float*>(gm + G_T);
+    float* sG = reinterpret_cast<float*>(gm + G_GM);
     float* sBeta = sG + 64;
     unsigned char* rec = ws + ((size_t)s * p.HV + hv) * kRecBytes;
 
@@ -150,21 +164,21 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
         cp_async16(sKQ + umma::kmaj_off(64 + r, c * 8, 128), p.q + row, ok);
     }
     cp_async_commit();
-    // gates and the inclusive scan of log g (warps 0 and 1)
+    // gates and the inclusive scan of log g (warps 0 and 1 of each group)
     float lg = 0.f, beta = 0.f;
-    if (tid < len) {
-        const size_t gi = (size_t)(tc + tid) * p.HV + hv;
+    if (gt < len) {
+        const size_t gi = (size_t)(tc + gt) * p.HV + hv;
         lg = log_gate(p.A_log[hv], bf16_to_f32(p.a[gi]), p.dt_bias[hv]);
         beta = sigmoidf_(bf16_to_f32(p.b[gi]));
     }
-    if (warp < 2) {
+    if (gwarp < 2) {
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const float y = __shfl_up_sync(0xffffffffu, lg, o);
-            if ((tid & 31) >= o) lg += y;
+            if ((gt & 31) >= o) lg += y;
         }
-        if (warp == 0) sG[tid] = lg;
-        sBeta[tid] = beta;
+        if (gwarp == 0) sG[gt] = lg;
+        sBeta[gt] = beta;
     }
     if (warp == 0) {
         umma::tmem_alloc(&tmem_base_sh, TM_COLS);
@@ -175,13 +189,13 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
         umma::fence_mbar_init();
     }
     __syncthreads();
-    if (warp == 1) sG[tid] = lg + sG[31];
+    if (gwarp == 1) sG[gt] = lg + sG[31];
     cp_async_wait_all();
     __syncthreads();
     // every product here takes [K ; Q] as f16: normalised rows are written as
     // f16, raw bf16 rows are converted (exact for |x| in f16's normal range)
     if (p.qk_l2norm) {
-        l2norm_row_to_f16(sm + OFF_KQ, tid, 128);
+        if (tid < 128) l2norm_row_to_f16(sm + OFF_KQ, tid, 128);
     } else {
 #pragma unroll 4
         for (int idx = tid; idx < (int)(kTileKQ / 16); idx += NT) {
@@ -193,12 +207,13 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
     }
     sync_for_mma();
     const uint32_t tmem = tmem_base_sh;
-    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    const uint32_t lane_base = (uint32_t)(32 * gwarp) << 16;
+    const uint32_t tg = tmem + 128 * g;  // this v-head's 128 TMEM columns
     const uint64_t dKQ = umma::desc_kmaj(sKQ, 128, 0);
     const uint64_t dKmn = umma::desc_sw128(sKQ, 16384u, 1024u);  // K rows read MN-major (K^T as A, K as B)
-    const uint64_t dEP = umma::desc_kmaj(umma::smem_u32(sm + OFF_EP), 192, 0);
+    bool ok = false;
 
-    // MMA_G: [K ; Q] K^T -> columns 0-63
+    // MMA_G: [K ; Q] K^T -> columns 0-63 (read by every v-head's masks)
     if (tid == 0) {
         constexpr uint32_t ID = umma::idesc_f16(128, 64, 0, 0, 0, 0);
 #pragma unroll
@@ -212,17 +227,17 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
     umma::fence_after_sync();
 
     // Both masks in one pass, each read from its own TMEM lanes:
-    //   A = beta_i e^{gamma_i - gamma_j} k_i.k_j (j < i), rows 0-63 (warps 0, 1),
-    //       into the strictly lower part of sA (whole float4 groups below the
-    //       diagonal, i.e. columns < ceil4(i));
+    //   A = beta_i e^{gamma_i - gamma_j} k_i.k_j (j < i), rows 0-63 (warps 0, 1 of
+    //       the group), into the strictly lower part of sA (whole float4
+    //       groups below the diagonal, i.e. columns < ceil4(i));
     //   P = scale e^{gamma_i - gamma_j} q_i.k_j (j <= i), rows 64-127 (warps 2, 3),
     //       as f16 into the part of sA the solve never touches: P row i (i + 1
     //       values) in row 63 - i from column ceil4(63 - i) on, which leaves
     //       4 (i + 2) bytes of room (with the padding columns 64-67).
     // P reaches its tile after the solve, once sA is free.
     {
-        const int i = tid & 63;
-        const bool arow = tid < 64;
+        const int i = gt & 63;
+        const bool arow = gt < 64;
         const float gi = sG[i];
         const float coef = arow ? sBeta[i] : p.scale;
         const int lim = arow ? i : i + 1;  // columns jj < lim are kept
@@ -232,7 +247,7 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
             // the warp's rows are 32 * (warp % 2) .. + 31: blocks of columns
             // past them are zero for all of its threads (a warp-uniform exit,
             // as tcgen05.ld is executed by whole warps)
-            if (c16 > 32 * (warp & 1) + 31) break;
+            if (c16 > 32 * (gwarp & 1) + 31) break;
             float d[16], r[16];
             umma::tmem_ld16(tmem + lane_base + c16, d);
             if (c16 >= lim) continue;
@@ -253,14 +268,14 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
         }
     }
     __syncthreads();
-    ::gdn::chunk::prep::solve_T(sA, sT, tid);
+    ::gdn::chunk::prep::solve_T(sA, sT, gt);
 
     // f16 copies of T: T diag(beta) -> rows 0-63 of [T ; P] (the B operand of
     // MMA_P, read MN-major from those rows) and diag(f_K) T diag(beta) -> T1;
     // the P rows from their place in sA -> rows 64-127 of [T ; P].  Every
     // thread reads its part first: the tiles overlay sA and sT.
     {
-        const int i = tid >> 1, h = (tid & 1) * 32;  // row i, columns h..h+31
+        const int i = gt >> 1, h = (gt & 1) * 32;  // row i, columns h..h+31
         float t[32];
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
@@ -276,10 +291,10 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
             }
         }
         const float fk = __expf(fminf(sG[C - 1] - sG[i], 0.f));
-        // P row pi (threads 64-127): 8 chunks of 8 f16, chunks past the diagonal zero
-        const int pi = tid - 64;
+        // P row pi (threads 64-127 of the group): 8 chunks of 8 f16, chunks past the diagonal zero
+        const int pi = gt - 64;
         uint4 pr[8];
-        if (tid >= 64) {
+        if (gt >= 64) {
             const unsigned char* prow = reinterpret_cast<const unsigned char*>(sA + ix(63 - pi, ((63 - pi) + 3) & ~3));
 #pragma unroll
             for (int c = 0; c < 8; ++c)
@@ -294,33 +309,37 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
                 x[e] = t[c + e] * sBeta[h + c + e];
                 y[e] = fk * x[e];
             }
-            st_f16x8(sm + OFF_TP, umma::kmaj_off(i, h + c, 128), x);
-            st_f16x8(sm + OFF_T1, umma::kmaj_off(i, h + c, 64), y);
+            st_f16x8(gm + G_TP, umma::kmaj_off(i, h + c, 128), x);
+            st_f16x8(gm + G_T1, umma::kmaj_off(i, h + c, 64), y);
         }
-        if (tid >= 64) {
+        if (gt >= 64) {
 #pragma unroll
             for (int c = 0; c < 8; ++c)
-                *reinterpret_cast<uint4*>(sm + OFF_TP + umma::kmaj_off(64 + pi, 8 * c, 128)) = pr[c];
+                *reinterpret_cast<uint4*>(gm + G_TP + umma::kmaj_off(64 + pi, 8 * c, 128)) = pr[c];
         }
     }
     sync_for_mma();
 
-    // MMA_P: [T diag(beta) ; P] x T diag(beta) -> columns 0-63, rows 64-127 = Pt
-    // MMA_E: K^T x T1 -> columns 64-127 = Et
+    // per v-head u (columns 128u ..): MMA_P: [T diag(beta) ; P] x T diag(beta)
+    // -> columns 0-63, rows 64-127 = Pt;  MMA_E: K^T x T1 -> columns 64-127 = Et
     if (tid == 0) {
         constexpr uint32_t IDP = umma::idesc_f16(128, 64, 0, 0, 0, 1);
         constexpr uint32_t IDE = umma::idesc_f16(128, 64, 0, 0, 1, 1);
-        const uint64_t dTP = umma::desc_kmaj(umma::smem_u32(sm + OFF_TP), 128, 0);
-        const uint64_t dTB = umma::desc_mnmaj(umma::smem_u32(sm + OFF_TP), C, 0);
-        const uint64_t dT1 = umma::desc_mnmaj(umma::smem_u32(sm + OFF_T1), C, 0);
 #pragma unroll
-        for (int k0 = 0; k0 < C; k0 += 16)
-            umma::mma_f16(tmem, umma::desc_add(dTP, umma::koff_kmaj(128, k0)),
-                          umma::desc_add(dTB, umma::koff_mnmaj(k0)), IDP, k0 > 0);
+        for (int u = 0; u < NU; ++u) {
+            unsigned char* um = sm + kTileKQ + u * kGroupBytes;
+            const uint64_t dTP = umma::desc_kmaj(umma::smem_u32(um + G_TP), 128, 0);
+            const uint64_t dTB = umma::desc_mnmaj(umma::smem_u32(um + G_TP), C, 0);
+            const uint64_t dT1 = umma::desc_mnmaj(umma::smem_u32(um + G_T1), C, 0);
 #pragma unroll
-        for (int k0 = 0; k0 < C; k0 += 16)
-            umma::mma_f16(tmem + 64, umma::desc_add(dKmn, umma::koff_mnmaj(k0)),
-                          umma::desc_add(dT1, umma::koff_mnmaj(k0)), IDE, k0 > 0);
+            for (int k0 = 0; k0 < C; k0 += 16)
+                umma::mma_f16(tmem + 128 * u, umma::desc_add(dTP, umma::koff_kmaj(128, k0)),
+                              umma::desc_add(dTB, umma::koff_mnmaj(k0)), IDP, k0 > 0);
+#pragma unroll
+            for (int k0 = 0; k0 < C; k0 += 16)
+                umma::mma_f16(tmem + 128 * u + 64, umma::desc_add(dKmn, umma::koff_mnmaj(k0)),
+                              umma::desc_add(dT1, umma::koff_mnmaj(k0)), IDE, k0 > 0);
+        }
         umma::mma_commit(&mbar[1]);
     }
     if (!wait_mma(&mbar[1], 0)) goto done;
@@ -331,60 +350,64 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
     // Thread = TMEM lane.
     {
         float eg[16];
-        if (tid >= 64) {
-            const int i = tid - 64;
+        if (gt >= 64) {
+            const int i = gt - 64;
 #pragma unroll 1
             for (int c16 = 0; c16 < C; c16 += 16) {
                 float d[16];
-                umma::tmem_ld16(tmem + lane_base + c16, d);
+                umma::tmem_ld16(tg + lane_base + c16, d);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) eg[e] = __expf(sG[c16 + e]);
                 st_f16x8(rec + REC_EP, umma::kmaj_off(128 + i, c16, kRecRows), d);
                 st_f16x8(rec + REC_EP, umma::kmaj_off(128 + i, c16 + 8, kRecRows), d + 8);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) d[e] *= eg[e];
-                st_f16x8(sm + OFF_EP, umma::kmaj_off(128 + i, c16, 192), d);
-                st_f16x8(sm + OFF_EP, umma::kmaj_off(128 + i, c16 + 8, 192), d + 8);
+                st_f16x8(gm + G_EP, umma::kmaj_off(128 + i, c16, 192), d);
+                st_f16x8(gm + G_EP, umma::kmaj_off(128 + i, c16 + 8, 192), d + 8);
             }
         }
 #pragma unroll 1
         for (int c16 = 0; c16 < C; c16 += 16) {
             float d[16];
-            umma::tmem_ld16(tmem + lane_base + 64 + c16, d);
+            umma::tmem_ld16(tg + lane_base + 64 + c16, d);
 #pragma unroll
             for (int e = 0; e < 16; ++e) eg[e] = __expf(sG[c16 + e]);
-            st_f16x8(rec + REC_EP, umma::kmaj_off(tid, c16, kRecRows), d);
-            st_f16x8(rec + REC_EP, umma::kmaj_off(tid, c16 + 8, kRecRows), d + 8);
+            st_f16x8(rec + REC_EP, umma::kmaj_off(gt, c16, kRecRows), d);
+            st_f16x8(rec + REC_EP, umma::kmaj_off(gt, c16 + 8, kRecRows), d + 8);
 #pragma unroll
             for (int e = 0; e < 16; ++e) d[e] *= eg[e];
-            st_f16x8(sm + OFF_EP, umma::kmaj_off(tid, c16, 192), d);
-            st_f16x8(sm + OFF_EP, umma::kmaj_off(tid, c16 + 8, 192), d + 8);
+            st_f16x8(gm + G_EP, umma::kmaj_off(gt, c16, 192), d);
+            st_f16x8(gm + G_EP, umma::kmaj_off(gt, c16 + 8, 192), d + 8);
         }
-        if (tid == 0)
+        if (gt == 0)
             *reinterpret_cast<float4*>(rec + REC_DECAY) = make_float4(__expf(sG[C - 1]), 0.f, 0.f, 0.f);
     }
     sync_for_mma();
 
-    // MMA_A: [E2 ; P2] rows 0-127 x K -> columns 0-127 = Abar
+    // MMA_A: [E2 ; P2] rows 0-127 x K -> columns 0-127 = Abar (per v-head)
     if (tid == 0) {
         constexpr uint32_t ID = umma::idesc_f16(128, 128, 0, 0, 0, 1);
 #pragma unroll
-        for (int k0 = 0; k0 < C; k0 += 16)
-            umma::mma_f16(tmem, umma::desc_add(dEP, umma::koff_kmaj(192, k0)),
-                          umma::desc_add(dKmn, umma::koff_mnmaj(k0)), ID, k0 > 0);
+        for (int u = 0; u < NU; ++u) {
+            const uint64_t dEP = umma::desc_kmaj(umma::smem_u32(sm + kTileKQ + u * kGroupBytes + G_EP), 192, 0);
+#pragma unroll
+            for (int k0 = 0; k0 < C; k0 += 16)
+                umma::mma_f16(tmem + 128 * u, umma::desc_add(dEP, umma::koff_kmaj(192, k0)),
+                              umma::desc_add(dKmn, umma::koff_mnmaj(k0)), ID, k0 > 0);
+        }
         umma::mma_commit(&mbar[2]);
     }
     if (!wait_mma(&mbar[2], 0)) goto done;
     umma::fence_after_sync();
-    // -Abar row k' = tid -> record rows 0-127 of [-Abar ; Qt]
+    // -Abar row k' = gt -> record rows 0-127 of [-Abar ; Qt]
 #pragma unroll 1
     for (int c32 = 0; c32 < kDim; c32 += 32) {
         float d[32];
-        umma::tmem_ld32(tmem + lane_base + c32, d);
+        umma::tmem_ld32(tg + lane_base + c32, d);
 #pragma unroll
         for (int e = 0; e < 32; ++e) d[e] = -d[e];
 #pragma unroll
-        for (int e = 0; e < 32; e += 8) st_f16x8(rec + REC_AQ, umma::kmaj_off(tid, c32 + e, kRecRows), d + e);
+        for (int e = 0; e < 32; e += 8) st_f16x8(rec + REC_AQ, umma::kmaj_off(gt, c32 + e, kRecRows), d + e);
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -393,23 +416,27 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
     // MMA_Q: [E2 ; P2] rows 64-191 x K -> columns 0-127; rows 64-127 = Pt diag(e^gamma) K
     if (tid == 0) {
         constexpr uint32_t ID = umma::idesc_f16(128, 128, 0, 0, 0, 1);
-        const uint64_t a0 = umma::desc_add(dEP, 64 * 128);
 #pragma unroll
-        for (int k0 = 0; k0 < C; k0 += 16)
-            umma::mma_f16(tmem, umma::desc_add(a0, umma::koff_kmaj(192, k0)),
-                          umma::desc_add(dKmn, umma::koff_mnmaj(k0)), ID, k0 > 0);
+        for (int u = 0; u < NU; ++u) {
+            const uint64_t a0 =
+                umma::desc_add(umma::desc_kmaj(umma::smem_u32(sm + kTileKQ + u * kGroupBytes + G_EP), 192, 0), 64 * 128);
+#pragma unroll
+            for (int k0 = 0; k0 < C; k0 += 16)
+                umma::mma_f16(tmem + 128 * u, umma::desc_add(a0, umma::koff_kmaj(192, k0)),
+                              umma::desc_add(dKmn, umma::koff_mnmaj(k0)), ID, k0 > 0);
+        }
         umma::mma_commit(&mbar[3]);
     }
     if (!wait_mma(&mbar[3], 0)) goto done;
     umma::fence_after_sync();
     // Qt row i = scale e^{gamma_i} q_i - (Pt diag(e^gamma) K)_i -> record rows 128-191 of [-Abar ; Qt]
-    if (tid >= 64) {
-        const int i = tid - 64;
+    if (gt >= 64) {
+        const int i = gt - 64;
         const float fq = p.scale * __expf(sG[i]);
 #pragma unroll 1
         for (int c32 = 0; c32 < kDim; c32 += 32) {
             float d[32];
-            umma::tmem_ld32(tmem + lane_base + c32, d);
+            umma::tmem_ld32(tg + lane_base + c32, d);
 #pragma unroll
             for (int e = 0; e < 32; e += 8) {
                 const __half2* qh =
@@ -425,17 +452,16 @@ __global__ void __launch_bounds__(NT, 3) gdn_prefill_scan_prep_kernel(const Pref
             }
         }
     }
-
-    // every thread's record writes, then the ready flag (release, device scope)
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(ready_flag(p, ws, s, hv)), "r"(1u) : "memory");
-    }
+    ok = true;
 
 done:
     umma::fence_before_sync();
     __syncthreads();
+    // every thread's record writes, then the records' ready flags (release, device scope)
+    if (ok && gt == 0) {
+        __threadfence();
+        asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(ready_flag(p, ws, s, hv)), "r"(1u) : "memory");
+    }
     if (warp == 0) umma::tmem_dealloc(tmem, TM_COLS);
 }
 
@@ -502,7 +528,7 @@ static_assert(SMEM_BYTES <= 232448 - 512, "dynamic shared memory limit (with the
 static_assert(kTileAQ % 1024 == 0 && kTileEP % 1024 == 0 && OFF_EP % 1024 == 0 && OFF_V % 1024 == 0 &&
               OFF_O % 1024 == 0, "tile alignment");
 // no prep CTA fits beside a chain CTA, so the chain's TMEM columns are never contended
-static_assert(SMEM_BYTES + prep::SMEM_BYTES > 233472, "chain CTA alone on its SM");
+static_assert(SMEM_BYTES + prep::smem_bytes<1>() > 233472, "chain CTA alone on its SM");
 constexpr uint32_t kXO = 192;            // [X | O] columns
 constexpr uint32_t TM_XO = 0, TM_SA = 2 * kXO, TM_COLS = 512;
 static_assert(TM_SA + 64 <= TM_COLS, "tensor memory budget");
