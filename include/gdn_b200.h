@@ -222,7 +222,7 @@ size_t gdn_prefill_host_workspace_bytes(int N, int T, int H, int HV, int segment
  * tile and gates (17,424 bytes) and, per q/k head, its f16 [K ; Q] operand
  * tile (32,768 bytes) and its cross-Gram tile [K ; Q] K_prev^T (16,384 bytes);
  * or (the scan kernels) per v-head the chunk's state-transition record
- * (73,744 bytes) and a 4-byte ready flag (the flags rounded up to 256 bytes).
+ * (73,984 bytes) and a 4-byte ready flag (the flags rounded up to 256 bytes).
  * The value is the larger of the two layouts.  No counterpart in the
  * reference, whose AITER kernels allocate their intermediates with torch.
  */

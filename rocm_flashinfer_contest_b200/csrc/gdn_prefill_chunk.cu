@@ -1734,7 +1734,10 @@ int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspa
     // result within the operand rounding; the tests run every chunked case
     // through each); the scan chain needs the larger workspace layout.
     const long long pairs = (long long)p.N * p.HV;
-    const bool scan_fits = workspace_bytes >= chunk::scan::workspace_bytes(p.N, p.T, p.HV);
+    // the scan path's records are written with 32-byte stores: it needs its
+    // layout's size and a 256-byte aligned workspace (torch's allocations are)
+    const bool scan_fits = workspace_bytes >= chunk::scan::workspace_bytes(p.N, p.T, p.HV) &&
+                           (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0;
     int which = (p.N == 1 && 2 * pairs <= num_sms && scan_fits) ? 4 : 4 * pairs <= num_sms ? 2 : 3;
     const char* sel = getenv("GDN_PREFILL_CHAIN");
     if (sel && sel[0] >= '2' && sel[0] <= '4' && sel[1] == '\0' && (sel[0] != '4' || scan_fits)) which = sel[0] - '0';

@@ -32,9 +32,11 @@ namespace scan {
 //                 columns k (two 64-column slabs of 24 KiB)     48 KiB
 //   [Et ; Pt]     rows 0-127: Et row k; rows 128-191: Pt row (token i);
 //                 columns token (j)                             24 KiB
-//   e^{gamma_C} (fp32), padding                                  16 B
+//   e^{gamma_C} (fp32), padding to a multiple of 256 bytes         256 B
+// (the prep writes the tiles with 32-byte stores: records, and so the
+// workspace, are 32-byte aligned)
 constexpr uint32_t REC_AQ = 0, REC_EP = 49152, REC_DECAY = 73728;
-constexpr uint32_t kRecBytes = 73744;
+constexpr uint32_t kRecBytes = 73984;
 constexpr uint32_t kRecRows = 192;
 
 // The records, then one ready flag (uint32) per record: the prep sets it
@@ -72,6 +74,29 @@ __device__ __forceinline__ bool wait_ready(const unsigned int* flag) {
         __nanosleep(64);
     }
     return true;
+}
+
+// 16 f16 values (columns k0 .. k0 + 15, k0 a multiple of 16) of row `row` of
+// a K-major 128-byte-swizzled tile in global memory, as one 32-byte store:
+// chunks k0/8 and k0/8 + 1 of a row stay one aligned 32-byte pair under the
+// swizzle (XOR with row % 8), in swapped order when the row is odd.  A warp
+// of rows then writes whole 32-byte sectors.
+__device__ __forceinline__ void st_f16x16_tile(unsigned char* tile, uint32_t row, uint32_t k0, uint32_t rows,
+                                               const float* x) {
+    uint32_t h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        __half2 t = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        h[i] = *reinterpret_cast<uint32_t*>(&t);
+    }
+    if (row & 1u) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { const uint32_t t = h[i]; h[i] = h[4 + i]; h[4 + i] = t; }
+    }
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                 :: "l"(tile + (umma::kmaj_off(row, k0, rows) & ~31u)), "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3]),
+                    "r"(h[4]), "r"(h[5]), "r"(h[6]), "r"(h[7])
+                 : "memory");
 }
 
 // ============================================================================
@@ -358,8 +383,7 @@ __global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_
                 umma::tmem_ld16(tg + lane_base + c16, d);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) eg[e] = __expf(sG[c16 + e]);
-                st_f16x8(rec + REC_EP, umma::kmaj_off(128 + i, c16, kRecRows), d);
-                st_f16x8(rec + REC_EP, umma::kmaj_off(128 + i, c16 + 8, kRecRows), d + 8);
+                st_f16x16_tile(rec + REC_EP, 128 + i, c16, kRecRows, d);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) d[e] *= eg[e];
                 st_f16x8(gm + G_EP, umma::kmaj_off(128 + i, c16, 192), d);
@@ -372,8 +396,7 @@ __global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_
             umma::tmem_ld16(tg + lane_base + 64 + c16, d);
 #pragma unroll
             for (int e = 0; e < 16; ++e) eg[e] = __expf(sG[c16 + e]);
-            st_f16x8(rec + REC_EP, umma::kmaj_off(gt, c16, kRecRows), d);
-            st_f16x8(rec + REC_EP, umma::kmaj_off(gt, c16 + 8, kRecRows), d + 8);
+            st_f16x16_tile(rec + REC_EP, gt, c16, kRecRows, d);
 #pragma unroll
             for (int e = 0; e < 16; ++e) d[e] *= eg[e];
             st_f16x8(gm + G_EP, umma::kmaj_off(gt, c16, 192), d);
@@ -407,7 +430,7 @@ __global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_
 #pragma unroll
         for (int e = 0; e < 32; ++e) d[e] = -d[e];
 #pragma unroll
-        for (int e = 0; e < 32; e += 8) st_f16x8(rec + REC_AQ, umma::kmaj_off(gt, c32 + e, kRecRows), d + e);
+        for (int e = 0; e < 32; e += 16) st_f16x16_tile(rec + REC_AQ, gt, c32 + e, kRecRows, d + e);
     }
     umma::fence_before_sync();
     __syncthreads();
@@ -438,17 +461,20 @@ __global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_
             float d[32];
             umma::tmem_ld32(tg + lane_base + c32, d);
 #pragma unroll
-            for (int e = 0; e < 32; e += 8) {
-                const __half2* qh =
-                    reinterpret_cast<const __half2*>(sm + OFF_KQ + umma::kmaj_off(64 + i, c32 + e, 128));
-                float x[8];
+            for (int e = 0; e < 32; e += 16) {
+                float x[16];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float2 q2 = __half22float2(qh[u]);
-                    x[2 * u] = fmaf(fq, q2.x, -d[e + 2 * u]);
-                    x[2 * u + 1] = fmaf(fq, q2.y, -d[e + 2 * u + 1]);
+                for (int h8 = 0; h8 < 16; h8 += 8) {
+                    const __half2* qh =
+                        reinterpret_cast<const __half2*>(sm + OFF_KQ + umma::kmaj_off(64 + i, c32 + e + h8, 128));
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float2 q2 = __half22float2(qh[u]);
+                        x[h8 + 2 * u] = fmaf(fq, q2.x, -d[e + h8 + 2 * u]);
+                        x[h8 + 2 * u + 1] = fmaf(fq, q2.y, -d[e + h8 + 2 * u + 1]);
+                    }
                 }
-                st_f16x8(rec + REC_AQ, umma::kmaj_off(128 + i, c32 + e, kRecRows), x);
+                st_f16x16_tile(rec + REC_AQ, 128 + i, c32 + e, kRecRows, x);
             }
         }
     }

@@ -288,14 +288,14 @@ def test_prefill_host_workspace_bytes():
 def test_prefill_workspace_size(monkeypatch):
     """The workspace covers both layouts of the chunked path: per 64-token
     slot, the split/transposed chains' [T;P'] records and [K;Q] + G tiles,
-    and the scan chain's 73,744-byte transition records per v-head plus a
+    and the scan chain's 73,984-byte transition records per v-head plus a
     4-byte ready flag each (the flags rounded up to 256 bytes)."""
     ws = _lib.lib().gdn_prefill_workspace_bytes
 
     def want(N, T, H, HV):
         slots = T // 64 + N
         split = slots * (HV * 17424 + H * (32768 + 16384))
-        scan = slots * HV * 73744 + (slots * HV * 4 + 255) // 256 * 256
+        scan = slots * HV * 73984 + (slots * HV * 4 + 255) // 256 * 256
         return max(split, scan)
 
     monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "128")
@@ -306,7 +306,7 @@ def test_prefill_workspace_size(monkeypatch):
     monkeypatch.setenv("GDN_PREFILL_CHUNK_MIN", "0")
     assert ws(3, 100, 4, 8) == want(3, 100, 4, 8)
     assert ws(2, 640, 16, 16) == want(2, 640, 16, 16)
-    assert ws(2, 640, 4, 32) == want(2, 640, 4, 32) == 12 * 32 * 73744 + 1536  # the scan layout
+    assert ws(2, 640, 4, 32) == want(2, 640, 4, 32) == 12 * 32 * 73984 + 1536  # the scan layout
 
 
 def test_error_is_raised_as_exception():
