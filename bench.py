@@ -630,6 +630,14 @@ def bench_ours(args, rank, world, local):
         barrier(world)
         bf16_ms = timed_steps(bf16_step, args.steps, flush, stream)
         barrier(world)
+        # the same launches after a clean L2 (as for the headline decode): at
+        # 128 MB per step the flush's dirty lines, written back inside the
+        # timed kernel, are a large share of the plain-flush time
+        clean = torch.zeros(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+        bf16_clean_ms = timed_steps(bf16_step, args.steps, flush, stream, clean=clean)
+        del clean
+        torch.cuda.synchronize()
+        barrier(world)
     clocks = clk.summary()
     mtp_step_ms = max_over_ranks(statistics.mean(mtp_ms), world, dev)
     bf16_step_ms = max_over_ranks(statistics.mean(bf16_ms), world, dev)
@@ -723,6 +731,19 @@ def bench_ours(args, rank, world, local):
     pre_flops = prefill_alg_flops(PREFILL_T)
     bf16_alg = decode_alg_bytes(DECODE_B) - decode_state_bytes(DECODE_B) // 2 + DECODE_B * 4
     pre_achieved = pre_flops / (statistics.mean(pre_ms) * 1e-3) / 1e12
+    # one kernel per decode / MTP call, two per chunked prefill call (prep +
+    # chain), one per batch slice of the host-buffer decode, and per
+    # host-buffer prefill step a cu_seqlens widening plus (cu, prep, chain)
+    # per segment; the paired bars and contest workloads (one GPU) add
+    # theirs; counted over every timed region
+    launch_regions = {"decode": args.steps, "decode_clean_l2": args.steps,
+                      "decode_b1024": args.steps, "prefill": 2 * args.steps,
+                      "prefill_config3": 2 * args.steps if c3_shard.seqs else 0,
+                      "mtp": args.steps,
+                      "decode_bf16_state": 2 * args.steps,
+                      "decode_e2e": e2e_steps * host_slices,
+                      "prefill_e2e": pe2e_steps * host_pre_launches,
+                      "bars_and_contest_workloads": contest_launches}
     c3_times = [r[0] for r in c3_per_rank]
     c3_toks = [r[1] for r in c3_per_rank]
     c3_max = max(c3_times)
@@ -760,21 +781,8 @@ def bench_ours(args, rank, world, local):
                 "path": "gdn_decode.run_host_into -> C-ABI gdn_decode_fwd_host: pinned host inputs -> "
                         "device -> pinned host outputs, batch slices of ~16 MiB of state with the two "
                         "copy directions overlapped"},
-        # one kernel per decode / MTP call, two per chunked prefill call (prep +
-        # chain), one per batch slice of the host-buffer decode, and per
-        # host-buffer prefill step a cu_seqlens widening plus (cu, prep, chain)
-        # per segment; the paired bars and contest workloads (one GPU) add
-        # theirs; counted over every timed region
-        "gpu_launches": (8 * args.steps + e2e_steps * host_slices + pe2e_steps * host_pre_launches
-                         + contest_launches),
-        "gpu_launches_by_region": {"decode": args.steps, "decode_clean_l2": args.steps,
-                                   "decode_b1024": args.steps, "prefill": 2 * args.steps,
-                                   "prefill_config3": 2 * args.steps if c3_shard.seqs else 0,
-                                   "mtp": args.steps,
-                                   "decode_bf16_state": args.steps,
-                                   "decode_e2e": e2e_steps * host_slices,
-                                   "prefill_e2e": pe2e_steps * host_pre_launches,
-                                   "bars_and_contest_workloads": contest_launches},
+        "gpu_launches": sum(launch_regions.values()),
+        "gpu_launches_by_region": launch_regions,
         "clocks": clocks,
         "decode_b1024": {
             "metric": f"gdn_decode state GB/s, one B={DECODE_B_STRONG} batch split across the ranks",
@@ -839,6 +847,10 @@ def bench_ours(args, rank, world, local):
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(bf16_alg / (statistics.mean(bf16_ms) * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                          "alg_bytes_per_launch": bf16_alg, "peak_src": peaks["src"]},
+            "clean_l2": {"us_per_step": round(statistics.mean(bf16_clean_ms) * 1e3, 2),
+                         "achieved_gbs": round(bf16_alg / (statistics.mean(bf16_clean_ms) * 1e-3) / 1e9, 1),
+                         "frac": round(bf16_alg / (statistics.mean(bf16_clean_ms) * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                         "note": "same launches, L2 written then read clean before each step"},
         },
     }
     if bars is not None:
