@@ -51,6 +51,8 @@ def test_mtp_matches_golden(cuda_device):
     (3, 1, 5, 16, 32, torch.int64, True, 3),     # T = 1: pool-indexed decode
     (5, 8, 9, 1, 4, torch.int32, False, 4),      # GVA 4, long draft
     (40, 3, 40, 16, 32, torch.int64, False, 5),  # above the small-grid threshold
+    (24, 6, 30, 16, 32, torch.int32, True, 6),   # two chunks of the chunk form, the second padded
+    (6, 5, 6, 4, 8, torch.int64, True, 7),       # a chunk of four and one of a single token
 ])
 def test_mtp_matches_oracle(cuda_device, B, T, pool, H, HV, idx_dtype, inter, seed):
     args = inputs.mtp_inputs(B, T, pool, H, HV, seed=seed, idx_dtype=idx_dtype, intermediate=inter)
@@ -115,8 +117,8 @@ def test_mtp_intermediate_layout(cuda_device):
     assert torch.equal(buf[1, T - 1], s[1])
 
 
-def test_mtp_flashinfer_api_modes(cuda_device):
-    B, T, pool, H, HV = 6, 4, 10, 4, 8
+@pytest.mark.parametrize("B,T,pool,H,HV", [(6, 4, 10, 4, 8), (6, 2, 6, 4, 8), (40, 5, 40, 16, 32)])
+def test_mtp_flashinfer_api_modes(cuda_device, B, T, pool, H, HV):
     args = inputs.mtp_inputs(B, T, pool, H, HV, seed=30)
     # raw (unnormalised) q, k for use_qk_l2norm
     g = torch.Generator().manual_seed(31)
@@ -183,6 +185,9 @@ def _bf16_tol(sol, ref):
     (64, 1, 96, 16, 32, 60),   # bf16-state decode at the benchmark heads
     (8, 4, 12, 4, 8, 61),      # bf16-state MTP, contest heads
     (5, 2, 5, 1, 4, 62),       # GVA 4, small grid
+    (32, 4, 40, 16, 32, 63),   # 64-row CTAs (large grid), chunk of four
+    (32, 2, 32, 16, 32, 64),   # 64-row CTAs, chunk of two
+    (20, 7, 24, 16, 32, 65),   # 32-row CTAs, two chunks
 ])
 def test_mtp_bf16_state_matches_oracle(cuda_device, B, T, pool, H, HV, seed):
     args = inputs.mtp_inputs(B, T, pool, H, HV, seed=seed)

@@ -101,7 +101,7 @@ def test_one_token_prefills_equal_a_decode_step(cuda_device, monkeypatch, path):
     assert_state_close(ps.cpu(), ds.cpu())
 
 
-@pytest.mark.parametrize("T", [2, 4, 8])
+@pytest.mark.parametrize("T", [2, 3, 4, 5, 8])
 def test_mtp_equals_stepwise_decode(cuda_device, T):
     B, pool = 64, 64
     q, k, v, pool_state, idx, A_log, a, dt_bias, b, scale, _ = inputs.mtp_inputs(
