@@ -57,9 +57,10 @@ int gdn_abi_version(void);
 /* Human-readable text for a status code. */
 const char *gdn_strerror(int status);
 
-/* Error bits recorded by the prefill kernels since the last clear (1 = a
- * bounded wait on the tensor cores timed out); synchronises the device.
- * clear != 0 resets the word.  Returns -1 if it cannot be read. */
+/* Error bits recorded by the prefill kernels and the streaming multi-token
+ * decode kernel since the last clear (1 = a bounded wait on an mbarrier timed
+ * out); synchronises the device.  clear != 0 resets the word.  Returns -1 if
+ * it cannot be read. */
 int gdn_device_status(int clear);
 
 /*

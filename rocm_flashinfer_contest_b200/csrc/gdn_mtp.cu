@@ -27,137 +27,22 @@
 //   sk = S.k   sq = S.q   kq = k.q
 //   delta = beta * (v - g*sk);  o = scale*(g*sq + delta*kq);  S = g*S + delta*k
 // The pool row is read once and written once whatever T is; each snapshot
-// adds one streaming write.  q/k/v/gates of token t+1 are loaded while token t
-// computes, so the only exposed latency is the first state load.
-#include "gdn_common.cuh"
+// adds one streaming write.  Kernels here: the pool decode (T = 1), the staged
+// token loop and the chunk form (T > 1); the persistent streaming kernel of
+// gdn_mtp_stream.cu takes part of the T > 1 calls (see gdn_mtp_fwd).
+#include <stdlib.h>
+#include <string.h>
+
+#include "gdn_mtp_common.cuh"
 
 namespace gdn {
-
-struct MtpParams {
-    const __nv_bfloat16* q;  // [B, T, H, 128]
-    const __nv_bfloat16* k;
-    const __nv_bfloat16* v;  // [B, T, HV, 128]
-    const void* pool_in;     // [pool, HV, 128, 128] fp32 or bf16
-    void* pool_out;          // nullable: final state not written
-    const void* idx;         // [B] int32 or int64
-    const void* out_idx;     // nullable: final state to slot idx[i]
-    const float* A_log;
-    const __nv_bfloat16* a;  // [B, T, HV]
-    const float* dt_bias;
-    const __nv_bfloat16* b;
-    __nv_bfloat16* out;      // [B, T, HV, 128]
-    float* inter;            // nullable: [inter_slots, cache_steps, HV, 128, 128]
-    float scale;
-    int T, H, HV, rep, pool_size, inter_slots, cache_steps, idx64, l2norm;
-    int snap_entry;          // snapshots indexed by batch entry (row bi * T + t), not by pool slot
-};
-
-__device__ __forceinline__ float mtp_dot4(float4 x, float4 y) {
-    return x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
-}
-
-// Column layout of a lane's 16 values of a row (4 groups of 4).  fp32 state:
-// group j at columns 4*sub + 32*j (one 16-byte access per group).  bf16 state:
-// groups 2p, 2p+1 at columns 8*sub + 64*p (+4), so one 16-byte access moves
-// two groups and a row needs two accesses per lane.
-// First snapshot row (in units of one head's V x K state times HV) of batch
-// entry bi reading pool slot `slot`, or -1 when its snapshots do not fit in
-// the buffer (an entry is written whole or not at all).
-__device__ __forceinline__ long long mtp_snap_row(const MtpParams& p, int bi, long long slot) {
-    if (p.inter == nullptr) return -1;
-    if (p.snap_entry) {
-        const long long r = (long long)bi * p.T;
-        return r + p.T <= (long long)p.inter_slots * p.cache_steps ? r : -1;
-    }
-    return slot < p.inter_slots ? slot * p.cache_steps : -1;
-}
-
-template <typename StateT>
-__device__ __forceinline__ int mtp_col(int sub, int j) {
-    return sizeof(StateT) == 4 ? 4 * sub + 32 * j : 8 * sub + 64 * (j >> 1) + 4 * (j & 1);
-}
-
-__device__ __forceinline__ float4 mtp_widen4(uint2 raw);
-
-// One row's 16 values for this lane (row base `off`, in elements), widened.
-__device__ __forceinline__ void mtp_load_row(const float* base, size_t off, int sub, float4 (&r)[4]) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) r[j] = __ldcs(reinterpret_cast<const float4*>(base + off + mtp_col<float>(sub, j)));
-}
-__device__ __forceinline__ void mtp_load_row(const __nv_bfloat16* base, size_t off, int sub, float4 (&r)[4]) {
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-        uint4 raw = __ldcs(reinterpret_cast<const uint4*>(base + off + mtp_col<__nv_bfloat16>(sub, 2 * p)));
-        r[2 * p] = mtp_widen4(make_uint2(raw.x, raw.y));
-        r[2 * p + 1] = mtp_widen4(make_uint2(raw.z, raw.w));
-    }
-}
-__device__ __forceinline__ void mtp_store_row(float* base, size_t off, int sub, const float4 (&r)[4]) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) __stcs(reinterpret_cast<float4*>(base + off + mtp_col<float>(sub, j)), r[j]);
-}
-__device__ __forceinline__ uint32_t mtp_pack2(float x, float y) {
-    __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
-    return *reinterpret_cast<uint32_t*>(&h);
-}
-__device__ __forceinline__ void mtp_store_row(__nv_bfloat16* base, size_t off, int sub, const float4 (&r)[4]) {
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-        const float4 a = r[2 * p], b = r[2 * p + 1];
-        uint4 raw = make_uint4(mtp_pack2(a.x, a.y), mtp_pack2(a.z, a.w), mtp_pack2(b.x, b.y), mtp_pack2(b.z, b.w));
-        __stcs(reinterpret_cast<uint4*>(base + off + mtp_col<__nv_bfloat16>(sub, 2 * p)), raw);
-    }
-}
-
-__device__ __forceinline__ long long mtp_index(const void* idx, int idx64, int i) {
-    return idx64 ? static_cast<const long long*>(idx)[i] : (long long)static_cast<const int*>(idx)[i];
-}
-
-__device__ __forceinline__ float row8_sum(float x) {
-    x += __shfl_xor_sync(0xffffffffu, x, 1);
-    x += __shfl_xor_sync(0xffffffffu, x, 2);
-    x += __shfl_xor_sync(0xffffffffu, x, 4);
-    return x;
-}
-
-// Everything one token contributes to one lane (q, k still packed bf16).
-template <int kPasses>
-struct MtpToken {
-    uint2 q[4], k[4];
-    float v[kPasses];
-    float a, b;
-};
-
-__device__ __forceinline__ float4 mtp_widen4(uint2 raw) {
-    __nv_bfloat162 lo = *reinterpret_cast<__nv_bfloat162*>(&raw.x);
-    __nv_bfloat162 hi = *reinterpret_cast<__nv_bfloat162*>(&raw.y);
-    float2 x = __bfloat1622float2(lo), y = __bfloat1622float2(hi);
-    return make_float4(x.x, x.y, y.x, y.y);
-}
-
-template <typename StateT, int kPasses>
-__device__ __forceinline__ void mtp_load_token(MtpToken<kPasses>& tk, const MtpParams& p, size_t bt,
-                                               int hq, int hv, int sub, int row_base) {
-    const __nv_bfloat16* qh = p.q + (bt * p.H + hq) * kDim;
-    const __nv_bfloat16* kh = p.k + (bt * p.H + hq) * kDim;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        tk.q[j] = *reinterpret_cast<const uint2*>(qh + mtp_col<StateT>(sub, j));
-        tk.k[j] = *reinterpret_cast<const uint2*>(kh + mtp_col<StateT>(sub, j));
-    }
-    const size_t vh = bt * p.HV + hv;
-#pragma unroll
-    for (int ps = 0; ps < kPasses; ++ps) tk.v[ps] = bf16_to_f32(p.v[vh * kDim + row_base + ps * 4]);
-    tk.a = bf16_to_f32(p.a[vh]);
-    tk.b = bf16_to_f32(p.b[vh]);
-}
 
 // ROWS_PER_CTA rows of one (batch entry, v-head) per CTA of 4 warps; the pool
 // holds StateT (float or __nv_bfloat16).
 // Resident CTAs per SM each instantiation is compiled for (register cap
 // 65536 / (128 * n)).  The fp32 32-row kernels stream the pool at B = 64 and
-// gain from one more resident CTA (more state bytes in flight): the T > 1
-// kernel 149.5 -> 141.3 us at T = 4 with 96 instead of 123 registers, the
+// gain from one more resident CTA (more state bytes in flight): a T > 1 token
+// loop 149.5 -> 141.3 us at T = 4 with 96 instead of 123 registers, the
 // T = 1 kernel 47.1 -> 46.1 us with 80 instead of 92, both without spills
 // of note; the other instantiations keep the occupancy their register
 // counts give them (a tighter cap made the bf16 64-row decode spill and
@@ -169,117 +54,6 @@ constexpr int mtp_min_blocks() {
 template <int ROWS, typename StateT>
 constexpr int pool_decode_min_blocks() {
     return sizeof(StateT) == 4 ? (ROWS == 32 ? 6 : 8) : (ROWS == 64 ? 5 : 8);
-}
-
-template <int ROWS_PER_CTA, typename StateT>
-__global__ void __launch_bounds__(128, mtp_min_blocks<ROWS_PER_CTA, StateT>()) gdn_mtp_kernel(const MtpParams p) {
-    constexpr int kRowsPerWarp = ROWS_PER_CTA / 4;
-    constexpr int kPasses = kRowsPerWarp / 4;
-    constexpr int kBlocksPerHead = kDim / ROWS_PER_CTA;
-    static_assert(kPasses >= 1 && kRowsPerWarp % 4 == 0, "4 rows per warp pass");
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int sub = lane & 7;
-    const int rsub = lane >> 3;
-    const long long head = blockIdx.x / kBlocksPerHead;  // bi * HV + hv
-    const int rb = blockIdx.x % kBlocksPerHead;
-    const int bi = (int)(head / p.HV), hv = (int)(head % p.HV);
-    const int hq = hv / p.rep;
-    const int row_base = rb * ROWS_PER_CTA + warp * kRowsPerWarp + rsub;
-    const int T = p.T;
-
-    const long long slot = mtp_index(p.idx, p.idx64, bi);
-    if (slot < 0 || slot >= p.pool_size) {  // padding entry
-        if (sub == 0) {
-            for (int t = 0; t < T; ++t) {
-                const size_t ob = (((size_t)bi * T + t) * p.HV + hv) * kDim + row_base;
-#pragma unroll
-                for (int ps = 0; ps < kPasses; ++ps) p.out[ob + ps * 4] = __float2bfloat16_rn(0.0f);
-            }
-        }
-        return;
-    }
-
-    const size_t row_off = (size_t)row_base * kDim;
-    const size_t sbase = ((size_t)slot * p.HV + hv) * kDim * kDim + row_off;
-    const StateT* pin = static_cast<const StateT*>(p.pool_in);
-    float4 s[kPasses][4];
-#pragma unroll
-    for (int ps = 0; ps < kPasses; ++ps) mtp_load_row(pin, sbase + (size_t)ps * 4 * kDim, sub, s[ps]);
-
-    const long long snap_row = mtp_snap_row(p, bi, slot);
-    const bool snap = snap_row >= 0;
-    const bool upper = (sub & 4) != 0;
-    MtpToken<kPasses> cur, nxt;
-    mtp_load_token<StateT>(cur, p, (size_t)bi * T, hq, hv, sub, row_base);
-
-    for (int t = 0; t < T; ++t) {
-        const size_t bt = (size_t)bi * T + t;
-        mtp_load_token<StateT>(nxt, p, t + 1 < T ? bt + 1 : bt, hq, hv, sub, row_base);
-
-        float4 qf[4], kf[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            qf[j] = mtp_widen4(cur.q[j]);
-            kf[j] = mtp_widen4(cur.k[j]);
-        }
-        const float g = expf(log_gate(p.A_log[hv], cur.a, p.dt_bias[hv]));
-        const float beta = sigmoidf_(cur.b);
-        if (p.l2norm) {
-            float qq = 0.f, kk = 0.f;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                qq += mtp_dot4(qf[j], qf[j]);
-                kk += mtp_dot4(kf[j], kf[j]);
-            }
-            const float iq = rsqrtf(row8_sum(qq) + 1e-6f), ik = rsqrtf(row8_sum(kk) + 1e-6f);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                qf[j] = make_float4(qf[j].x * iq, qf[j].y * iq, qf[j].z * iq, qf[j].w * iq);
-                kf[j] = make_float4(kf[j].x * ik, kf[j].y * ik, kf[j].z * ik, kf[j].w * ik);
-            }
-        }
-        float kq = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) kq += mtp_dot4(kf[j], qf[j]);
-        kq = row8_sum(kq);
-
-        const size_t ob = (bt * p.HV + hv) * kDim + row_base;
-        float* snap_dst = snap ? p.inter + (((size_t)snap_row + t) * p.HV + hv) * kDim * kDim + row_off : nullptr;
-#pragma unroll
-        for (int ps = 0; ps < kPasses; ++ps) {
-            float2 sk2 = make_float2(0.f, 0.f), sq2 = make_float2(0.f, 0.f);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                sk2 = dot4_acc2(s[ps][j], kf[j], sk2);
-                sq2 = dot4_acc2(s[ps][j], qf[j], sq2);
-            }
-            const float sk = sk2.x + sk2.y, sq = sq2.x + sq2.y;
-            float give = upper ? sk : sq;
-            float keep = upper ? sq : sk;
-            keep += __shfl_xor_sync(0xffffffffu, give, 4);
-            keep += __shfl_xor_sync(0xffffffffu, keep, 1);
-            keep += __shfl_xor_sync(0xffffffffu, keep, 2);
-            // keep == full sk on lanes sub < 4, full sq on lanes sub >= 4
-            const float sk_all = __shfl_sync(0xffffffffu, keep, lane & ~4);
-            const float delta = beta * (cur.v[ps] - g * sk_all);
-            if (sub == 4) p.out[ob + ps * 4] = __float2bfloat16_rn(p.scale * (g * keep + delta * kq));
-#pragma unroll
-            for (int j = 0; j < 4; ++j) s[ps][j] = gs_plus_dk(g, s[ps][j], delta, kf[j]);
-            if constexpr (sizeof(StateT) == 4) {  // snapshots exist for fp32 pools only
-                if (snap) mtp_store_row(snap_dst, (size_t)ps * 4 * kDim, sub, s[ps]);
-            }
-        }
-        cur = nxt;
-    }
-
-    const long long oslot = p.out_idx != nullptr ? mtp_index(p.out_idx, p.idx64, bi) : slot;
-    if (p.pool_out != nullptr && oslot >= 0 && oslot < p.pool_size) {
-        StateT* pout = static_cast<StateT*>(p.pool_out);
-        const size_t obase = ((size_t)oslot * p.HV + hv) * kDim * kDim + row_off;
-#pragma unroll
-        for (int ps = 0; ps < kPasses; ++ps) mtp_store_row(pout, obase + (size_t)ps * 4 * kDim, sub, s[ps]);
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -311,12 +85,6 @@ __device__ __forceinline__ float4 lds4_fresh(const float4* p) {
     return v;
 }
 
-// One bf16 output value, stored through the global state space (a store the
-// compiler knows cannot touch shared memory).
-__device__ __forceinline__ void stg_bf16(__nv_bfloat16* p, float x) {
-    const __nv_bfloat16 h = __float2bfloat16_rn(x);
-    asm volatile("st.global.b16 [%0], %1;" ::"l"(p), "h"(*reinterpret_cast<const unsigned short*>(&h)) : "memory");
-}
 
 template <int C>
 struct MtpChunkDims {
@@ -608,7 +376,7 @@ __global__ void __launch_bounds__(128, mtp_min_blocks<ROWS_PER_CTA, StateT>())
 }
 
 // ---------------------------------------------------------------------------
-// Staged token loop (T > 1).  The per-token recurrence of gdn_mtp_kernel, with
+// Staged token loop (T > 1).  The per-token recurrence above, with
 // everything a token contributes that does not depend on the state prepared
 // once per CTA before the loop, beside the state load: q and k widened to fp32
 // in shared memory (and normalised, under in-kernel L2 normalisation), k.q,
@@ -765,6 +533,31 @@ __global__ void __launch_bounds__(128, mtp_min_blocks<ROWS_PER_CTA, StateT>())
 // bytes per value in registers) and widens one row pass at a time.  That
 // keeps the register count near the batch decode kernel's and with it the
 // bytes in flight per SM, which is what bounds an HBM stream.
+
+// Everything one token contributes to one lane (q, k still packed bf16).
+template <int kPasses>
+struct MtpToken {
+    uint2 q[4], k[4];
+    float v[kPasses];
+    float a, b;
+};
+
+template <typename StateT, int kPasses>
+__device__ __forceinline__ void mtp_load_token(MtpToken<kPasses>& tk, const MtpParams& p, size_t bt,
+                                               int hq, int hv, int sub, int row_base) {
+    const __nv_bfloat16* qh = p.q + (bt * p.H + hq) * kDim;
+    const __nv_bfloat16* kh = p.k + (bt * p.H + hq) * kDim;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        tk.q[j] = *reinterpret_cast<const uint2*>(qh + mtp_col<StateT>(sub, j));
+        tk.k[j] = *reinterpret_cast<const uint2*>(kh + mtp_col<StateT>(sub, j));
+    }
+    const size_t vh = bt * p.HV + hv;
+#pragma unroll
+    for (int ps = 0; ps < kPasses; ++ps) tk.v[ps] = bf16_to_f32(p.v[vh * kDim + row_base + ps * 4]);
+    tk.a = bf16_to_f32(p.a[vh]);
+    tk.b = bf16_to_f32(p.b[vh]);
+}
 
 template <typename StateT>
 struct RowPack;
@@ -968,6 +761,21 @@ extern "C" int gdn_mtp_fwd(const void* q, const void* k, const void* v, const vo
     p.snap_entry = (flags & GDN_MTP_SNAPSHOTS_BY_ENTRY) != 0;
     const long long heads = (long long)B * HV;
     const bool small = heads * (gdn::kDim / 32) < 4 * 148;
+    // Kernel form.  Default, by measurement on B200 (µs at B = 64, HV = 32, L2
+    // flushed): T = 1 -> the per-CTA pool decode; T > 1 with snapshots -> the
+    // staged loop (the snapshot writes keep it HBM-bound); T > 1 without
+    // snapshots -> the streaming kernel for fp32 pools up to T = 4 (T = 2:
+    // 58.9 vs 74.8, T = 4: 80.0 vs 89.5) and bf16 pools at T = 2 (50.5 vs
+    // 56.7), the staged loop otherwise (its 20 warps per SM hide the longer
+    // token chains better).  GDN_MTP_FORM = "stream", "staged" or "chunk"
+    // forces a T > 1 form (stream falls back when the call does not qualify).
+    const char* form = getenv("GDN_MTP_FORM");
+    const bool forced = form != nullptr && *form != 0;
+    const bool stream_default = !small && intermediate == nullptr && (state_bf16 ? T == 2 : T >= 2 && T <= 4);
+    if (T > 1 && (forced ? strcmp(form, "stream") == 0 : stream_default)) {
+        const int r = gdn::launch_mtp_stream(p, B, state_bf16 != 0, st);
+        if (r != 1) return r;
+    }
     if (T == 1) {
         // bf16 rows are half as long: twice the rows per CTA for the same bytes in flight
         const int rows = small ? 16 : state_bf16 ? 64 : 32;
@@ -981,23 +789,18 @@ extern "C" int gdn_mtp_fwd(const void* q, const void* k, const void* v, const vo
         }
         return gdn_launch_status();
     }
-    const char* form = getenv("GDN_MTP_FORM");
-    const int which = form && form[0] == 't' ? 0 : form && form[0] == 'c' ? 1 : 2;
+    const bool chunk = forced && strcmp(form, "chunk") == 0;
     if (state_bf16) {
         // half the bytes per row: 64 rows per CTA keep as many bytes in flight
         const bool large = heads * (gdn::kDim / 64) >= 8 * 148;
         const int rows = small ? 16 : large ? 64 : 32;
         const unsigned grid = (unsigned)(heads * (gdn::kDim / rows));
         using BF = __nv_bfloat16;
-        if (which == 0) {
-            if (rows == 16) gdn::gdn_mtp_kernel<16, BF><<<grid, 128, 0, st>>>(p);
-            else if (rows == 32) gdn::gdn_mtp_kernel<32, BF><<<grid, 128, 0, st>>>(p);
-            else gdn::gdn_mtp_kernel<64, BF><<<grid, 128, 0, st>>>(p);
-        } else if (which == 1 && T == 2) {
+        if (chunk && T == 2) {
             if (rows == 16) gdn::gdn_mtp_chunk_kernel<16, BF, 2><<<grid, 128, 0, st>>>(p);
             else if (rows == 32) gdn::gdn_mtp_chunk_kernel<32, BF, 2><<<grid, 128, 0, st>>>(p);
             else gdn::gdn_mtp_chunk_kernel<64, BF, 2><<<grid, 128, 0, st>>>(p);
-        } else if (which == 1) {
+        } else if (chunk) {
             if (rows == 16) gdn::gdn_mtp_chunk_kernel<16, BF, 4><<<grid, 128, 0, st>>>(p);
             else if (rows == 32) gdn::gdn_mtp_chunk_kernel<32, BF, 4><<<grid, 128, 0, st>>>(p);
             else gdn::gdn_mtp_chunk_kernel<64, BF, 4><<<grid, 128, 0, st>>>(p);
@@ -1008,13 +811,10 @@ extern "C" int gdn_mtp_fwd(const void* q, const void* k, const void* v, const vo
         }
     } else {
         const unsigned grid = (unsigned)(heads * (gdn::kDim / (small ? 16 : 32)));
-        if (which == 0) {
-            if (small) gdn::gdn_mtp_kernel<16, float><<<grid, 128, 0, st>>>(p);
-            else gdn::gdn_mtp_kernel<32, float><<<grid, 128, 0, st>>>(p);
-        } else if (which == 1 && T == 2) {
+        if (chunk && T == 2) {
             if (small) gdn::gdn_mtp_chunk_kernel<16, float, 2><<<grid, 128, 0, st>>>(p);
             else gdn::gdn_mtp_chunk_kernel<32, float, 2><<<grid, 128, 0, st>>>(p);
-        } else if (which == 1) {
+        } else if (chunk) {
             if (small) gdn::gdn_mtp_chunk_kernel<16, float, 4><<<grid, 128, 0, st>>>(p);
             else gdn::gdn_mtp_chunk_kernel<32, float, 4><<<grid, 128, 0, st>>>(p);
         } else {

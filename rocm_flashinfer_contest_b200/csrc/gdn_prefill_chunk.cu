@@ -1810,6 +1810,12 @@ int launch_prefill_chunk(const PrefillParams& p, void* workspace, size_t workspa
 
 }  // namespace gdn
 
+namespace gdn {
+int mtp_stream_status(bool clear);  // gdn_mtp_stream.cu
+}
+
+// The status words of the prefill's and of the streaming MTP kernel's
+// translation units, or-ed.
 extern "C" int gdn_device_status(int clear) {
     unsigned int v = 0;
     if (cudaMemcpyFromSymbol(&v, gdn::g_device_status, sizeof(v)) != cudaSuccess) return -1;
@@ -1817,5 +1823,7 @@ extern "C" int gdn_device_status(int clear) {
         const unsigned int z = 0;
         if (cudaMemcpyToSymbol(gdn::g_device_status, &z, sizeof(z)) != cudaSuccess) return -1;
     }
-    return (int)v;
+    const int m = gdn::mtp_stream_status(clear != 0);
+    if (m < 0) return -1;
+    return (int)(v | (unsigned int)m);
 }

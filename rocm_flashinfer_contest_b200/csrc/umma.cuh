@@ -223,6 +223,21 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst_smem, const void* src, uin
         :: "r"(dst_smem), "l"(src), "r"(bytes), "r"(smem_u32(mbar)) : "memory");
 }
 
+// The same copy with an L2 eviction-priority hint (a policy from
+// l2_evict_first_policy): for data read once, so that its lines leave L2
+// before anything else does.
+__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst_smem, const void* src, uint32_t bytes, uint64_t* mbar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+        :: "r"(dst_smem), "l"(src), "r"(bytes), "r"(smem_u32(mbar)), "l"(policy) : "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 // Shared -> global bulk copy (TMA engine, no multicast), in a bulk group of
 // the issuing thread: both addresses 16-byte aligned, bytes a multiple of 16;
 // the source must be fenced (fence_proxy_async_smem) after the threads that

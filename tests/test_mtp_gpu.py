@@ -305,3 +305,43 @@ def test_mtp_serving_api_snapshots_by_entry(cuda_device, T, steps, rows_entries)
     assert torch.equal(untouched, got == -3.0)   # the same rows written
     assert_state_close(got[~untouched.all(-1).all(-1).all(-1)], want[~untouched.all(-1).all(-1).all(-1)],
                        what="snapshots")
+
+
+# ---- every T > 1 kernel form, whatever the default routing picks ----
+
+@pytest.mark.parametrize("form", ["stream", "staged", "chunk"])
+@pytest.mark.parametrize("dtype,B,T,inter,l2,seed", [
+    (torch.float32, 40, 2, False, False, 70),   # benchmark heads, above the small-grid threshold
+    (torch.float32, 40, 4, True, False, 71),    # snapshots
+    (torch.float32, 40, 6, False, True, 72),    # two chunks / stages, L2 norm
+    (torch.bfloat16, 40, 3, False, False, 73),
+    (torch.bfloat16, 40, 8, False, True, 74),
+])
+def test_mtp_forms_match_oracle(cuda_device, monkeypatch, form, dtype, B, T, inter, l2, seed):
+    monkeypatch.setenv("GDN_MTP_FORM", form)
+    pool = B + 3
+    idx = list(range(1, B)) + [-1]  # the last entry is padding
+    args = inputs.mtp_inputs(B, T, pool, 16, 32, seed=seed, indices=idx, intermediate=inter and dtype == torch.float32)
+    if l2:
+        g = torch.Generator().manual_seed(seed + 100)
+        args[0] = (torch.randn(args[0].shape, generator=g) * 2.0).to(torch.bfloat16)
+        args[1] = (torch.randn(args[1].shape, generator=g) * 2.0).to(torch.bfloat16)
+    args[3] = args[3].to(dtype)
+    dargs = inputs.to_device(args, cuda_device)
+    pool_dev = dargs[3].clone()
+    out = torch.empty((B, T, 32, 128), dtype=torch.bfloat16, device=cuda_device)
+    gdn_mtp.run_into(*dargs[:3], pool_dev, *dargs[4:10], out, pool_dev,
+                     intermediate_states_buffer=dargs[10], qk_l2norm=l2)
+    torch.cuda.synchronize()
+    rb = None if args[10] is None else torch.zeros(args[10].shape)
+    ro, rs = oracle.mtp(*inputs.to_cpu(args[:10]), rb, qk_l2norm=l2)
+    assert_output_close(out.cpu(), ro)
+    assert bool((out[-1] == 0).all())  # padding entry: zero output
+    if dtype == torch.float32:
+        assert_state_close(pool_dev.cpu(), rs)
+    else:
+        _bf16_tol(pool_dev, rs)
+    assert torch.equal(pool_dev[0].cpu(), args[3][0])  # a slot no entry reads is untouched
+    if rb is not None:
+        for slot in range(1, B):
+            assert_state_close(dargs[10][slot].cpu(), rb[slot], what=f"intermediate[{slot}]")
