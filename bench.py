@@ -66,13 +66,13 @@ def decode_alg_bytes(B):
 MTP_B, MTP_T = 64, 4
 
 
-def mtp_alg_bytes(B, T):
-    """Algorithmic HBM bytes of one MTP launch with snapshots: each pool row
-    read once and written once, one snapshot per token (fp32), plus q, k
+def mtp_alg_bytes(B, T, snapshots=True):
+    """Algorithmic HBM bytes of one MTP launch (fp32 pool): each pool row read
+    once and written once, with snapshots one more write per token, plus q, k
     (bf16), v in and o out (bf16), a and b (bf16) for every token."""
     head = D * D * 4
-    return (B * HV * head * (2 + T) + T * (2 * B * H * D * 2 + 2 * B * HV * D * 2 + 2 * B * HV * 2)
-            + B * 4 + 2 * HV * 4)
+    return (B * HV * head * (2 + (T if snapshots else 0))
+            + T * (2 * B * H * D * 2 + 2 * B * HV * D * 2 + 2 * B * HV * 2) + B * 4 + 2 * HV * 4)
 
 
 def prefill_alg_flops(T):
@@ -614,6 +614,18 @@ def bench_ours(args, rank, world, local):
         barrier(world)
         mtp_ms = timed_steps(mtp_step, args.steps, flush, stream)
         barrier(world)
+        # the same batch without snapshots (serving without rollback, or
+        # flashinfer's disable_state_update=False without a cache): no longer
+        # HBM-bound at T = 4 by the snapshot writes
+        def mtp_ns_step():
+            gdn_mtp.run_into(*margs[:10], mout, mpool)
+
+        for _ in range(max(3, args.warmup)):
+            mtp_ns_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        mtp_ns_ms = timed_steps(mtp_ns_step, args.steps, flush, stream)
+        barrier(world)
 
         # ---- bf16-state decode: B = 64, state pool in bf16, in place ----
         bargs = inputs.mtp_inputs(DECODE_B, 1, DECODE_B, H, HV, seed=4000 + rank, device=dev,
@@ -640,6 +652,7 @@ def bench_ours(args, rank, world, local):
         barrier(world)
     clocks = clk.summary()
     mtp_step_ms = max_over_ranks(statistics.mean(mtp_ms), world, dev)
+    mtp_ns_step_ms = max_over_ranks(statistics.mean(mtp_ns_ms), world, dev)
     bf16_step_ms = max_over_ranks(statistics.mean(bf16_ms), world, dev)
 
     dec_step_ms = max_over_ranks(statistics.mean(dec_ms), world, dev)
@@ -739,7 +752,7 @@ def bench_ours(args, rank, world, local):
     launch_regions = {"decode": args.steps, "decode_clean_l2": args.steps,
                       "decode_b1024": args.steps, "prefill": 2 * args.steps,
                       "prefill_config3": 2 * args.steps if c3_shard.seqs else 0,
-                      "mtp": args.steps,
+                      "mtp": args.steps, "mtp_no_snapshots": args.steps,
                       "decode_bf16_state": 2 * args.steps,
                       "decode_e2e": e2e_steps * host_slices,
                       "prefill_e2e": pe2e_steps * host_pre_launches,
@@ -837,6 +850,19 @@ def bench_ours(args, rank, world, local):
                                        / peaks["hbm_gbs"], 4),
                          "traffic": profile_traffic("gdn_mtp_B64_T4_ncu.txt"),
                          "alg_bytes_per_launch": mtp_alg_bytes(MTP_B, MTP_T), "peak_src": peaks["src"]},
+        },
+        "mtp_no_snapshots": {
+            "metric": f"gdn_mtp GB/s at B={MTP_B}, T={MTP_T} (pool 128 slots, no snapshots, in place)",
+            "value": round(mtp_alg_bytes(MTP_B, MTP_T, False) * world / (mtp_ns_step_ms * 1e-3) / 1e9, 2),
+            "unit": "GB/s", "ms_per_step": round(mtp_ns_step_ms, 5), "step_ms_stats": _stats(mtp_ns_ms),
+            "kernel": "gdn_mtp_stream_kernel (persistent, bulk-copy ring)",
+            "roofline": {"bound": "hbm",
+                         "achieved": round(mtp_alg_bytes(MTP_B, MTP_T, False)
+                                           / (statistics.mean(mtp_ns_ms) * 1e-3) / 1e9, 1),
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(mtp_alg_bytes(MTP_B, MTP_T, False) / (statistics.mean(mtp_ns_ms) * 1e-3)
+                                       / 1e9 / peaks["hbm_gbs"], 4),
+                         "alg_bytes_per_launch": mtp_alg_bytes(MTP_B, MTP_T, False), "peak_src": peaks["src"]},
         },
         "decode_bf16_state": {
             "metric": "gdn decode with a bf16 state pool, B=64 (H=16, HV=32), in place: us/step",
