@@ -198,9 +198,37 @@ constexpr uint32_t TM_COLS = 128;  // columns 0-63: [K ; Q] K^T, then P'; 64-127
 // four-row float4 loads); offsets stay compile-time immediates.
 __device__ __forceinline__ int ix(int r, int c) { return r * LDA + c; }
 
+// Row r, columns c .. c+3 of the 16 x 16 x 16 product X Y of two blocks
+// (X, Y: their top-left elements in solve matrices, row stride LDA).
+__device__ __forceinline__ float4 blk_product_row(const float* X, const float* Y, int r, int c) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k4 = 0; k4 < 16; k4 += 4) {
+        const float4 x = *reinterpret_cast<const float4*>(X + ix(r, k4));
+        const float xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            const float4 y = *reinterpret_cast<const float4*>(Y + ix(k4 + kk, c));
+            acc.x = fmaf(xs[kk], y.x, acc.x);
+            acc.y = fmaf(xs[kk], y.y, acc.y);
+            acc.z = fmaf(xs[kk], y.z, acc.z);
+            acc.w = fmaf(xs[kk], y.w, acc.w);
+        }
+    }
+    return acc;
+}
+// Lower block (i, j) number n of (1,0) (2,0) (3,0) (2,1) (3,1) (3,2).
+__device__ __forceinline__ int blk_pair_i(int n) { return n < 3 ? n + 1 : (n == 3 ? 2 : 3); }
+__device__ __forceinline__ int blk_pair_j(int n) { return n < 3 ? 0 : (n == 5 ? 2 : 1); }
+__device__ __forceinline__ float4 f4_sub(float4 a, float4 b) {
+    return make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
+}
+
 // Blocked T = (I + A)^-1 for the 64 x 64 strictly lower A in sA; writes the
 // diagonal and lower 16 x 16 blocks of T into sT (the upper blocks are never
-// read).  Every matrix access goes through ix().
+// read) and leaves intermediate blocks in the lower blocks of sA (the upper
+// triangle of sA, where the scan prep parks P, is not touched).  Every matrix
+// access goes through ix(); tid: 0..127 within the matrix's thread group.
 __device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
     const int warp = tid >> 5, lane = tid & 31;
     // diagonal blocks: warp b inverts I + A_bb by right-looking substitution,
@@ -220,57 +248,77 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
         for (int r = 0; r < 16; ++r) sT[ix(b0 + r, b0 + lane)] = x[r];
     }
     __syncthreads();
-    // Off-diagonal blocks, one column block at a time: for i > j,
-    //   X_ij = sum_{k=j}^{i-1} A_ik T_kj,   T_ij = -T_ii X_ij.
-    // Column blocks are independent once the diagonal inverses exist, so each
-    // warp walks down its own 8 columns of one (warps 0, 3: column block 0)
-    // or two (warps 1, 2: column blocks 1 and 2) column blocks; a lane holds
-    // 4 rows of one column.  X_ij passes through the T_ij block itself (only
-    // this warp touches these columns), so the walk needs no block-wide
-    // barrier and no scratch matrix.
-    const int half = (warp == 0 || warp == 1) ? 0 : 1;
-    const int cc = 8 * half + (lane & 7);  // column within the column block
-    const int rq = (lane >> 3) * 4;        // first of this lane's 4 rows
-    const int jfirst = (warp == 0 || warp == 3) ? 0 : 1;
-    const int jlast = (warp == 0 || warp == 3) ? 0 : 2;
-#pragma unroll 1
-    for (int j = jfirst; j <= jlast; ++j) {
-        const int col = 16 * j + cc;
-#pragma unroll 1
-        for (int i = j + 1; i < 4; ++i) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-            for (int k = j; k < i; ++k) {
+    // Off-diagonal blocks by the product form.  With E_i = (I + A_ii)^-1 (the
+    // diagonal blocks just written) and M_ij = E_i A_ij (i > j),
+    //   I + A = diag(I + A_ii) (I + M),   (I + M)^-1 = I - M + M^2 - M^3
+    // (M is strictly block-lower with 4 blocks, so M^4 = 0).  Writing W for
+    // (I + M)^-1: W_10 = -M_10, W_21 = -M_21, W_32 = -M_32,
+    //   W_20 = M_21 M_10 - M_20,  W_31 = M_32 M_21 - M_31,
+    //   W_30 = (M_31 M_10 - M_30) - M_32 W_20,
+    // and T_ij = W_ij E_j.  Sixteen 16 x 16 x 16 products in four stages of
+    // independent products (6, 3, 1, 6), each spread over all 128 threads
+    // (64 per product, four outputs per thread), in place of a substitution
+    // whose row blocks wait on one another.  M and W overwrite the lower
+    // blocks of A, which nothing reads after the solve.
+    float* sAw = const_cast<float*>(sA);
+    const int half = tid >> 6, pt = tid & 63;
+    const int r = pt >> 2, c = 4 * (pt & 3);  // this thread's row and first column in a product
+    // stage 1: M_ij = E_i A_ij for (1,0) (2,0) | (3,0) (2,1) | (3,1) (3,2)
+    {
+        float4 m[3];
 #pragma unroll
-                for (int s4 = 0; s4 < 16; s4 += 4) {
-                    const float t0 = sT[ix(16 * k + s4 + 0, col)], t1 = sT[ix(16 * k + s4 + 1, col)];
-                    const float t2 = sT[ix(16 * k + s4 + 2, col)], t3 = sT[ix(16 * k + s4 + 3, col)];
+        for (int q = 0; q < 3; ++q) {
+            const int i = blk_pair_i(2 * q + half), j = blk_pair_j(2 * q + half);
+            m[q] = blk_product_row(sT + ix(16 * i, 16 * i), sA + ix(16 * i, 16 * j), r, c);
+        }
+        __syncthreads();
 #pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const float4 x = *reinterpret_cast<const float4*>(sA + ix(16 * i + rq + r, 16 * k + s4));
-                        acc[r] = fmaf(x.x, t0, fmaf(x.y, t1, fmaf(x.z, t2, fmaf(x.w, t3, acc[r]))));
-                    }
-                }
-            }
+        for (int q = 0; q < 3; ++q) {
+            const int i = blk_pair_i(2 * q + half), j = blk_pair_j(2 * q + half);
+            *reinterpret_cast<float4*>(sAw + ix(16 * i + r, 16 * j + c)) = m[q];
+        }
+        __syncthreads();
+    }
+    // stage 2: W_20 = M_21 M_10 - M_20 and Q_30 = M_31 M_10 - M_30 (half 0),
+    // W_31 = M_32 M_21 - M_31 (half 1)
+    {
+        float4 w0, w1 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (half == 0) {
+            w0 = blk_product_row(sA + ix(32, 16), sA + ix(16, 0), r, c);
+            w1 = blk_product_row(sA + ix(48, 16), sA + ix(16, 0), r, c);
+            w0 = f4_sub(w0, *reinterpret_cast<const float4*>(sA + ix(32 + r, c)));
+            w1 = f4_sub(w1, *reinterpret_cast<const float4*>(sA + ix(48 + r, c)));
+        } else {
+            w0 = blk_product_row(sA + ix(48, 32), sA + ix(32, 16), r, c);
+            w0 = f4_sub(w0, *reinterpret_cast<const float4*>(sA + ix(48 + r, 16 + c)));
+        }
+        __syncthreads();
+        if (half == 0) {
+            *reinterpret_cast<float4*>(sAw + ix(32 + r, c)) = w0;
+            *reinterpret_cast<float4*>(sAw + ix(48 + r, c)) = w1;
+        } else {
+            *reinterpret_cast<float4*>(sAw + ix(48 + r, 16 + c)) = w0;
+        }
+        __syncthreads();
+    }
+    // stage 3: W_30 = Q_30 - M_32 W_20 (half 0)
+    {
+        float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (half == 0)
+            w = f4_sub(*reinterpret_cast<const float4*>(sA + ix(48 + r, c)),
+                       blk_product_row(sA + ix(48, 32), sA + ix(32, 0), r, c));
+        __syncthreads();
+        if (half == 0) *reinterpret_cast<float4*>(sAw + ix(48 + r, c)) = w;
+        __syncthreads();
+    }
+    // stage 4: T_ij = W_ij E_j (W_10, W_21, W_32 are -M): (1,0) (2,0) | (3,0) (2,1) | (3,1) (3,2)
+    {
 #pragma unroll
-            for (int r = 0; r < 4; ++r) sT[ix(16 * i + rq + r, col)] = acc[r];
-            __syncwarp();
-            float xc[16];
-#pragma unroll
-            for (int s = 0; s < 16; ++s) xc[s] = sT[ix(16 * i + s, col)];
-            __syncwarp();  // every lane holds its X column before T_ij replaces it
-            float o[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int s4 = 0; s4 < 16; s4 += 4) {
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const float4 y = *reinterpret_cast<const float4*>(sT + ix(16 * i + rq + r, 16 * i + s4));
-                    o[r] = fmaf(y.x, xc[s4], fmaf(y.y, xc[s4 + 1], fmaf(y.z, xc[s4 + 2], fmaf(y.w, xc[s4 + 3], o[r]))));
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < 4; ++r) sT[ix(16 * i + rq + r, col)] = -o[r];
-            __syncwarp();
+        for (int q = 0; q < 3; ++q) {
+            const int i = blk_pair_i(2 * q + half), j = blk_pair_j(2 * q + half);
+            float4 t = blk_product_row(sA + ix(16 * i, 16 * j), sT + ix(16 * j, 16 * j), r, c);
+            if (i == j + 1) t = make_float4(-t.x, -t.y, -t.z, -t.w);
+            *reinterpret_cast<float4*>(sT + ix(16 * i + r, 16 * j + c)) = t;
         }
     }
     __syncthreads();
