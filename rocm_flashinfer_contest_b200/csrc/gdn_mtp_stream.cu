@@ -329,11 +329,20 @@ __global__ void __launch_bounds__(kThreads, 3)
 struct KernelInfo {
     int regs = 0, static_smem = 0, sms = 0, smem_sm = 0, smem_optin = 0;
     bool ok = false;
+    // the driver's resident-CTA count per dynamic shared-memory size seen
+    size_t occ_smem[8] = {};
+    int occ_ctas[8] = {};
 };
 
 template <int ROWS, typename StateT, int TM>
-static const KernelInfo& kernel_info() {
+static std::mutex& kernel_info_mutex() {
     static std::mutex mu;
+    return mu;
+}
+
+template <int ROWS, typename StateT, int TM>
+static const KernelInfo& kernel_info() {
+    std::mutex& mu = kernel_info_mutex<ROWS, StateT, TM>();
     static KernelInfo info[16];
     static bool done[16] = {};
     int dev = 0;
@@ -342,8 +351,7 @@ static const KernelInfo& kernel_info() {
         return none;
     }
     std::lock_guard<std::mutex> lk(mu);
-    if (!done[dev]) {
-        done[dev] = true;
+    if (!done[dev]) {  // set once the queries succeed (a failed attempt is retried on the next call)
         KernelInfo& k = info[dev];
         cudaFuncAttributes fa;
         auto fn = gdn_mtp_stream_kernel<ROWS, StateT, TM>;
@@ -361,6 +369,7 @@ static const KernelInfo& kernel_info() {
                                         (int)cudaSharedmemCarveoutMaxShared) == cudaSuccess;
         }
         cudaGetLastError();
+        done[dev] = k.ok;
     }
     return info[dev];
 }
@@ -387,11 +396,31 @@ static int launch(const MtpParams& p, int B, cudaStream_t st) {
     }
     if (per_sm < 1) return 1;
     // the driver's count for the chosen size, which the grid must not exceed
+    // (asked once per size and cached: no runtime query on later calls, which
+    // may be inside a graph capture)
     int resident = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, gdn_mtp_stream_kernel<ROWS, StateT, TM>, kThreads,
-                                                      smem) != cudaSuccess) {
-        cudaGetLastError();
-        return 1;
+    {
+        std::lock_guard<std::mutex> lk(kernel_info_mutex<ROWS, StateT, TM>());
+        KernelInfo& km = const_cast<KernelInfo&>(k);
+        int slot = -1;
+        for (int e = 0; e < 8; ++e) {
+            if (km.occ_smem[e] == smem) {
+                resident = km.occ_ctas[e];
+                break;
+            }
+            if (km.occ_smem[e] == 0 && slot < 0) slot = e;
+        }
+        if (resident == 0) {
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, gdn_mtp_stream_kernel<ROWS, StateT, TM>,
+                                                              kThreads, smem) != cudaSuccess) {
+                cudaGetLastError();
+                return 1;
+            }
+            if (slot >= 0) {
+                km.occ_smem[slot] = smem;
+                km.occ_ctas[slot] = resident;
+            }
+        }
     }
     per_sm = min(per_sm, resident);
     if (per_sm < 1) return 1;

@@ -20,12 +20,13 @@ def _fill(dst, src):
             d.copy_(s)
 
 
-def test_mtp_serving_step_replays(cuda_device):
-    """gated_delta_rule_mtp with the pool updated in place and per-token
-    snapshots, captured once and replayed on two new batches."""
+@pytest.mark.parametrize("snapshots", [True, False])  # the staged loop / the streaming kernel
+def test_mtp_serving_step_replays(cuda_device, snapshots):
+    """gated_delta_rule_mtp with the pool updated in place (and per-token
+    snapshots), captured once and replayed on two new batches."""
     B, T, pool, H, HV = 16, 4, 24, 16, 32
     static = inputs.mtp_inputs(B, T, pool, H, HV, seed=70, device=cuda_device, indices=list(range(3, 3 + B)))
-    buf = torch.zeros((B, T, HV, 128, 128), device=cuda_device)
+    buf = torch.zeros((B, T, HV, 128, 128), device=cuda_device) if snapshots else None
     out = torch.empty((B, T, HV, 128), dtype=torch.bfloat16, device=cuda_device)
 
     def step():
@@ -44,7 +45,7 @@ def test_mtp_serving_step_replays(cuda_device):
         _fill(static, new)
         # the eager reference on copies of the same inputs
         ref_pool = new[3].clone()
-        ref_buf = torch.zeros_like(buf)
+        ref_buf = torch.zeros_like(buf) if snapshots else None
         ref_o, _ = gdn_mtp.gated_delta_rule_mtp(*new[:3], ref_pool, *new[4:9], scale=None,
                                                 intermediate_states_buffer=ref_buf,
                                                 disable_state_update=False, use_qk_l2norm=True)
@@ -52,7 +53,31 @@ def test_mtp_serving_step_replays(cuda_device):
         torch.cuda.synchronize()
         assert torch.equal(out, ref_o)
         assert torch.equal(static[3], ref_pool)
-        assert torch.equal(buf, ref_buf)
+        if snapshots:
+            assert torch.equal(buf, ref_buf)
+
+
+def test_mtp_stream_first_call_inside_capture(cuda_device):
+    """The streaming kernel's one-time set-up (function attributes, occupancy)
+    also works when its first call of an instantiation is being captured: a
+    bf16 pool at T = 2, no snapshots, captured without an eager warm-up."""
+    B, T, pool, H, HV = 24, 2, 30, 16, 32
+    static = inputs.mtp_inputs(B, T, pool, H, HV, seed=75, device=cuda_device, indices=list(range(B)))
+    static[3] = static[3].to(torch.bfloat16)
+    out = torch.empty((B, T, HV, 128), dtype=torch.bfloat16, device=cuda_device)
+    start = static[3].clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        gdn_mtp.run_into(*static[:3], static[3], *static[4:10], out, static[3])
+    static[3].copy_(start)
+    g.replay()
+    torch.cuda.synchronize()
+    ref_pool = start.clone()
+    ref_o = torch.empty_like(out)
+    gdn_mtp.run_into(*static[:3], ref_pool, *static[4:10], ref_o, ref_pool)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_o)
+    assert torch.equal(static[3], ref_pool)
 
 
 def test_bf16_pool_decode_replays(cuda_device):
