@@ -216,7 +216,10 @@ def test_mtp_golden_bf16_state(cuda_device):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_mtp_output_state_indices(cuda_device, dtype):
+@pytest.mark.parametrize("form", ["", "stream", "chunk"])
+def test_mtp_output_state_indices(cuda_device, monkeypatch, dtype, form):
+    if form:
+        monkeypatch.setenv("GDN_MTP_FORM", form)
     B, T, pool = 4, 2, 10
     idx = [1, 3, -1, 6]
     oidx = [7, 2, 5, 11]          # entry 3 writes out of range: no state write
@@ -280,11 +283,14 @@ def test_decode_pretranspose_pool_mode(cuda_device):
 
 
 @pytest.mark.parametrize("T,steps,rows_entries", [(4, 4, 6), (3, 5, 4), (2, 2, 3), (1, 1, 6)])
-def test_mtp_serving_api_snapshots_by_entry(cuda_device, T, steps, rows_entries):
+@pytest.mark.parametrize("form", ["", "stream"])
+def test_mtp_serving_api_snapshots_by_entry(cuda_device, monkeypatch, T, steps, rows_entries, form):
     """gated_delta_rule_mtp puts snapshots where flashinfer's kernel does: batch
     entry i, token t at row i * T + t of the buffer seen as [slots * steps]
     rows (buffer[i, t] when steps == T); padding entries and entries whose T
     rows do not fit write nothing."""
+    if form:
+        monkeypatch.setenv("GDN_MTP_FORM", form)
     B, pool, H, HV = 6, 10, 4, 8
     idx = [7, -1, 2, 9, 0, 4]
     args = inputs.mtp_inputs(B, T, pool, H, HV, seed=60 + T, indices=idx)
@@ -321,7 +327,8 @@ def test_mtp_forms_match_oracle(cuda_device, monkeypatch, form, dtype, B, T, int
     monkeypatch.setenv("GDN_MTP_FORM", form)
     pool = B + 3
     idx = list(range(1, B)) + [-1]  # the last entry is padding
-    args = inputs.mtp_inputs(B, T, pool, 16, 32, seed=seed, indices=idx, intermediate=inter and dtype == torch.float32)
+    args = inputs.mtp_inputs(B, T, pool, 16, 32, seed=seed, indices=idx, intermediate=inter and dtype == torch.float32,
+                             idx_dtype=torch.int64 if seed % 2 else torch.int32)  # both index widths
     if l2:
         g = torch.Generator().manual_seed(seed + 100)
         args[0] = (torch.randn(args[0].shape, generator=g) * 2.0).to(torch.bfloat16)
