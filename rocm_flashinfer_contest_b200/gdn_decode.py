@@ -71,8 +71,12 @@ def _validate(q, k, v, state, A_log, a, dt_bias, b):
 def run_into(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
     """Destination-passing decode: writes ``output`` [B,1,HV,V] bf16 and
     ``new_state`` [B,HV,V,K] fp32 (``new_state`` may be ``state``)."""
-    dev, (q, k, v, state, A_log, a, dt_bias, b), (B, H, HV, K, V) = _validate(
-        q, k, v, state, A_log, a, dt_bias, b)
+    return _run_checked(*_validate(q, k, v, state, A_log, a, dt_bias, b), scale, output, new_state)
+
+
+def _run_checked(dev, tensors, dims, scale, output, new_state):
+    q, k, v, state, A_log, a, dt_bias, b = tensors
+    B, H, HV, K, V = dims
     if output.dtype != torch.bfloat16 or tuple(output.shape) != (B, 1, HV, V) \
             or not output.is_contiguous() or output.device != dev:
         raise ValueError("output must be a contiguous bf16 [B, 1, HV, V] tensor on the inputs' device")
@@ -89,10 +93,10 @@ def run_into(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state):
 
 def run(q, k, v, state, A_log, a, dt_bias, b, scale):
     """Contest entry point; see the module docstring."""
-    dev, _, (B, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b)
+    dev, tensors, (B, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b)
     output = torch.empty((B, 1, HV, V), dtype=torch.bfloat16, device=dev)
     new_state = torch.empty((B, HV, V, K), dtype=torch.float32, device=dev)
-    return run_into(q, k, v, state, A_log, a, dt_bias, b, scale, output, new_state)
+    return _run_checked(dev, tensors, (B, H, HV, K, V), scale, output, new_state)
 
 
 def gated_delta_rule_decode_pretranspose(q, k, v, state, A_log, a, dt_bias, b, scale=None,

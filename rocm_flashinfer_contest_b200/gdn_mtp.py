@@ -149,13 +149,15 @@ def run_into(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b
 def run(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, scale,
         intermediate_states_buffer=None):
     """Contest MTP definition; see the module docstring."""
-    dev, _, (B, T, H, HV, K, V), _ = _validate(
+    dev, tensors, dims, (slots, steps) = _validate(
         q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b, intermediate_states_buffer)
+    B, T, H, HV, K, V = dims
     pool_in = initial_state.contiguous()
     output = torch.empty((B, T, HV, V), dtype=torch.bfloat16, device=dev)
     final_state = torch.empty_like(pool_in)
-    return run_into(q, k, v, pool_in, initial_state_indices, A_log, a, dt_bias, b, scale,
-                    output, final_state, intermediate_states_buffer)
+    _launch(dev, tensors, dims, pool_in, final_state, scale, output, intermediate_states_buffer, slots, steps,
+            False)
+    return output, final_state
 
 
 def gated_delta_rule_mtp(q, k, v, initial_state, initial_state_indices, A_log, a, dt_bias, b,

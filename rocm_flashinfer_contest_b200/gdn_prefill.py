@@ -117,7 +117,14 @@ def run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, ne
              use_qk_l2norm_in_kernel: bool = False):
     """Destination-passing prefill into ``output`` [T,HV,V] bf16 and
     ``new_state`` [N,HV,V,K] fp32 (``new_state`` may be ``state``)."""
-    dev, args, (T, N, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
+    return _run_checked(*_validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens), scale, output, new_state,
+                        state_checkpoints, checkpoint_cu_starts, checkpoint_every_n_tokens,
+                        use_qk_l2norm_in_kernel)
+
+
+def _run_checked(dev, args, dims, scale, output, new_state, state_checkpoints, checkpoint_cu_starts,
+                 checkpoint_every_n_tokens, use_qk_l2norm_in_kernel):
+    T, N, H, HV, K, V = dims
     ck = _validate_checkpoints(state_checkpoints, checkpoint_cu_starts, checkpoint_every_n_tokens,
                                N, HV, K, dev)
     q, k, v, state, A_log, a, dt_bias, b, cu = args
@@ -152,13 +159,12 @@ def run(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, *,
         state_checkpoints=None, checkpoint_cu_starts=None, checkpoint_every_n_tokens: int = 0,
         use_qk_l2norm_in_kernel: bool = False):
     """Contest entry point; see the module docstring."""
-    dev, _, (T, N, H, HV, K, V) = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
+    dev, args, dims = _validate(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens)
+    T, N, H, HV, K, V = dims
     output = torch.empty((T, HV, V), dtype=torch.bfloat16, device=dev)
     new_state = torch.empty((N, HV, V, K), dtype=torch.float32, device=dev)
-    return run_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state,
-                    state_checkpoints=state_checkpoints, checkpoint_cu_starts=checkpoint_cu_starts,
-                    checkpoint_every_n_tokens=checkpoint_every_n_tokens,
-                    use_qk_l2norm_in_kernel=use_qk_l2norm_in_kernel)
+    return _run_checked(dev, args, dims, scale, output, new_state, state_checkpoints, checkpoint_cu_starts,
+                        checkpoint_every_n_tokens, use_qk_l2norm_in_kernel)
 
 
 def run_host_into(q, k, v, state, A_log, a, dt_bias, b, cu_seqlens, scale, output, new_state, *,
