@@ -118,9 +118,9 @@ constexpr uint32_t G_T = 64 * LDA * 4;              // T fp32 [64][LDA] during t
 constexpr uint32_t G_TP = 0;                        // [T diag(beta) ; P] K-major 128 x 64       16 KiB
 constexpr uint32_t G_T1 = 18432;                    // diag(f_K) T diag(beta), 64 x 64 (MN-major B) 8 KiB
 constexpr uint32_t G_EP = 0;                        // [Et diag(e^g) ; Pt diag(e^g)] K-major 192 x 64, 24 KiB
-constexpr uint32_t G_GM = 2 * 64 * LDA * 4;         // gamma[64], beta[64]
+constexpr uint32_t G_GM = 2 * 64 * LDA * 4;         // gamma[64], beta[64], e^gamma[64]
 static_assert(G_T1 % 1024 == 0 && G_T1 >= G_TP + kTileTP && G_T1 + 8192 <= G_GM, "T1 after [T ; P], before the gates");
-static_assert(G_EP + 24576 <= G_GM && G_GM + 512 <= kGroupBytes && kGroupBytes % 1024 == 0, "group region");
+static_assert(G_EP + 24576 <= G_GM && G_GM + 768 <= kGroupBytes && kGroupBytes % 1024 == 0, "group region");
 template <int NU> constexpr uint32_t smem_bytes() { return kTileKQ + NU * kGroupBytes + 1024; }  // + alignment slack
 template <int NU> constexpr int ctas_per_sm() { return NU == 1 ? 3 : 2; }
 static_assert(3 * (smem_bytes<1>() + 1024) <= 233472 && 2 * (smem_bytes<2>() + 1024) <= 233472,
@@ -176,6 +176,7 @@ __global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_
     float* sT = reinterpret_cast<float*>(gm + G_T);
     float* sG = reinterpret_cast<float*>(gm + G_GM);
     float* sBeta = sG + 64;
+    float* sEg = sG + 128;  // e^gamma per token: the column factors of the read-outs, one exp each
     unsigned char* rec = ws + ((size_t)s * p.HV + hv) * kRecBytes;
 
     // raw k rows -> [K ; Q] rows 0-63, q rows -> rows 64-127 (bf16, swizzled K-major)
@@ -217,6 +218,7 @@ __global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_
     if (gwarp == 1) sG[gt] = lg + sG[31];
     cp_async_wait_all();
     __syncthreads();
+    if (gt < C) sEg[gt] = __expf(sG[gt]);  // read after the masks' and solve's barriers
     // every product here takes [K ; Q] as f16: normalised rows are written as
     // f16, raw bf16 rows are converted (exact for |x| in f16's normal range)
     if (p.qk_l2norm) {
@@ -382,7 +384,7 @@ __global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_
                 float d[16];
                 umma::tmem_ld16(tg + lane_base + c16, d);
 #pragma unroll
-                for (int e = 0; e < 16; ++e) eg[e] = __expf(sG[c16 + e]);
+                for (int e = 0; e < 16; ++e) eg[e] = sEg[c16 + e];
                 st_f16x16_tile(rec + REC_EP, 128 + i, c16, kRecRows, d);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) d[e] *= eg[e];
@@ -395,7 +397,7 @@ __global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_
             float d[16];
             umma::tmem_ld16(tg + lane_base + 64 + c16, d);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) eg[e] = __expf(sG[c16 + e]);
+            for (int e = 0; e < 16; ++e) eg[e] = sEg[c16 + e];
             st_f16x16_tile(rec + REC_EP, gt, c16, kRecRows, d);
 #pragma unroll
             for (int e = 0; e < 16; ++e) d[e] *= eg[e];
