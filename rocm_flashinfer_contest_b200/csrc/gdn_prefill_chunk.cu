@@ -224,12 +224,21 @@ __device__ __forceinline__ float4 f4_sub(float4 a, float4 b) {
     return make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
 }
 
+// Barrier of the 128 threads that work on one solve matrix: the whole CTA
+// (id 0) or the named barrier `id` of its thread group, so that the groups of
+// a CTA that solve different matrices need not wait for one another.
+__device__ __forceinline__ void group_bar(int id) {
+    if (id == 0) __syncthreads();
+    else asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory");
+}
+
 // Blocked T = (I + A)^-1 for the 64 x 64 strictly lower A in sA; writes the
 // diagonal and lower 16 x 16 blocks of T into sT (the upper blocks are never
 // read) and leaves intermediate blocks in the lower blocks of sA (the upper
 // triangle of sA, where the scan prep parks P, is not touched).  Every matrix
-// access goes through ix(); tid: 0..127 within the matrix's thread group.
-__device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
+// access goes through ix(); tid: 0..127 within the matrix's thread group,
+// bar_id: its barrier (group_bar).
+__device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid, int bar_id = 0) {
     const int warp = tid >> 5, lane = tid & 31;
     // diagonal blocks: warp b inverts I + A_bb by right-looking substitution,
     // lane l < 16 owning column l
@@ -247,7 +256,7 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
 #pragma unroll
         for (int r = 0; r < 16; ++r) sT[ix(b0 + r, b0 + lane)] = x[r];
     }
-    __syncthreads();
+    group_bar(bar_id);
     // Off-diagonal blocks by the product form.  With E_i = (I + A_ii)^-1 (the
     // diagonal blocks just written) and M_ij = E_i A_ij (i > j),
     //   I + A = diag(I + A_ii) (I + M),   (I + M)^-1 = I - M + M^2 - M^3
@@ -271,13 +280,13 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
             const int i = blk_pair_i(2 * q + half), j = blk_pair_j(2 * q + half);
             m[q] = blk_product_row(sT + ix(16 * i, 16 * i), sA + ix(16 * i, 16 * j), r, c);
         }
-        __syncthreads();
+        group_bar(bar_id);
 #pragma unroll
         for (int q = 0; q < 3; ++q) {
             const int i = blk_pair_i(2 * q + half), j = blk_pair_j(2 * q + half);
             *reinterpret_cast<float4*>(sAw + ix(16 * i + r, 16 * j + c)) = m[q];
         }
-        __syncthreads();
+        group_bar(bar_id);
     }
     // stage 2: W_20 = M_21 M_10 - M_20 and Q_30 = M_31 M_10 - M_30 (half 0),
     // W_31 = M_32 M_21 - M_31 (half 1)
@@ -292,14 +301,14 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
             w0 = blk_product_row(sA + ix(48, 32), sA + ix(32, 16), r, c);
             w0 = f4_sub(w0, *reinterpret_cast<const float4*>(sA + ix(48 + r, 16 + c)));
         }
-        __syncthreads();
+        group_bar(bar_id);
         if (half == 0) {
             *reinterpret_cast<float4*>(sAw + ix(32 + r, c)) = w0;
             *reinterpret_cast<float4*>(sAw + ix(48 + r, c)) = w1;
         } else {
             *reinterpret_cast<float4*>(sAw + ix(48 + r, 16 + c)) = w0;
         }
-        __syncthreads();
+        group_bar(bar_id);
     }
     // stage 3: W_30 = Q_30 - M_32 W_20 (half 0)
     {
@@ -307,9 +316,9 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
         if (half == 0)
             w = f4_sub(*reinterpret_cast<const float4*>(sA + ix(48 + r, c)),
                        blk_product_row(sA + ix(48, 32), sA + ix(32, 0), r, c));
-        __syncthreads();
+        group_bar(bar_id);
         if (half == 0) *reinterpret_cast<float4*>(sAw + ix(48 + r, c)) = w;
-        __syncthreads();
+        group_bar(bar_id);
     }
     // stage 4: T_ij = W_ij E_j (W_10, W_21, W_32 are -M): (1,0) (2,0) | (3,0) (2,1) | (3,1) (3,2)
     {
@@ -321,7 +330,7 @@ __device__ __forceinline__ void solve_T(const float* sA, float* sT, int tid) {
             *reinterpret_cast<float4*>(sT + ix(16 * i + r, 16 * j + c)) = t;
         }
     }
-    __syncthreads();
+    group_bar(bar_id);
 }
 
 // MMA_P reads rows 0-63 of the K-major [T ; P] tile as an MN-major operand.

@@ -294,8 +294,10 @@ __global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_
             }
         }
     }
-    __syncthreads();
-    ::gdn::chunk::prep::solve_T(sA, sT, gt);
+    // from the masks to the T copies each v-head group works on its own
+    // matrices: its own named barrier (1 + g), not the whole CTA
+    ::gdn::chunk::prep::group_bar(1 + g);
+    ::gdn::chunk::prep::solve_T(sA, sT, gt, 1 + g);
 
     // f16 copies of T: T diag(beta) -> rows 0-63 of [T ; P] (the B operand of
     // MMA_P, read MN-major from those rows) and diag(f_K) T diag(beta) -> T1;
@@ -327,7 +329,7 @@ __global__ void __launch_bounds__(128 * NU, ctas_per_sm<NU>()) gdn_prefill_scan_
             for (int c = 0; c < 8; ++c)
                 pr[c] = 8 * c <= pi ? *reinterpret_cast<const uint4*>(prow + 16 * c) : make_uint4(0u, 0u, 0u, 0u);
         }
-        __syncthreads();  // the tiles below overwrite sA and part of sT
+        ::gdn::chunk::prep::group_bar(1 + g);  // the tiles below overwrite sA and part of sT
 #pragma unroll
         for (int c = 0; c < 32; c += 8) {
             float x[8], y[8];
