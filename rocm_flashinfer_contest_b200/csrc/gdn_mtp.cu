@@ -765,13 +765,14 @@ extern "C" int gdn_mtp_fwd(const void* q, const void* k, const void* v, const vo
     // flushed): T = 1 -> the per-CTA pool decode; T > 1 with snapshots -> the
     // staged loop (the snapshot writes keep it HBM-bound); T > 1 without
     // snapshots -> the streaming kernel for fp32 pools up to T = 4 (T = 2:
-    // 58.9 vs 74.8, T = 4: 80.0 vs 89.5) and bf16 pools at T = 2 (50.5 vs
-    // 56.7), the staged loop otherwise (its 20 warps per SM hide the longer
-    // token chains better).  GDN_MTP_FORM = "stream", "staged" or "chunk"
-    // forces a T > 1 form (stream falls back when the call does not qualify).
+    // 59.9 vs 74.8, T = 4: 72.5 vs 89.5) and bf16 pools up to T = 3 (T = 3:
+    // 60.1 vs 64.5), the staged loop otherwise (its 20 warps per SM hide the
+    // longer token chains better).  GDN_MTP_FORM = "stream", "staged" or
+    // "chunk" forces a T > 1 form (stream falls back when the call does not
+    // qualify).
     const char* form = getenv("GDN_MTP_FORM");
     const bool forced = form != nullptr && *form != 0;
-    const bool stream_default = !small && intermediate == nullptr && (state_bf16 ? T == 2 : T >= 2 && T <= 4);
+    const bool stream_default = !small && intermediate == nullptr && (state_bf16 ? T <= 3 : T <= 4);
     if (T > 1 && (forced ? strcmp(form, "stream") == 0 : stream_default)) {
         const int r = gdn::launch_mtp_stream(p, B, state_bf16 != 0, st);
         if (r != 1) return r;

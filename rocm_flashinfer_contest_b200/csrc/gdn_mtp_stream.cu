@@ -252,7 +252,15 @@ __global__ void __launch_bounds__(kThreads, 3)
         const size_t row_off = (size_t)row_base * kDim;
         const long long snap_row = mtp_snap_row(p, bi, slot);
         const long long oslot = p.out_idx != nullptr ? mtp_index(p.out_idx, p.idx64, bi) : slot;
-        const float A_log = s_alog[hv], dt_bias = s_dtb[hv];
+        // lane t < T forms token t's gate and beta once; the token loop takes
+        // them by shuffle instead of every lane recomputing them per token
+        float g_lane = 1.f, beta_lane = 0.f;
+        if (lane < T) {
+            const float ga = bf16_to_f32(reinterpret_cast<const __nv_bfloat16*>(st + L.a + 4 * lane)[hv & 1]);
+            const float gb = bf16_to_f32(reinterpret_cast<const __nv_bfloat16*>(st + L.b + 4 * lane)[hv & 1]);
+            g_lane = expf(log_gate(s_alog[hv], ga, s_dtb[hv]));
+            beta_lane = sigmoidf_(gb);
+        }
         for (int t = 0; t < T; ++t) {
             float4 kf[4], qf[4];
 #pragma unroll
@@ -261,10 +269,8 @@ __global__ void __launch_bounds__(kThreads, 3)
                 kf[j] = mtp_widen4(*reinterpret_cast<const uint2*>(st + L.k + 256 * t + 2 * c));
                 qf[j] = mtp_widen4(*reinterpret_cast<const uint2*>(st + L.q + 256 * t + 2 * c));
             }
-            const float ga = bf16_to_f32(reinterpret_cast<const __nv_bfloat16*>(st + L.a + 4 * t)[hv & 1]);
-            const float gb = bf16_to_f32(reinterpret_cast<const __nv_bfloat16*>(st + L.b + 4 * t)[hv & 1]);
-            const float g = expf(log_gate(A_log, ga, dt_bias));
-            const float beta = sigmoidf_(gb);
+            const float g = __shfl_sync(0xffffffffu, g_lane, t);
+            const float beta = __shfl_sync(0xffffffffu, beta_lane, t);
             if (p.l2norm) {
                 float qq = 0.f, kk = 0.f;
 #pragma unroll
